@@ -1,0 +1,15 @@
+"""im-not-llm B200: the packed variable-length encoder forward of im-not-llm's
+embedding engines on sm_100a, behind a C ABI (libinl_cuda.so) and a Python
+host layer that mirrors the reference's engine API."""
+from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  # noqa: F401
+                     TimeoutError_)
+from .model import CudaModel  # noqa: F401
+from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder,  # noqa: F401
+                     TextEmbedder, TextOptions)
+from . import planner, synthetic  # noqa: F401
+
+__all__ = [
+    "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "InferenceError",
+    "InlError", "InvalidInputError", "LateEncoder", "TextEmbedder", "TextOptions", "TimeoutError_",
+    "planner", "synthetic",
+]

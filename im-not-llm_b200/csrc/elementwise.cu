@@ -1,0 +1,468 @@
+// Bandwidth-bound kernels of the encoder forward: embedding gather, RMSNorm /
+// LayerNorm, per-head q/k norm + RoPE, pooling heads and weight conversion.
+// One warp per row (or per token-head) with warp-shuffle reductions; rows are
+// read with 16-byte vector loads where the shape allows.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace inl {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p, long long i);
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p, long long i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p, long long i) {
+  return __bfloat162float(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ void st_f(T* p, long long i, float v);
+template <>
+__device__ __forceinline__ void st_f<float>(float* p, long long i, float v) { p[i] = v; }
+template <>
+__device__ __forceinline__ void st_f<__nv_bfloat16>(__nv_bfloat16* p, long long i, float v) {
+  p[i] = __float2bfloat16_rn(v);
+}
+
+// Load 8 consecutive values (16 B for bf16, 32 B for f32) into floats.
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void ld8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 w = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+template <>
+__device__ __forceinline__ void ld8<float>(const float* p, float (&v)[8]) {
+  float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void st8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(v[0], v[1]); w.y = pack_bf16x2(v[2], v[3]);
+  w.z = pack_bf16x2(v[4], v[5]); w.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+template <>
+__device__ __forceinline__ void st8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// ------------------------------------------------------------ embedding
+template <typename TT, typename TO>
+__global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T, const TT* __restrict__ table,
+                                    int vocab, int H, float scale, TO* __restrict__ out, int* status) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const uint32_t id = ids[row];
+  TO* o = out + row * H;
+  if (id >= static_cast<uint32_t>(vocab)) {
+    if (lane == 0 && status) atomicCAS(status, 0, INL_DEV_BAD_INDEX);
+    for (int c = lane; c < H; c += 32) st_f<TO>(o, c, 0.f);
+    return;
+  }
+  const TT* src = table + static_cast<long long>(id) * H;
+  if ((H & 7) == 0) {
+    for (int c = lane * 8; c < H; c += 256) {
+      float v[8];
+      ld8<TT>(src + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= scale;
+      st8<TO>(o + c, v);
+    }
+  } else {
+    for (int c = lane; c < H; c += 32) st_f<TO>(o, c, ld_f<TT>(src, c) * scale);
+  }
+}
+
+// ------------------------------------------------------------ norms
+template <typename TI, typename TO, bool LN>
+__global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const float* __restrict__ w,
+                                 const float* __restrict__ b, float eps, int rows, int H, TO* __restrict__ out,
+                                 long long ldo) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const TI* xr = x + row * ldx;
+  TO* orow = out + row * ldo;
+  const bool vec = (H & 255) == 0;
+  float mean = 0.f;
+  if (LN) {
+    float s = 0.f;
+    if (vec) {
+      for (int c = lane * 8; c < H; c += 256) {
+        float v[8];
+        ld8<TI>(xr + c, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[j];
+      }
+    } else {
+      for (int c = lane; c < H; c += 32) s += ld_f<TI>(xr, c);
+    }
+    mean = warp_sum(s) / static_cast<float>(H);
+  }
+  float ss = 0.f;
+  if (vec) {
+    for (int c = lane * 8; c < H; c += 256) {
+      float v[8];
+      ld8<TI>(xr + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float t = v[j] - mean;
+        ss += t * t;
+      }
+    }
+  } else {
+    for (int c = lane; c < H; c += 32) {
+      const float t = ld_f<TI>(xr, c) - mean;
+      ss += t * t;
+    }
+  }
+  const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(H) + eps);
+  if (vec) {
+    for (int c = lane * 8; c < H; c += 256) {
+      float v[8];
+      ld8<TI>(xr + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float t = (v[j] - mean) * inv;
+        if (w) t *= w[c + j];
+        if (b) t += b[c + j];
+        v[j] = t;
+      }
+      st8<TO>(orow + c, v);
+    }
+  } else {
+    for (int c = lane; c < H; c += 32) {
+      float t = (ld_f<TI>(xr, c) - mean) * inv;
+      if (w) t *= w[c];
+      if (b) t += b[c];
+      st_f<TO>(orow, c, t);
+    }
+  }
+}
+
+// ------------------------------------------------------------ q/k norm + rope
+// One warp per (token, head). Lane l holds elements [E*l, E*l+E), E = d/32;
+// lanes 0..15 hold the first half of the head, lanes 16..31 the second, so the
+// RoPE partner of every element sits in lane l ^ 16.
+template <typename T, int E>
+__global__ void qk_norm_rope_kernel(QkRopeArgs a) {
+  const int warps = blockDim.x >> 5;
+  const long long item = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
+  if (item >= static_cast<long long>(a.T) * heads) return;
+  const int t = static_cast<int>(item / heads);
+  const int h = static_cast<int>(item - static_cast<long long>(t) * heads);
+  const int d = E * 32;
+  const int half = d / 2;
+  T* row = reinterpret_cast<T*>(a.qkv) + static_cast<long long>(t) * a.ld + static_cast<long long>(h) * d;
+  const bool is_q = h < a.hq;
+  const bool is_k = !is_q && h < a.hq + a.hkv;
+  const float* w = is_q ? a.qw : (is_k ? a.kw : nullptr);
+  const bool norm = is_q ? (a.qw != nullptr) : (is_k ? (a.kw != nullptr) : true);
+  const bool is_bf16 = sizeof(T) == 2;
+  float x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = ld_f<T>(row, lane * E + e);
+  if (norm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(d) + a.eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float v = x[e] * inv;
+      if (w) v *= w[lane * E + e];
+      x[e] = is_bf16 ? bf16_round(v) : v;
+    }
+  }
+  if (is_q || is_k) {
+    int p = a.pos[t];
+    if (p < 0 || p >= a.max_pos) {
+      if (lane == 0 && a.status) atomicCAS(a.status, 0, INL_DEV_BAD_INDEX);
+      p = 0;
+    }
+    const float* cr = a.cos + static_cast<long long>(p) * half;
+    const float* sr = a.sin + static_cast<long long>(p) * half;
+    const bool first = lane < 16;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      const int i = (lane * E + e) - (first ? 0 : half);
+      const float c = cr[i], s = sr[i];
+      x[e] = first ? (x[e] * c - other * s) : (x[e] * c + other * s);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) st_f<T>(row, lane * E + e, x[e]);
+}
+
+// ------------------------------------------------------------ positions
+__global__ void token_positions_kernel(const int* __restrict__ cu, int n, int T, int* __restrict__ pos) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  int lo = 0, hi = n;  // find i with cu[i] <= t < cu[i+1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= t) lo = mid;
+    else hi = mid;
+  }
+  pos[t] = t - cu[lo];
+}
+
+// ------------------------------------------------------------ heads
+template <typename T>
+__global__ void last_token_norm_l2_kernel(const T* __restrict__ h, long long ldh, const int* __restrict__ cu,
+                                          int n, const float* __restrict__ w, float eps, int H,
+                                          float* __restrict__ out) {
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  __shared__ float red[32];
+  const int last = cu[i + 1] - 1;
+  float* o = out + static_cast<long long>(i) * H;
+  if (last < cu[i]) {  // empty text: zero vector
+    for (int c = threadIdx.x; c < H; c += blockDim.x) o[c] = 0.f;
+    return;
+  }
+  const T* row = h + static_cast<long long>(last) * ldh;
+  auto block_sum = [&](float v) {
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+    const int nw = blockDim.x >> 5;
+    for (int j = 0; j < nw; ++j) t += red[j];
+    return t;
+  };
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    const float v = ld_f<T>(row, c);
+    ss += v * v;
+  }
+  const float inv = rsqrtf(block_sum(ss) / static_cast<float>(H) + eps);
+  const bool is_bf16 = sizeof(T) == 2;
+  float ss2 = 0.f;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float v = ld_f<T>(row, c) * inv * (w ? w[c] : 1.f);
+    if (is_bf16) v = bf16_round(v);  // the model-dtype norm output, cast to f32 before L2
+    o[c] = v;
+    ss2 += v * v;
+  }
+  const float inv2 = 1.0f / sqrtf(block_sum(ss2) + 1e-12f);
+  for (int c = threadIdx.x; c < H; c += blockDim.x) o[c] *= inv2;
+}
+
+__global__ void rows_l2_kernel(const float* __restrict__ x, long long ldx, int rows, int D, float clamp_min,
+                               float* __restrict__ out, long long ldo) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + row * ldx;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) ss += xr[c] * xr[c];
+  const float nrm = sqrtf(warp_sum(ss));
+  const float inv = 1.0f / fmaxf(nrm, clamp_min);
+  for (int c = lane; c < D; c += 32) out[row * ldo + c] = xr[c] * inv;
+}
+
+template <typename T>
+__global__ void segment_mean_kernel(const T* __restrict__ x, long long ldx, const int* __restrict__ cu, int n,
+                                    int H, float* __restrict__ out) {
+  const int i = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (i >= n || c >= H) return;
+  const int s = cu[i], e = cu[i + 1];
+  float acc = 0.f;
+  for (int t = s; t < e; ++t) acc += ld_f<T>(x + static_cast<long long>(t) * ldx, c);
+  out[static_cast<long long>(i) * H + c] = e > s ? acc / static_cast<float>(e - s) : 0.f;
+}
+
+__global__ void truncate_normalize_kernel(const float* __restrict__ x, int n, int D, int dim,
+                                          float* __restrict__ out) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const float* xr = x + row * D;
+  float ss = 0.f;
+  for (int c = lane; c < dim; c += 32) ss += xr[c] * xr[c];
+  const float nrm = sqrtf(warp_sum(ss));
+  for (int c = lane; c < dim; c += 32) out[row * dim + c] = nrm > 0.f ? xr[c] / nrm : xr[c];
+}
+
+template <typename TS, typename TD>
+__global__ void convert_rows_kernel(const TS* __restrict__ src, int rows, int cols, TD* __restrict__ dst,
+                                    long long ld_dst, int blk, long long blk_stride, long long off) {
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(idx / cols);
+    const int c = static_cast<int>(idx - static_cast<long long>(r) * cols);
+    const long long dr = static_cast<long long>(r / blk) * blk_stride + off + (r % blk);
+    st_f<TD>(dst, dr * ld_dst + c, ld_f<TS>(src, idx));
+  }
+}
+
+inline int rows_grid(long long rows, int warps_per_block) {
+  return static_cast<int>((rows + warps_per_block - 1) / warps_per_block);
+}
+
+inline int ok(cudaError_t e) { return e == cudaSuccess ? 0 : -3; }
+
+}  // namespace
+
+int embed_gather(const uint32_t* ids, int T, const void* table, int table_bf16, int vocab, int H, float scale,
+                 void* out, int out_bf16, int* status, cudaStream_t s) {
+  if (T <= 0) return 0;
+  const int grid = rows_grid(T, 4);
+  if (table_bf16 && out_bf16)
+    embed_gather_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 128, 0, s>>>(
+        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), status);
+  else if (table_bf16)
+    embed_gather_kernel<__nv_bfloat16, float><<<grid, 128, 0, s>>>(
+        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<float*>(out), status);
+  else if (out_bf16)
+    embed_gather_kernel<float, __nv_bfloat16><<<grid, 128, 0, s>>>(
+        ids, T, static_cast<const float*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), status);
+  else
+    embed_gather_kernel<float, float><<<grid, 128, 0, s>>>(ids, T, static_cast<const float*>(table), vocab, H,
+                                                           scale, static_cast<float*>(out), status);
+  return ok(cudaGetLastError());
+}
+
+template <bool LN>
+static int norm_dispatch(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps,
+                         int rows, int H, void* out, int out_bf16, long long ldo, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const int grid = rows_grid(rows, 4);
+  if (x_bf16 && out_bf16)
+    norm_rows_kernel<__nv_bfloat16, __nv_bfloat16, LN><<<grid, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, w, b, eps, rows, H, static_cast<__nv_bfloat16*>(out), ldo);
+  else if (x_bf16)
+    norm_rows_kernel<__nv_bfloat16, float, LN><<<grid, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, w, b, eps, rows, H, static_cast<float*>(out), ldo);
+  else if (out_bf16)
+    norm_rows_kernel<float, __nv_bfloat16, LN><<<grid, 128, 0, s>>>(
+        static_cast<const float*>(x), ldx, w, b, eps, rows, H, static_cast<__nv_bfloat16*>(out), ldo);
+  else
+    norm_rows_kernel<float, float, LN><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, w, b, eps, rows, H,
+                                                            static_cast<float*>(out), ldo);
+  return ok(cudaGetLastError());
+}
+
+int rms_norm(const void* x, int x_bf16, long long ldx, const float* w, float eps, int rows, int H, void* out,
+             int out_bf16, long long ldo, cudaStream_t s) {
+  return norm_dispatch<false>(x, x_bf16, ldx, w, nullptr, eps, rows, H, out, out_bf16, ldo, s);
+}
+
+int layer_norm(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
+               void* out, int out_bf16, long long ldo, cudaStream_t s) {
+  return norm_dispatch<true>(x, x_bf16, ldx, w, b, eps, rows, H, out, out_bf16, ldo, s);
+}
+
+int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return 0;
+  const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
+  const long long items = static_cast<long long>(a.T) * heads;
+  const int grid = rows_grid(items, 8);
+  const int E = a.d / 32;
+  if (a.d % 32 != 0) return -1;
+#define INL_QKR(EE)                                                              \
+  if (a.bf16) qk_norm_rope_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);   \
+  else qk_norm_rope_kernel<float, EE><<<grid, 256, 0, s>>>(a);
+  switch (E) {
+    case 2: INL_QKR(2) break;
+    case 4: INL_QKR(4) break;
+    case 8: INL_QKR(8) break;
+    default: return -1;
+  }
+#undef INL_QKR
+  return ok(cudaGetLastError());
+}
+
+int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s) {
+  if (T <= 0) return 0;
+  token_positions_kernel<<<(T + 255) / 256, 256, 0, s>>>(cu, n, T, pos);
+  return ok(cudaGetLastError());
+}
+
+int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, int n, const float* w, float eps,
+                       int H, float* out, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (h_bf16)
+    last_token_norm_l2_kernel<__nv_bfloat16><<<n, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh, cu, n, w,
+                                                                eps, H, out);
+  else
+    last_token_norm_l2_kernel<float><<<n, 256, 0, s>>>(static_cast<const float*>(h), ldh, cu, n, w, eps, H, out);
+  return ok(cudaGetLastError());
+}
+
+int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min, float* out, long long ldo,
+                cudaStream_t s) {
+  if (rows <= 0) return 0;
+  rows_l2_kernel<<<rows_grid(rows, 8), 256, 0, s>>>(x, ldx, rows, D, clamp_min, out, ldo);
+  return ok(cudaGetLastError());
+}
+
+int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, float* out,
+                 cudaStream_t s) {
+  if (n <= 0) return 0;
+  dim3 grid(n, (H + 127) / 128);
+  if (x_bf16)
+    segment_mean_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, cu, n, H, out);
+  else
+    segment_mean_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, cu, n, H, out);
+  return ok(cudaGetLastError());
+}
+
+int truncate_normalize(const float* x, int n, int D, int dim, float* out, cudaStream_t s) {
+  if (n <= 0) return 0;
+  truncate_normalize_kernel<<<rows_grid(n, 8), 256, 0, s>>>(x, n, D, dim, out);
+  return ok(cudaGetLastError());
+}
+
+int convert_rows(const float* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
+                 long long blk_stride, long long off, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const long long total = static_cast<long long>(rows) * cols;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  if (dst_bf16)
+    convert_rows_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<__nv_bfloat16*>(dst),
+                                                                    ld_dst, blk, blk_stride, off);
+  else
+    convert_rows_kernel<float, float><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<float*>(dst), ld_dst, blk,
+                                                           blk_stride, off);
+  return ok(cudaGetLastError());
+}
+
+int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst,
+                      int blk, long long blk_stride, long long off, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const long long total = static_cast<long long>(rows) * cols;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  if (dst_bf16)
+    convert_rows_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(
+        src, rows, cols, static_cast<__nv_bfloat16*>(dst), ld_dst, blk, blk_stride, off);
+  else
+    convert_rows_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<float*>(dst), ld_dst,
+                                                                   blk, blk_stride, off);
+  return ok(cudaGetLastError());
+}
+
+}  // namespace inl

@@ -1,0 +1,416 @@
+// Persistent bf16 GEMM for sm_100a on the 5th-generation tensor cores.
+//
+//   Y[M, N] = X[M, K] . W[N, K]^T        (X = packed token rows, W = nn.Linear weight)
+//
+// One CTA per SM, 192 threads, warp-specialised:
+//   warp 0      TMA producer: X and W tiles -> shared memory (128-byte swizzle),
+//               STAGES-deep ring guarded by full/empty mbarriers;
+//   warp 1      allocates TMEM and issues tcgen05.mma (one elected thread),
+//               M=128 x N=BN x K=16 per instruction, accumulators in TMEM,
+//               two accumulator buffers so the epilogue of tile i overlaps the
+//               main loop of tile i+1;
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers, fused epilogue
+//               (plain store, residual add, gated activation, f32 store,
+//               per-row scale), 16-byte global stores. Warp w reads TMEM lane
+//               quadrant w % 4, i.e. tile rows 32*(w%4) .. 32*(w%4)+31, one
+//               row per thread.
+// Tiles are walked in row-major tile order by a static stride-gridDim
+// schedule, so the CTAs resident at one time share the same few X row blocks
+// and read W (a few MB) out of L2.
+#include <cstdio>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace inl {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct EpiArgs {
+  void* out;
+  long long ldo;
+  const __nv_bfloat16* resid;
+  long long ldr;
+  const float* row_scale;
+  int M, N;
+};
+
+template <int ACT>
+__device__ __forceinline__ float gate_act(float x) {
+  if constexpr (ACT == INL_ACT_SILU) return silu_f(x);
+  else if constexpr (ACT == INL_ACT_GELU_ERF) return gelu_erf_f(x);
+  else return gelu_tanh_f(x);
+}
+
+// Store 32 consecutive bf16 values of one row (64 bytes) with column guard.
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float (&v)[32], int ncols_left) {
+  if (ncols_left >= 32) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      d4[j] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols_left) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+__device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* src, float (&v)[32], int ncols_left) {
+  if (ncols_left >= 32) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w = s4[j];
+      float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+      v[8 * j + 0] = a.x; v[8 * j + 1] = a.y; v[8 * j + 2] = b.x; v[8 * j + 3] = b.y;
+      v[8 * j + 4] = c.x; v[8 * j + 5] = c.y; v[8 * j + 6] = d.x; v[8 * j + 7] = d.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = j < ncols_left ? __bfloat162float(src[j]) : 0.f;
+  }
+}
+
+template <int BN, int EPI, int ACT>
+__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, const EpiArgs& e) {
+  const bool row_ok = row < e.M;
+  const float rs = (e.row_scale != nullptr && row_ok) ? e.row_scale[row] : 1.0f;
+  uint32_t r[32];
+  float v[32];
+  if constexpr (EPI == INL_EPI_GATED_BF16) {
+    // Columns [0, BN/2) of the tile are the gate half, [BN/2, BN) the up half
+    // (weights interleaved in BN/2-row blocks at load time). Output width N/2.
+    constexpr int H = BN / 2;
+    const int out_n = e.N / 2;
+    const int o0 = n0 / 2;
+#pragma unroll 1
+    for (int c = 0; c < H; c += 32) {
+      uint32_t u[32];
+      tmem_ld32(t_row + c, r);
+      tmem_ld32(t_row + H + c, u);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float g = bf16_round(__uint_as_float(r[j]) * rs);
+        const float up = bf16_round(__uint_as_float(u[j]) * rs);
+        v[j] = gate_act<ACT>(g) * up;
+      }
+      if (row_ok) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + o0 + c;
+        store_row32_bf16(dst, v, out_n - (o0 + c));
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      tmem_ld32(t_row + c, r);
+      tmem_ld_wait();
+      const int col = n0 + c;
+      const int left = e.N - col;
+      if (!row_ok || left <= 0) continue;  // loads above stay warp-uniform
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
+      if constexpr (EPI == INL_EPI_F32) {
+        float* dst = reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col;
+        if (left >= 32) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          for (int j = 0; j < left; ++j) dst[j] = v[j];
+        }
+      } else {
+        if constexpr (EPI == INL_EPI_RESID_BF16) {
+          float rr[32];
+          load_row32_bf16(e.resid + (long long)row * e.ldr + col, rr, left);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]) + rr[j];
+        }
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col;
+        store_row32_bf16(dst, v, left);
+      }
+    }
+  }
+}
+
+template <int BN, int EPI, int ACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                        int N, int K, EpiArgs e, int* status) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status, INL_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * kBK, mb * kBM);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * kBK, nb * BN);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every copy this thread issued must have landed before the CTA
+      // can exit (on the normal path the MMA warp already consumed them all).
+      const long long first = issued > C::STAGES ? issued - C::STAGES : 0;
+      for (long long f = first; f < issued; ++f) {
+        const int s = static_cast<int>(f % C::STAGES);
+        const uint32_t ph = static_cast<uint32_t>((f / C::STAGES) & 1);
+        if (!mbar_wait(&full[s], ph, status, INL_DEV_TIMEOUT_DRAIN)) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status, INL_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, INL_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                      (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..5.
+    const int quad = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+      if (!mbar_wait(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int row = mb * kBM + quad * 32 + lane;
+      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, e);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// Row-major [rows, cols] bf16 with row stride `ld` elements; box = [box_rows, 64].
+bool make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                     int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int EPI, int ACT>
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& e,
+                        int* status, int max_ctas, cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  auto kern = gemm_bf16_tn_kernel<BN, EPI, ACT>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    attr_set = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  int grid = num_sms();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (tiles < grid) grid = tiles;
+  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, M, N, K, e, status);
+  return cudaGetLastError();
+}
+
+template <int BN, int EPI>
+cudaError_t dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                         const EpiArgs& e, int* status, int max_ctas, cudaStream_t s) {
+  switch (act) {
+    case INL_ACT_SILU: return launch_gemm<BN, EPI, INL_ACT_SILU>(ta, tb, M, N, K, e, status, max_ctas, s);
+    case INL_ACT_GELU_ERF: return launch_gemm<BN, EPI, INL_ACT_GELU_ERF>(ta, tb, M, N, K, e, status, max_ctas, s);
+    default: return launch_gemm<BN, EPI, INL_ACT_GELU_TANH>(ta, tb, M, N, K, e, status, max_ctas, s);
+  }
+}
+
+}  // namespace
+
+int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0) return 0;
+  if (g.K <= 0 || (g.K % 8) != 0 || (g.lda % 8) != 0 || (g.ldw % 8) != 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.W) & 15)) return -1;
+  if ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.ldo % 8) != 0) return -1;
+  if (g.epi == INL_EPI_RESID_BF16 && ((reinterpret_cast<uintptr_t>(g.resid) & 15) || (g.ldr % 8) != 0)) return -1;
+  int bn = (g.N <= 128 || (g.N % 256) != 0) ? 128 : 256;
+  if (g.epi == INL_EPI_GATED_BF16) {
+    // Gate/up interleaved in blocks of bn/2 rows; the caller picks the block.
+    bn = g.gate_block * 2;
+    if ((bn != 128 && bn != 256) || (g.N % bn) != 0) return -1;
+  }
+  if (g.force_bn == 128 || g.force_bn == 256) {
+    if (g.epi == INL_EPI_GATED_BF16 && g.force_bn != bn) return -1;
+    bn = g.force_bn;
+  }
+  CUtensorMap ta, tb;
+  if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
+  if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, bn)) return -2;
+  EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.row_scale, g.M, g.N};
+  cudaError_t err;
+  if (bn == 256) {
+    switch (g.epi) {
+      case INL_EPI_BF16: err = launch_gemm<256, INL_EPI_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      default: return -1;
+    }
+  } else {
+    switch (g.epi) {
+      case INL_EPI_BF16: err = launch_gemm<128, INL_EPI_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_BF16: err = launch_gemm<128, INL_EPI_RESID_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_F32: err = launch_gemm<128, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_BF16: err = dispatch_act<128, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      default: return -1;
+    }
+  }
+  return err == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace inl

@@ -1,0 +1,144 @@
+// Host-side launchers of the sm_100a kernels (internal interface of
+// libinl_cuda.so; the public C ABI is include/inl_cuda.h).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum InlEpilogue : int {
+  INL_EPI_BF16 = 0,        // out = bf16(acc * row_scale)
+  INL_EPI_RESID_BF16 = 1,  // out = bf16(bf16(acc * row_scale) + resid)   (out may alias resid)
+  INL_EPI_GATED_BF16 = 2,  // out[:, n/2] = act(gate) * up, gate/up interleaved in gate_block-row blocks
+  INL_EPI_F32 = 3,         // out = acc * row_scale (f32)
+  INL_EPI_F32_ROWL2 = 4,   // out = v / max(|v|, 1e-12), v = acc (f32), needs N <= tile width (SIMT path only)
+};
+
+enum InlAct : int { INL_ACT_SILU = 0, INL_ACT_GELU_ERF = 1, INL_ACT_GELU_TANH = 2 };
+
+namespace inl {
+
+struct GemmArgs {
+  const __nv_bfloat16* A = nullptr;  // [M, K] row stride lda
+  long long lda = 0;
+  const __nv_bfloat16* W = nullptr;  // [N, K] row stride ldw
+  long long ldw = 0;
+  int M = 0, N = 0, K = 0;
+  int epi = INL_EPI_BF16;
+  int act = INL_ACT_SILU;
+  int gate_block = 128;  // rows per gate (or up) block of the interleaved weight
+  void* out = nullptr;
+  long long ldo = 0;
+  const __nv_bfloat16* resid = nullptr;
+  long long ldr = 0;
+  const float* row_scale = nullptr;
+  int* status = nullptr;
+  int max_ctas = 0;   // 0 = one CTA per SM
+  int force_bn = 0;   // 0 = automatic tile width
+};
+
+// tcgen05 bf16 GEMM; returns 0 on success, <0 on bad arguments / launch error.
+int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream);
+
+struct GemmF32Args {
+  const float* A = nullptr;
+  long long lda = 0;
+  const float* W = nullptr;
+  long long ldw = 0;
+  const float* bias = nullptr;  // [N] or null
+  int M = 0, N = 0, K = 0;
+  int epi = INL_EPI_F32;  // INL_EPI_F32, INL_EPI_RESID_BF16 (meaning: f32 residual add), INL_EPI_GATED_BF16 (f32)
+  int act = INL_ACT_SILU;
+  int gate_block = 64;
+  float* out = nullptr;
+  long long ldo = 0;
+  const float* resid = nullptr;
+  long long ldr = 0;
+};
+
+// SIMT f32 GEMM (f32-accurate path for the f32 configurations).
+int gemm_f32_tn(const GemmF32Args& g, cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise
+// out[t, :] = table[ids[t], :] * scale ; ids >= vocab set *status = BAD_INDEX and write zeros.
+int embed_gather(const uint32_t* ids, int T, const void* table, int table_bf16, int vocab, int H, float scale,
+                 void* out, int out_bf16, int* status, cudaStream_t s);
+
+// out = x / sqrt(mean(x^2) + eps) * w   (w f32, may be null)  rows x H
+int rms_norm(const void* x, int x_bf16, long long ldx, const float* w, float eps, int rows, int H, void* out,
+             int out_bf16, long long ldo, cudaStream_t s);
+
+// LayerNorm without bias (bias may be null): (x - mu)/sqrt(var + eps) * w + b
+int layer_norm(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
+               void* out, int out_bf16, long long ldo, cudaStream_t s);
+
+// In place on qkv rows [T, ld]: per head RMSNorm (weights qw/kw, may be null) on the
+// q heads (cols [0, hq*d)) and k heads (cols [hq*d, (hq+hkv)*d)), optional weightless
+// RMSNorm on v heads, then half-split RoPE on q and k with position pos[t] and the
+// table cos/sin [max_pos, d/2]. rope_sel: which of (cos0,sin0)/(cos1,sin1) to use.
+struct QkRopeArgs {
+  void* qkv = nullptr;
+  int bf16 = 1;
+  long long ld = 0;
+  int T = 0, hq = 0, hkv = 0, d = 0;
+  const float* qw = nullptr;
+  const float* kw = nullptr;
+  int v_norm = 0;
+  float eps = 1e-6f;
+  const int* pos = nullptr;
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  int max_pos = 0;
+  int* status = nullptr;
+};
+int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s);
+
+// Position of every packed token inside its text: pos[t] = t - cu[i] for cu[i] <= t < cu[i+1].
+int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s);
+
+// Dense last-token head: out[i] = L2(RMSNorm(h[cu[i+1]-1])) in f32, L2 = x / sqrt(sum x^2 + 1e-12).
+int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, int n, const float* w, float eps,
+                       int H, float* out, cudaStream_t s);
+
+// Row L2: out = x / max(|x|, clamp) for f32 rows (x may alias out).
+int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min, float* out, long long ldo,
+                cudaStream_t s);
+
+// Segment mean over packed rows: out[i] = mean_{t in text i} x[t] (f32 out) .
+int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, float* out,
+                 cudaStream_t s);
+
+// Truncate rows of [n, D] f32 to `dim` and renormalise (Matryoshka); out [n, dim].
+int truncate_normalize(const float* x, int n, int D, int dim, float* out, cudaStream_t s);
+
+// f32 -> bf16/f32 conversion with row remapping: dst_row(r) = (r / blk) * blk_stride + off + r % blk.
+int convert_rows(const float* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
+                 long long blk_stride, long long off, cudaStream_t s);
+int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst,
+                      int blk, long long blk_stride, long long off, cudaStream_t s);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  const void* q = nullptr;  // [T, ldq] q heads at column h*d
+  const void* k = nullptr;  // [T, ldk] kv heads at column g*d
+  const void* v = nullptr;
+  long long ldq = 0, ldk = 0, ldv = 0;
+  void* out = nullptr;  // [T, ldo] q heads at column h*d
+  long long ldo = 0;
+  int bf16 = 1;
+  int hq = 0, hkv = 0, d = 0;
+  float scale = 1.0f;
+  int causal = 0;
+  int window = -1;  // |q - k| > window masked when >= 0
+  const int* cu = nullptr;     // device [n+1]
+  int n = 0;
+  const int2* work = nullptr;  // device [n_work] = (text, q_block)
+  int n_work = 0;
+  int q_block = 64;
+};
+int attention(const AttnArgs& a, cudaStream_t s);
+
+// Number of query rows per work item the attention kernels expect.
+int attention_q_block(int bf16, int d);
+
+}  // namespace inl

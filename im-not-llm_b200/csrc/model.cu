@@ -1,0 +1,997 @@
+// libinl_cuda runtime: model load (config JSON + safetensors or named host
+// tensors), device weight layout, workspaces, and the forward launch plan of
+// the packed variable-length encoder, exported through the C ABI of
+// include/inl_cuda.h.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/inl_cuda.h"
+#include "../../include/inl_cuda_kernels.h"
+#include "common.cuh"
+#include "model.h"
+
+using inl::DevBuf;
+using inl::ProfileRec;
+using inl::ModelConfig;
+using inl::TensorMap;
+using inl::TensorSrc;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define INL_CUDA_TRY(expr, what)                                                              \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess)                                                                    \
+      return fail(INL_ERR_INFERENCE, std::string(what) + ": " + cudaGetErrorString(_e));      \
+  } while (0)
+
+#define INL_K_TRY(expr, what)                                                                 \
+  do {                                                                                        \
+    int _r = (expr);                                                                          \
+    if (_r != 0) {                                                                            \
+      cudaError_t _e = cudaGetLastError();                                                    \
+      return fail(INL_ERR_INFERENCE, std::string(what) + " failed (" + std::to_string(_r) + \
+                                         "): " + cudaGetErrorString(_e));                     \
+    }                                                                                         \
+  } while (0)
+
+// ------------------------------------------------------------ config parsing
+double num_or(const inl::json::Value& v, const char* key, double def) {
+  const inl::json::Value* x = v.get(key);
+  return (x && x->is_num()) ? x->num : def;
+}
+bool bool_or(const inl::json::Value& v, const char* key, bool def) {
+  const inl::json::Value* x = v.get(key);
+  return (x && x->kind == inl::json::Value::Bool) ? x->b : def;
+}
+std::string str_or(const inl::json::Value& v, const char* key, const std::string& def) {
+  const inl::json::Value* x = v.get(key);
+  return (x && x->kind == inl::json::Value::String) ? x->str : def;
+}
+
+int parse_config(const std::string& text, ModelConfig& c) {
+  inl::json::Value root;
+  try {
+    root = inl::json::parse(text);
+  } catch (const std::exception& e) {
+    return fail(INL_ERR_CONFIG, std::string("config: ") + e.what());
+  }
+  if (root.kind != inl::json::Value::Object) return fail(INL_ERR_CONFIG, "config: not a JSON object");
+  // Qwen3-VL style nesting (crates/inl-text/src/qwen3/mod.rs:55-69).
+  if (const inl::json::Value* tc = root.get("text_config"); tc && tc->kind == inl::json::Value::Object)
+    root = *tc;
+  const std::string mt = str_or(root, "model_type", "qwen3");
+  if (mt == "qwen3") c.arch = inl::ARCH_QWEN3;
+  else if (mt == "modernbert") c.arch = inl::ARCH_MODERNBERT;
+  else if (mt == "gemma_style" || mt == "gemma3_text" || mt == "embeddinggemma")
+    c.arch = inl::ARCH_GEMMA;
+  else
+    return fail(INL_ERR_CONFIG, "config: unsupported model_type '" + mt + "'");
+  c.H = static_cast<int>(num_or(root, "hidden_size", 0));
+  c.I = static_cast<int>(num_or(root, "intermediate_size", 0));
+  c.hq = static_cast<int>(num_or(root, "num_attention_heads", 0));
+  c.hkv = static_cast<int>(num_or(root, "num_key_value_heads", c.hq));
+  c.layers = static_cast<int>(num_or(root, "num_hidden_layers", 0));
+  c.V = static_cast<int>(num_or(root, "vocab_size", 0));
+  c.d = static_cast<int>(num_or(root, "head_dim", c.hq > 0 ? c.H / c.hq : 0));
+  if (c.H <= 0 || c.I <= 0 || c.hq <= 0 || c.hkv <= 0 || c.layers <= 0 || c.V <= 0 || c.d <= 0)
+    return fail(INL_ERR_CONFIG, "config: missing or invalid model dimensions");
+  if (c.hq % c.hkv != 0)
+    return fail(INL_ERR_CONFIG, "config: num_attention_heads must be a multiple of num_key_value_heads");
+  if (bool_or(root, "attention_bias", false))
+    return fail(INL_ERR_CONFIG, "config: attention_bias = true is not supported");
+  c.eps = static_cast<float>(num_or(root, "rms_norm_eps", 1e-6));
+  c.theta = num_or(root, "rope_theta", 10000.0);
+  c.max_pos = static_cast<int>(std::min(32768.0, num_or(root, "max_position_embeddings", 32768.0)));
+  c.pad_token_id = static_cast<int>(num_or(root, "pad_token_id", 0));
+  if (c.arch == inl::ARCH_QWEN3) {
+    c.causal = bool_or(root, "is_causal", true);
+    c.theta_local = c.theta;
+  } else if (c.arch == inl::ARCH_MODERNBERT) {
+    c.causal = false;
+    c.norm_eps = static_cast<float>(num_or(root, "norm_eps", 1e-5));
+    c.theta = num_or(root, "global_rope_theta", 160000.0);
+    c.theta_local = num_or(root, "local_rope_theta", 10000.0);
+    c.global_every = static_cast<int>(num_or(root, "global_attn_every_n_layers", 3));
+    c.local_half_window = static_cast<int>(num_or(root, "local_attention", 128)) / 2;
+    c.logit_shift = static_cast<float>(num_or(root, "splade_logit_shift", 0.0));
+  } else {
+    c.causal = false;
+    c.sliding_window = static_cast<int>(num_or(root, "sliding_window", 512));
+    c.full_every = static_cast<int>(num_or(root, "full_attention_every_n_layers", 6));
+    c.theta_local = num_or(root, "rope_local_base_freq", 10000.0);
+    c.attn_scale = static_cast<float>(num_or(root, "query_pre_attn_scalar_inverse", 1.0));
+    c.embed_scale = static_cast<float>(std::sqrt(static_cast<double>(c.H)));
+  }
+  return INL_OK;
+}
+
+// ------------------------------------------------------------ safetensors
+struct MappedFile {
+  void* base = nullptr;
+  size_t size = 0;
+  ~MappedFile() {
+    if (base) munmap(base, size);
+  }
+};
+
+int read_safetensors(const char* path, MappedFile& mf, TensorMap& out) {
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(INL_ERR_INFERENCE, std::string("cannot open ") + path);
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 8) {
+    close(fd);
+    return fail(INL_ERR_INFERENCE, std::string("bad safetensors file ") + path);
+  }
+  mf.size = static_cast<size_t>(st.st_size);
+  mf.base = mmap(nullptr, mf.size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (mf.base == MAP_FAILED) {
+    mf.base = nullptr;
+    return fail(INL_ERR_INFERENCE, std::string("mmap failed for ") + path);
+  }
+  uint64_t hlen = 0;
+  std::memcpy(&hlen, mf.base, 8);
+  if (hlen + 8 > mf.size) return fail(INL_ERR_INFERENCE, "safetensors header overruns the file");
+  std::string header(static_cast<const char*>(mf.base) + 8, hlen);
+  inl::json::Value h;
+  try {
+    h = inl::json::parse(header);
+  } catch (const std::exception& e) {
+    return fail(INL_ERR_INFERENCE, std::string("safetensors header: ") + e.what());
+  }
+  const char* data = static_cast<const char*>(mf.base) + 8 + hlen;
+  const size_t data_size = mf.size - 8 - hlen;
+  for (const auto& kv : h.obj) {
+    if (kv.first == "__metadata__") continue;
+    const inl::json::Value& t = kv.second;
+    const inl::json::Value* dt = t.get("dtype");
+    const inl::json::Value* sh = t.get("shape");
+    const inl::json::Value* off = t.get("data_offsets");
+    if (!dt || !sh || !off || off->arr.size() != 2) return fail(INL_ERR_INFERENCE, "bad tensor entry " + kv.first);
+    TensorSrc src;
+    if (dt->str == "F32") src.bf16 = 0;
+    else if (dt->str == "BF16") src.bf16 = 1;
+    else continue;  // other dtypes are not model weights this library reads
+    int64_t numel = 1;
+    for (const auto& d : sh->arr) {
+      src.shape.push_back(static_cast<int64_t>(d.num));
+      numel *= static_cast<int64_t>(d.num);
+    }
+    const size_t b = static_cast<size_t>(off->arr[0].num), e = static_cast<size_t>(off->arr[1].num);
+    if (e > data_size || b > e || (e - b) != static_cast<size_t>(numel) * (src.bf16 ? 2 : 4))
+      return fail(INL_ERR_INFERENCE, "tensor " + kv.first + " has inconsistent offsets");
+    src.data = data + b;
+    src.numel = numel;
+    out[kv.first] = src;
+  }
+  return INL_OK;
+}
+
+// ------------------------------------------------------------ weight upload
+struct Loader {
+  inl_model* m;
+  const TensorMap& t;
+  std::string prefix;  // tried as "<prefix>name" first, then "name"
+  DevBuf staging;
+
+  ~Loader() { staging.release(); }
+
+  const TensorSrc* find(const std::string& name) const {
+    if (!prefix.empty()) {
+      auto it = t.find(prefix + name);
+      if (it != t.end()) return &it->second;
+    }
+    auto it = t.find(name);
+    return it == t.end() ? nullptr : &it->second;
+  }
+
+  void* alloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    m->allocs.push_back(p);
+    return p;
+  }
+
+  // Upload `name` ([rows, cols]) into dst rows remapped as (r / blk) * blk_stride + off + r % blk.
+  int upload(const std::string& name, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
+             long long blk_stride, long long off) {
+    const TensorSrc* s = find(name);
+    if (!s) return fail(INL_ERR_INFERENCE, "missing weight " + prefix + name);
+    if (s->numel != static_cast<int64_t>(rows) * cols)
+      return fail(INL_ERR_INFERENCE, "weight " + name + " has " + std::to_string(s->numel) + " values, expected " +
+                                         std::to_string(static_cast<long long>(rows) * cols));
+    const size_t bytes = static_cast<size_t>(s->numel) * (s->bf16 ? 2 : 4);
+    INL_CUDA_TRY(staging.ensure(bytes), "staging allocation");
+    INL_CUDA_TRY(cudaMemcpy(staging.p, s->data, bytes, cudaMemcpyHostToDevice), "weight upload");
+    int r = s->bf16 ? inl::convert_bf16_rows(staging.as<__nv_bfloat16>(), rows, cols, dst, dst_bf16, ld_dst, blk,
+                                             blk_stride, off, m->stream)
+                    : inl::convert_rows(staging.as<float>(), rows, cols, dst, dst_bf16, ld_dst, blk, blk_stride, off,
+                                        m->stream);
+    if (r != 0) return fail(INL_ERR_INFERENCE, "weight conversion launch failed");
+    INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "weight conversion");
+    return INL_OK;
+  }
+
+  int matrix(const std::string& name, int rows, int cols, void** out, int as_bf16) {
+    *out = alloc(static_cast<size_t>(rows) * cols * (as_bf16 ? 2 : 4));
+    if (!*out) return fail(INL_ERR_INFERENCE, "out of device memory for " + name);
+    return upload(name, rows, cols, *out, as_bf16, cols, rows, 0, 0);
+  }
+
+  int vec(const std::string& name, int n, float** out, bool optional = false, float fill = 1.f) {
+    *out = static_cast<float*>(alloc(static_cast<size_t>(n) * 4));
+    if (!*out) return fail(INL_ERR_INFERENCE, "out of device memory for " + name);
+    if (!find(name)) {
+      if (!optional) return fail(INL_ERR_INFERENCE, "missing weight " + prefix + name);
+      std::vector<float> v(n, fill);
+      INL_CUDA_TRY(cudaMemcpy(*out, v.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "fill");
+      return INL_OK;
+    }
+    return upload(name, 1, n, *out, 0, n, 1, 0, 0);
+  }
+};
+
+int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out) {
+  const int half = m->c.d / 2;
+  const int P = m->c.max_pos;
+  std::vector<float> c(static_cast<size_t>(P) * half), s(static_cast<size_t>(P) * half);
+  // RotaryTable::new (crates/inl-text/src/qwen3/mod.rs:129-153): f64 angles, stored f32.
+  std::vector<double> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = 1.0 / std::pow(theta, static_cast<double>(2 * i) / m->c.d);
+  for (int p = 0; p < P; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double a = static_cast<double>(p) * inv[i];
+      c[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(a));
+      s[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(a));
+    }
+  const size_t bytes = c.size() * 4;
+  void *dc = nullptr, *ds = nullptr;
+  INL_CUDA_TRY(cudaMalloc(&dc, bytes), "rope table");
+  m->allocs.push_back(dc);
+  INL_CUDA_TRY(cudaMalloc(&ds, bytes), "rope table");
+  m->allocs.push_back(ds);
+  INL_CUDA_TRY(cudaMemcpy(dc, c.data(), bytes, cudaMemcpyHostToDevice), "rope upload");
+  INL_CUDA_TRY(cudaMemcpy(ds, s.data(), bytes, cudaMemcpyHostToDevice), "rope upload");
+  *cos_out = static_cast<float*>(dc);
+  *sin_out = static_cast<float*>(ds);
+  return INL_OK;
+}
+
+// Qwen3 weights (crates/inl-text/src/qwen3/mod.rs:180-330 tensor names).
+int load_qwen3(inl_model* m, Loader& L) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv = q_out + 2 * kv_out;
+  const int gb = m->gate_block;
+  if (c.I % gb != 0)
+    return fail(INL_ERR_CONFIG, "intermediate_size must be a multiple of " + std::to_string(gb));
+  int r;
+  if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
+  m->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    inl::LayerWeights& w = m->layers[l];
+    const size_t es = bf ? 2 : 4;
+    w.wqkv = L.alloc(static_cast<size_t>(qkv) * c.H * es);
+    w.wo = L.alloc(static_cast<size_t>(c.H) * q_out * es);
+    w.wgu = L.alloc(static_cast<size_t>(2) * c.I * c.H * es);
+    w.wd = L.alloc(static_cast<size_t>(c.H) * c.I * es);
+    if (!w.wqkv || !w.wo || !w.wgu || !w.wd) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+    if ((r = L.upload(p + "self_attn.q_proj.weight", q_out, c.H, w.wqkv, bf, c.H, q_out, 0, 0))) return r;
+    if ((r = L.upload(p + "self_attn.k_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out))) return r;
+    if ((r = L.upload(p + "self_attn.v_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out + kv_out)))
+      return r;
+    if ((r = L.upload(p + "self_attn.o_proj.weight", c.H, q_out, w.wo, bf, q_out, c.H, 0, 0))) return r;
+    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, 0))) return r;
+    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, gb))) return r;
+    if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
+    if ((r = L.vec(p + "self_attn.q_norm.weight", c.d, &w.qn))) return r;
+    if ((r = L.vec(p + "self_attn.k_norm.weight", c.d, &w.kn))) return r;
+    if ((r = L.vec(p + "input_layernorm.weight", c.H, &w.ln1))) return r;
+    if ((r = L.vec(p + "post_attention_layernorm.weight", c.H, &w.ln2))) return r;
+  }
+  if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;
+  return INL_OK;
+}
+
+int create_common(const char* config_json, int device, int dtype, inl_model** out, inl_model** mm) {
+  if (!out) return fail(INL_ERR_CONFIG, "out is NULL");
+  *out = nullptr;
+  if (!config_json) return fail(INL_ERR_CONFIG, "config_json is NULL");
+  if (dtype != INL_DTYPE_F32 && dtype != INL_DTYPE_BF16) return fail(INL_ERR_CONFIG, "unknown dtype");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0)
+    return fail(INL_ERR_CONFIG, "no CUDA device is available");
+  if (device < 0 || device >= ndev) return fail(INL_ERR_CONFIG, "device ordinal out of range");
+  cudaDeviceProp prop;
+  INL_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "device query");
+  if (prop.major != 10)
+    return fail(INL_ERR_CONFIG, std::string("libinl_cuda is built for sm_100a (B200); device is ") + prop.name);
+  INL_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  inl_model* m = new inl_model();
+  m->dtype = dtype;
+  m->device = device;
+  m->gate_block = dtype == INL_DTYPE_BF16 ? 128 : 64;
+  int r = parse_config(config_json, m->c);
+  if (r) {
+    delete m;
+    return r;
+  }
+  if (m->c.H % 8 != 0) {
+    delete m;
+    return fail(INL_ERR_CONFIG, "hidden_size must be a multiple of 8");
+  }
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&m->d_status, sizeof(int)) != cudaSuccess ||
+      cudaMallocHost(&m->h_status, sizeof(int)) != cudaSuccess ||
+      cudaMemset(m->d_status, 0, sizeof(int)) != cudaSuccess) {
+    inl_cuda_model_destroy(m);
+    return fail(INL_ERR_INFERENCE, "stream / status allocation failed");
+  }
+  *mm = m;
+  return INL_OK;
+}
+
+int load_weights(inl_model* m, const TensorMap& t) {
+  Loader L{m, t, "", {}};
+  // Qwen3-VL checkpoints nest the tower (crates/inl-text/src/qwen3/mod.rs:397-404).
+  if (!t.count("embed_tokens.weight")) {
+    for (const char* p : {"model.language_model.", "model.", "language_model."})
+      if (t.count(std::string(p) + "embed_tokens.weight")) {
+        L.prefix = p;
+        break;
+      }
+  }
+  int r = INL_OK;
+  switch (m->c.arch) {
+    case inl::ARCH_QWEN3: r = load_qwen3(m, L); break;
+    default: r = fail(INL_ERR_CONFIG, "this model_type is not built into this library version"); break;
+  }
+  return r;
+}
+
+// ------------------------------------------------------------ forward plan
+struct Batch {
+  int n = 0;
+  int T = 0;
+  int max_len = 0;
+  const int32_t* cu_host = nullptr;
+};
+
+int check_inputs(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b) {
+  if (n < 0) return fail(INL_ERR_INVALID_INPUT, "n_texts is negative");
+  if (n > 0 && (!cu || !ids)) return fail(INL_ERR_INVALID_INPUT, "ids / cu_seqlens is NULL");
+  if (ids_mem != INL_MEM_HOST && ids_mem != INL_MEM_DEVICE) return fail(INL_ERR_INVALID_INPUT, "bad ids_mem");
+  b.n = n;
+  b.cu_host = cu;
+  if (n == 0) return INL_OK;
+  if (cu[0] != 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens[0] must be 0");
+  for (int i = 0; i < n; ++i) {
+    const int len = cu[i + 1] - cu[i];
+    if (len < 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
+    if (len > m->c.max_pos)
+      return fail(INL_ERR_INVALID_INPUT, "text " + std::to_string(i) + " has " + std::to_string(len) +
+                                             " tokens; the model accepts at most " + std::to_string(m->c.max_pos));
+    b.max_len = std::max(b.max_len, len);
+  }
+  b.T = cu[n];
+  if (ids_mem == INL_MEM_HOST) {
+    for (int t = 0; t < b.T; ++t)
+      if (ids[t] >= static_cast<uint32_t>(m->c.V))
+        return fail(INL_ERR_INVALID_INPUT, "token id " + std::to_string(ids[t]) + " at position " +
+                                               std::to_string(t) + " is outside the vocabulary");
+  }
+  return INL_OK;
+}
+
+size_t es(const inl_model* m) { return m->dtype == INL_DTYPE_BF16 ? 2 : 4; }
+
+int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const size_t T = static_cast<size_t>(std::max(b.T, 1));
+  const size_t e = es(m);
+  const size_t qkv_cols = static_cast<size_t>(c.hq + 2 * c.hkv) * c.d;
+  const size_t act_cols = static_cast<size_t>(c.I);
+  INL_CUDA_TRY(m->h.ensure(T * c.H * e), "workspace");
+  INL_CUDA_TRY(m->xn.ensure(T * c.H * e), "workspace");
+  INL_CUDA_TRY(m->qkv.ensure(T * std::max(qkv_cols, act_cols) * e), "workspace");
+  INL_CUDA_TRY(m->attn.ensure(T * static_cast<size_t>(c.hq) * c.d * e), "workspace");
+  INL_CUDA_TRY(m->ids.ensure(T * 4), "workspace");
+  INL_CUDA_TRY(m->pos.ensure(T * 4), "workspace");
+  INL_CUDA_TRY(m->cu.ensure(static_cast<size_t>(b.n + 1) * 4), "workspace");
+  INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
+  const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work) * 8 + 64;
+  if (stage > m->h_stage_bytes) {
+    if (m->h_stage) cudaFreeHost(m->h_stage);
+    m->h_stage = nullptr;
+    m->h_stage_bytes = 0;
+    INL_CUDA_TRY(cudaMallocHost(&m->h_stage, stage * 2), "pinned staging");
+    m->h_stage_bytes = stage * 2;
+  }
+  return INL_OK;
+}
+
+// Attention work items (text, query block), heaviest first so the long causal
+// tails start early and the short ones fill the gaps.
+int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch& b, int* n_work_out) {
+  const int qb = inl::attention_q_block(m->dtype == INL_DTYPE_BF16, m->c.d);
+  std::vector<std::pair<int, int2>> items;
+  for (int i = 0; i < b.n; ++i) {
+    const int L = b.cu_host[i + 1] - b.cu_host[i];
+    const int nb = (L + qb - 1) / qb;
+    for (int q = 0; q < nb; ++q) {
+      int cost = m->c.causal ? (q + 1) : nb;
+      items.push_back({cost, make_int2(i, q)});
+    }
+  }
+  std::stable_sort(items.begin(), items.end(), [](const auto& a, const auto& c) { return a.first > c.first; });
+  const int n_work = static_cast<int>(items.size());
+  int r = ensure_workspace(m, b, n_work);
+  if (r) return r;
+  int* cu_stage = m->h_stage;
+  std::memcpy(cu_stage, b.cu_host, static_cast<size_t>(b.n + 1) * 4);
+  int2* work_stage = reinterpret_cast<int2*>(cu_stage + ((b.n + 1 + 3) & ~3));
+  for (int i = 0; i < n_work; ++i) work_stage[i] = items[i].second;
+  INL_CUDA_TRY(cudaMemcpyAsync(m->cu.p, cu_stage, static_cast<size_t>(b.n + 1) * 4, cudaMemcpyHostToDevice,
+                               m->stream),
+               "cu_seqlens upload");
+  if (n_work > 0)
+    INL_CUDA_TRY(cudaMemcpyAsync(m->work.p, work_stage, static_cast<size_t>(n_work) * 8, cudaMemcpyHostToDevice,
+                                 m->stream),
+                 "work list upload");
+  if (b.T > 0) {
+    if (ids_mem == INL_MEM_HOST)
+      INL_CUDA_TRY(cudaMemcpyAsync(m->ids.p, ids, static_cast<size_t>(b.T) * 4, cudaMemcpyHostToDevice, m->stream),
+                   "ids upload");
+    INL_K_TRY(inl::token_positions(m->cu.as<int>(), b.n, b.T, m->pos.as<int>(), m->stream), "positions");
+    m->launches++;
+  }
+  *n_work_out = n_work;
+  return INL_OK;
+}
+
+cudaEvent_t take_event(inl_model* m) {
+  if (!m->event_pool.empty()) {
+    cudaEvent_t e = m->event_pool.back();
+    m->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// y = x . W^T with the model dtype's GEMM and a fused epilogue.
+int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int N, int K, int epi, int act,
+           void* out, long long ldo, const void* resid, long long ldr, int kind) {
+  ProfileRec rec{};
+  if (m->profiling) {
+    rec.start = take_event(m);
+    rec.stop = take_event(m);
+    rec.flops = 2.0 * M * N * K;
+    rec.kind = kind;
+    cudaEventRecord(rec.start, m->stream);
+  }
+  int r;
+  if (m->dtype == INL_DTYPE_BF16) {
+    inl::GemmArgs g;
+    g.A = static_cast<const __nv_bfloat16*>(A);
+    g.lda = lda;
+    g.W = static_cast<const __nv_bfloat16*>(W);
+    g.ldw = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.epi = epi;
+    g.act = act;
+    g.gate_block = m->gate_block;
+    g.out = out;
+    g.ldo = ldo;
+    g.resid = static_cast<const __nv_bfloat16*>(resid);
+    g.ldr = ldr;
+    g.status = m->d_status;
+    r = inl::gemm_bf16_tn(g, m->stream);
+  } else {
+    inl::GemmF32Args g;
+    g.A = static_cast<const float*>(A);
+    g.lda = lda;
+    g.W = static_cast<const float*>(W);
+    g.ldw = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.epi = epi == INL_EPI_BF16 ? INL_EPI_F32 : epi;
+    g.act = act;
+    g.gate_block = m->gate_block;
+    g.out = static_cast<float*>(out);
+    g.ldo = ldo;
+    g.resid = static_cast<const float*>(resid);
+    g.ldr = ldr;
+    r = inl::gemm_f32_tn(g, m->stream);
+  }
+  m->launches++;
+  if (m->profiling) {
+    cudaEventRecord(rec.stop, m->stream);
+    m->prof.push_back(rec);
+  }
+  return r;
+}
+
+// Embedding + every layer; leaves the last hidden state in m->h.
+int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int T = b.T;
+  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv_cols = q_out + 2 * kv_out;
+  cudaStream_t s = m->stream;
+  INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, bf, c.V, c.H, 1.0f, m->h.p, bf, m->d_status, s),
+            "embedding");
+  m->launches++;
+  for (int l = 0; l < c.layers; ++l) {
+    const inl::LayerWeights& w = m->layers[l];
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, w.ln1, c.eps, T, c.H, m->xn.p, bf, c.H, s), "input norm");
+    m->launches++;
+    INL_K_TRY(linear(m, m->xn.p, c.H, w.wqkv, T, qkv_cols, c.H, INL_EPI_BF16, 0, m->qkv.p, qkv_cols, nullptr, 0, 0),
+              "qkv projection");
+    inl::QkRopeArgs qa;
+    qa.qkv = m->qkv.p;
+    qa.bf16 = bf;
+    qa.ld = qkv_cols;
+    qa.T = T;
+    qa.hq = c.hq;
+    qa.hkv = c.hkv;
+    qa.d = c.d;
+    qa.qw = w.qn;
+    qa.kw = w.kn;
+    qa.eps = c.eps;
+    qa.pos = m->pos.as<int>();
+    qa.cos = m->cos0;
+    qa.sin = m->sin0;
+    qa.max_pos = c.max_pos;
+    qa.status = m->d_status;
+    INL_K_TRY(inl::qk_norm_rope(qa, s), "q/k norm + rope");
+    m->launches++;
+    inl::AttnArgs aa;
+    const size_t e = es(m);
+    aa.q = m->qkv.p;
+    aa.k = static_cast<const char*>(m->qkv.p) + static_cast<size_t>(q_out) * e;
+    aa.v = static_cast<const char*>(m->qkv.p) + static_cast<size_t>(q_out + kv_out) * e;
+    aa.ldq = aa.ldk = aa.ldv = qkv_cols;
+    aa.out = m->attn.p;
+    aa.ldo = q_out;
+    aa.bf16 = bf;
+    aa.hq = c.hq;
+    aa.hkv = c.hkv;
+    aa.d = c.d;
+    aa.scale = 1.0f / std::sqrt(static_cast<float>(c.d));
+    aa.causal = c.causal ? 1 : 0;
+    aa.window = -1;
+    aa.cu = m->cu.as<int>();
+    aa.n = b.n;
+    aa.work = m->work.as<int2>();
+    aa.n_work = n_work;
+    aa.q_block = inl::attention_q_block(bf, c.d);
+    INL_K_TRY(inl::attention(aa, s), "attention");
+    m->launches++;
+    INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, c.H, q_out, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 1),
+              "o projection");
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, w.ln2, c.eps, T, c.H, m->xn.p, bf, c.H, s), "post-attention norm");
+    m->launches++;
+    INL_K_TRY(linear(m, m->xn.p, c.H, w.wgu, T, 2 * c.I, c.H, INL_EPI_GATED_BF16, INL_ACT_SILU, m->qkv.p, c.I,
+                     nullptr, 0, 2),
+              "gate/up projection");
+    INL_K_TRY(linear(m, m->qkv.p, c.I, w.wd, T, c.H, c.I, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 3),
+              "down projection");
+  }
+  return INL_OK;
+}
+
+int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b) {
+  int r = check_inputs(m, ids, ids_mem, cu, n, b);
+  if (r) return r;
+  INL_CUDA_TRY(cudaSetDevice(m->device), "cudaSetDevice");
+  int n_work = 0;
+  if ((r = plan_and_upload(m, ids, ids_mem, b, &n_work))) return r;
+  if (b.T == 0) return INL_OK;
+  if (ids_mem == INL_MEM_DEVICE)
+    INL_CUDA_TRY(cudaMemcpyAsync(m->ids.p, ids, static_cast<size_t>(b.T) * 4, cudaMemcpyDeviceToDevice, m->stream),
+                 "ids copy");
+  switch (m->c.arch) {
+    case inl::ARCH_QWEN3: return qwen3_tower(m, b, n_work);
+    default: return fail(INL_ERR_CONFIG, "model_type not built");
+  }
+}
+
+// Check the device status word, then copy `bytes` of device results to the caller.
+int finish(inl_model* m, const void* dev_src, size_t bytes, void* out, int out_mem) {
+  INL_CUDA_TRY(cudaMemcpyAsync(m->h_status, m->d_status, sizeof(int), cudaMemcpyDeviceToHost, m->stream),
+               "status read");
+  if (bytes > 0 && out != dev_src) {
+    const cudaMemcpyKind kind = out_mem == INL_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+    INL_CUDA_TRY(cudaMemcpyAsync(out, dev_src, bytes, kind, m->stream), "result copy");
+  }
+  INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "forward");
+  const int st = *m->h_status;
+  if (st != 0) {
+    cudaMemsetAsync(m->d_status, 0, sizeof(int), m->stream);
+    cudaStreamSynchronize(m->stream);
+    switch (st) {
+      case INL_DEV_BAD_INDEX:
+        return fail(INL_ERR_INVALID_INPUT, "a token id or position was outside the model's tables");
+      default:
+        return fail(INL_ERR_TIMEOUT, "a device wait ran past its limit (status " + std::to_string(st) + ")");
+    }
+  }
+  return INL_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int inl_cuda_model_create_from_tensors(const char* config_json, int n_tensors, const char* const* names,
+                                       const float* const* data, const int64_t* numels, int device, int dtype,
+                                       inl_model** out) {
+  inl_model* m = nullptr;
+  int r = create_common(config_json, device, dtype, out, &m);
+  if (r) return r;
+  TensorMap t;
+  for (int i = 0; i < n_tensors; ++i) {
+    if (!names || !names[i] || !data || !data[i] || !numels) {
+      inl_cuda_model_destroy(m);
+      return fail(INL_ERR_CONFIG, "NULL tensor name or data");
+    }
+    TensorSrc s;
+    s.data = data[i];
+    s.numel = numels[i];
+    t[names[i]] = s;
+  }
+  r = load_weights(m, t);
+  if (r) {
+    inl_cuda_model_destroy(m);
+    return r;
+  }
+  *out = m;
+  return INL_OK;
+}
+
+int inl_cuda_model_create(const char* config_json, const char* safetensors_path, int device, int dtype,
+                          inl_model** out) {
+  inl_model* m = nullptr;
+  int r = create_common(config_json, device, dtype, out, &m);
+  if (r) return r;
+  if (!safetensors_path) {
+    inl_cuda_model_destroy(m);
+    return fail(INL_ERR_CONFIG, "safetensors_path is NULL");
+  }
+  MappedFile mf;
+  TensorMap t;
+  r = read_safetensors(safetensors_path, mf, t);
+  if (!r) r = load_weights(m, t);
+  if (r) {
+    inl_cuda_model_destroy(m);
+    return r;
+  }
+  *out = m;
+  return INL_OK;
+}
+
+int inl_cuda_model_set_dense_head(inl_model* m, const float* weight, int out_features, int in_features,
+                                  const float* bias) {
+  if (!m || !weight) return fail(INL_ERR_CONFIG, "NULL model or weight");
+  if (in_features != m->c.H)
+    return fail(INL_ERR_CONFIG, "Dense in_features must equal hidden_size (" + std::to_string(m->c.H) + ")");
+  if (out_features <= 0 || out_features % 8 != 0) return fail(INL_ERR_CONFIG, "Dense out_features must be a multiple of 8");
+  INL_CUDA_TRY(cudaSetDevice(m->device), "cudaSetDevice");
+  TensorMap t;
+  TensorSrc w;
+  w.data = weight;
+  w.numel = static_cast<int64_t>(out_features) * in_features;
+  t["linear.weight"] = w;
+  if (bias) {
+    TensorSrc b;
+    b.data = bias;
+    b.numel = out_features;
+    t["linear.bias"] = b;
+  }
+  Loader L{m, t, "", {}};
+  int r = L.matrix("linear.weight", out_features, in_features, &m->proj, m->dtype == INL_DTYPE_BF16);
+  if (r) return r;
+  m->proj_bias = nullptr;
+  if (bias && (r = L.vec("linear.bias", out_features, &m->proj_bias))) return r;
+  m->proj_out = out_features;
+  return INL_OK;
+}
+
+int inl_cuda_forward_hidden(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
+                            int normalize_final, float* out, int out_mem) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  Batch b;
+  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.T == 0) return INL_OK;
+  const ModelConfig& c = m->c;
+  const size_t bytes = static_cast<size_t>(b.T) * c.H * 4;
+  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  if (normalize_final) {
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->out.p, 0, c.H, m->stream),
+              "final norm");
+  } else {
+    if (bf) {
+      INL_K_TRY(inl::convert_bf16_rows(m->h.as<__nv_bfloat16>(), b.T, c.H, m->out.p, 0, c.H, b.T, 0, 0, m->stream),
+                "cast");
+    } else {
+      INL_CUDA_TRY(cudaMemcpyAsync(m->out.p, m->h.p, bytes, cudaMemcpyDeviceToDevice, m->stream), "copy");
+    }
+  }
+  m->launches++;
+  return finish(m, m->out.p, bytes, out, out_mem);
+}
+
+int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
+                           int out_dim, float* out, int out_mem) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  if (out_mem != INL_MEM_HOST && out_mem != INL_MEM_DEVICE) return fail(INL_ERR_INVALID_INPUT, "bad out_mem");
+  const ModelConfig& c = m->c;
+  if (out_dim != 0 && c.arch != inl::ARCH_GEMMA)
+    return fail(INL_ERR_CONFIG, "output_dim is only supported for EmbeddingGemma-style models");
+  Batch b;
+  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.n == 0) return INL_OK;
+  if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
+  const size_t bytes = static_cast<size_t>(b.n) * c.H * 4;
+  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  INL_K_TRY(inl::last_token_norm_l2(m->h.p, bf, c.H, m->cu.as<int>(), b.n, m->final_norm, c.eps, c.H,
+                                    m->out.as<float>(), m->stream),
+            "last-token pooling");
+  m->launches++;
+  return finish(m, m->out.p, bytes, out, out_mem);
+}
+
+int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens,
+                                 int n_texts, float* out, int out_mem) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  if (!m->proj) return fail(INL_ERR_CONFIG, "no Dense head attached (inl_cuda_model_set_dense_head)");
+  const ModelConfig& c = m->c;
+  Batch b;
+  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.T == 0) return INL_OK;
+  if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const size_t bytes = static_cast<size_t>(b.T) * m->proj_out * 4;
+  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  // final norm on every token -> Dense projection (f32 out) -> F.normalize.
+  INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->xn.p, bf, c.H, m->stream),
+            "final norm");
+  m->launches++;
+  INL_K_TRY(linear(m, m->xn.p, c.H, m->proj, b.T, m->proj_out, c.H, INL_EPI_F32, 0, m->out.p, m->proj_out, nullptr,
+                   0, 4),
+            "dense projection");
+  if (m->proj_bias) return fail(INL_ERR_CONFIG, "Dense bias is not supported yet");
+  INL_K_TRY(inl::rows_l2_f32(m->out.as<float>(), m->proj_out, b.T, m->proj_out, 1e-12f, m->out.as<float>(),
+                             m->proj_out, m->stream),
+            "normalize");
+  m->launches++;
+  return finish(m, m->out.p, bytes, out, out_mem);
+}
+
+int inl_cuda_forward_sparse(inl_model* m, const uint32_t*, int, const int32_t*, int, float*, int) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  return fail(INL_ERR_CONFIG, "this model has no SPLADE head");
+}
+
+int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
+  if (!m || !out) return fail(INL_ERR_CONFIG, "NULL argument");
+  out->arch = m->c.arch;
+  out->dtype = m->dtype;
+  out->device = m->device;
+  out->hidden_size = m->c.H;
+  out->num_layers = m->c.layers;
+  out->vocab_size = m->c.V;
+  out->dense_dim = m->c.H;
+  out->multivector_dim = m->proj_out;
+  out->sparse_dim = 0;
+  out->max_text_tokens = m->c.max_pos;
+  out->is_causal = m->c.causal ? 1 : 0;
+  return INL_OK;
+}
+
+void inl_cuda_model_destroy(inl_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (void* p : m->allocs) cudaFree(p);
+  for (DevBuf* d : {&m->h, &m->xn, &m->qkv, &m->attn, &m->ids, &m->cu, &m->pos, &m->work, &m->out, &m->pooled,
+                    &m->tmp})
+    d->release();
+  for (auto& r : m->prof) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  for (cudaEvent_t e : m->event_pool) cudaEventDestroy(e);
+  if (m->h_stage) cudaFreeHost(m->h_stage);
+  if (m->h_status) cudaFreeHost(m->h_status);
+  if (m->d_status) cudaFree(m->d_status);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+int inl_cuda_last_error(char* buf, size_t len) {
+  if (buf && len > 0) {
+    const size_t n = std::min(len - 1, g_last_error.size());
+    std::memcpy(buf, g_last_error.data(), n);
+    buf[n] = '\0';
+  }
+  return static_cast<int>(g_last_error.size());
+}
+
+int inl_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+const char* inl_cuda_version(void) { return "inl_cuda 0.1.0 (sm_100a)"; }
+
+// ---------------------------------------------------------------- profiling
+int inl_cuda_model_set_profiling(inl_model* m, int enable) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  cudaStreamSynchronize(m->stream);
+  for (auto& r : m->prof) {
+    m->event_pool.push_back(r.start);
+    m->event_pool.push_back(r.stop);
+  }
+  m->prof.clear();
+  m->profiling = enable != 0;
+  return INL_OK;
+}
+
+int inl_cuda_model_profile(inl_model* m, int kind, int* launches, double* total_ms, double* flops) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "profile sync");
+  int n = 0;
+  double ms = 0, fl = 0;
+  for (const auto& r : m->prof) {
+    if (kind >= 0 && r.kind != kind) continue;
+    float t = 0;
+    cudaEventElapsedTime(&t, r.start, r.stop);
+    ms += t;
+    fl += r.flops;
+    ++n;
+  }
+  if (launches) *launches = n;
+  if (total_ms) *total_ms = ms;
+  if (flops) *flops = fl;
+  return INL_OK;
+}
+
+long long inl_cuda_model_launch_count(inl_model* m, int reset) {
+  if (!m) return -1;
+  const long long n = m->launches;
+  if (reset) m->launches = 0;
+  return n;
+}
+
+void* inl_cuda_model_stream(inl_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
+// ------------------------------------------------------------ kernel hooks
+int inl_cuda_gemm_bf16(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K, int epi, int act,
+                       int gate_block, void* out, int64_t ldo, const void* resid, int64_t ldr, int force_bn,
+                       int* status, void* stream) {
+  inl::GemmArgs g;
+  g.A = static_cast<const __nv_bfloat16*>(A);
+  g.lda = lda;
+  g.W = static_cast<const __nv_bfloat16*>(W);
+  g.ldw = ldw;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = epi;
+  g.act = act;
+  g.gate_block = gate_block;
+  g.out = out;
+  g.ldo = ldo;
+  g.resid = static_cast<const __nv_bfloat16*>(resid);
+  g.ldr = ldr;
+  g.status = status;
+  g.force_bn = force_bn;
+  const int r = inl::gemm_bf16_tn(g, static_cast<cudaStream_t>(stream));
+  if (r == -1) return fail(INL_ERR_INVALID_INPUT, "gemm: unsupported shape / alignment / epilogue");
+  if (r != 0) return fail(INL_ERR_INFERENCE, std::string("gemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+  return INL_OK;
+}
+
+int inl_cuda_gemm_f32(const float* A, int64_t lda, const float* W, int64_t ldw, int M, int N, int K, int epi, int act,
+                      float* out, int64_t ldo, const float* resid, int64_t ldr, void* stream) {
+  inl::GemmF32Args g;
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = epi;
+  g.act = act;
+  g.out = out;
+  g.ldo = ldo;
+  g.resid = resid;
+  g.ldr = ldr;
+  const int r = inl::gemm_f32_tn(g, static_cast<cudaStream_t>(stream));
+  if (r == -1) return fail(INL_ERR_INVALID_INPUT, "gemm_f32: unsupported shape / epilogue");
+  if (r != 0) return fail(INL_ERR_INFERENCE, "gemm_f32 launch failed");
+  return INL_OK;
+}
+
+int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq, int64_t ldk, int64_t ldv, void* out,
+                       int64_t ldo, int dtype, int hq, int hkv, int d, float scale, int causal, int window,
+                       const int32_t* cu_seqlens_host, int n_texts, void* stream) {
+  if (n_texts <= 0) return INL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int qb = inl::attention_q_block(dtype == INL_DTYPE_BF16, d);
+  std::vector<int2> work;
+  for (int i = 0; i < n_texts; ++i) {
+    const int L = cu_seqlens_host[i + 1] - cu_seqlens_host[i];
+    if (L < 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
+    for (int b = 0; b * qb < L; ++b) work.push_back(make_int2(i, b));
+  }
+  int* dcu = nullptr;
+  int2* dwork = nullptr;
+  INL_CUDA_TRY(cudaMalloc(&dcu, static_cast<size_t>(n_texts + 1) * 4), "alloc");
+  INL_CUDA_TRY(cudaMalloc(&dwork, std::max<size_t>(work.size(), 1) * 8), "alloc");
+  cudaMemcpyAsync(dcu, cu_seqlens_host, static_cast<size_t>(n_texts + 1) * 4, cudaMemcpyHostToDevice, s);
+  if (!work.empty()) cudaMemcpyAsync(dwork, work.data(), work.size() * 8, cudaMemcpyHostToDevice, s);
+  inl::AttnArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ldq = ldq;
+  a.ldk = ldk;
+  a.ldv = ldv;
+  a.out = out;
+  a.ldo = ldo;
+  a.bf16 = dtype == INL_DTYPE_BF16;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.d = d;
+  a.scale = scale;
+  a.causal = causal;
+  a.window = window;
+  a.cu = dcu;
+  a.n = n_texts;
+  a.work = dwork;
+  a.n_work = static_cast<int>(work.size());
+  a.q_block = qb;
+  const int r = inl::attention(a, s);
+  cudaStreamSynchronize(s);
+  cudaFree(dcu);
+  cudaFree(dwork);
+  if (r == -1) return fail(INL_ERR_INVALID_INPUT, "attention: unsupported head_dim / heads");
+  if (r != 0) return fail(INL_ERR_INFERENCE, "attention launch failed");
+  return INL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,134 @@
+// Model state of libinl_cuda: configuration, device weights, workspaces and
+// the per-forward launch plan. Internal to the library.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/inl_cuda.h"
+#include "json.h"
+#include "kernels.h"
+
+namespace inl {
+
+enum Arch : int { ARCH_QWEN3 = 0, ARCH_MODERNBERT = 1, ARCH_GEMMA = 2 };
+
+struct ModelConfig {
+  Arch arch = ARCH_QWEN3;
+  int H = 0, I = 0, hq = 0, hkv = 0, d = 0, layers = 0, V = 0;
+  float eps = 1e-6f;
+  double theta = 10000.0;        // rope theta (global / full layers)
+  double theta_local = 10000.0;  // rope theta of local / sliding layers
+  bool causal = true;
+  int max_pos = 32768;           // rope table rows = longest text accepted
+  // ModernBERT: a layer is global iff idx % global_every == 0; local layers
+  // mask |q - k| > local_half_window.
+  int global_every = 3;
+  int local_half_window = 64;
+  float norm_eps = 1e-5f;
+  int pad_token_id = 0;
+  // SPLADE head (ModernBERT MLM): logit shift before relu.
+  float logit_shift = 0.f;
+  // Gemma-style tower: sliding radius, full layer every `full_every` (idx % full_every == full_every-1),
+  // attention scale, embedding scale, dense head dims.
+  int sliding_window = 512;
+  int full_every = 6;
+  float attn_scale = 0.f;  // 0 = head_dim^-1/2
+  float embed_scale = 1.f;
+  std::vector<int> dense_dims;  // Gemma-style projection chain after pooling
+};
+
+struct TensorSrc {
+  const void* data = nullptr;
+  int64_t numel = 0;
+  std::vector<int64_t> shape;  // may be empty (numel only)
+  int bf16 = 0;                // 0 = f32, 1 = bf16
+};
+
+using TensorMap = std::map<std::string, TensorSrc>;
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  cudaError_t ensure(size_t n) {
+    if (n <= bytes) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  template <typename T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+struct LayerWeights {
+  void* wqkv = nullptr;  // [(hq + 2 hkv) d, H]
+  void* wo = nullptr;    // [H, hq d]
+  void* wgu = nullptr;   // [2 I, H] gate/up interleaved in gate_block rows
+  void* wd = nullptr;    // [H, I]
+  float* ln1 = nullptr;  // attention input norm
+  float* ln2 = nullptr;  // MLP input norm
+  float* ln1_post = nullptr;  // Gemma post-attention norm
+  float* ln2_post = nullptr;  // Gemma post-feedforward norm
+  float* qn = nullptr;
+  float* kn = nullptr;
+};
+
+struct ProfileRec {
+  cudaEvent_t start, stop;
+  double flops;
+  int kind;
+};
+
+}  // namespace inl
+
+struct inl_model {
+  inl::ModelConfig c;
+  int dtype = INL_DTYPE_BF16;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int* d_status = nullptr;
+  int* h_status = nullptr;  // pinned
+  int gate_block = 128;
+  std::vector<void*> allocs;
+  void* embed = nullptr;
+  float* final_norm = nullptr;
+  float* final_norm_b = nullptr;
+  float* emb_norm = nullptr;  // ModernBERT embedding LayerNorm
+  std::vector<inl::LayerWeights> layers;
+  // rope tables [max_pos, d/2] f32: global and local
+  float* cos0 = nullptr;
+  float* sin0 = nullptr;
+  float* cos1 = nullptr;
+  float* sin1 = nullptr;
+  // late Dense head
+  void* proj = nullptr;
+  float* proj_bias = nullptr;
+  int proj_out = 0;
+  // SPLADE / MLM head (ModernBERT)
+  void* head_dense = nullptr;
+  float* head_norm = nullptr;
+  float* decoder_bias = nullptr;
+  // Gemma-style dense chain (f32 or bf16 weights) after pooling
+  std::vector<void*> dense_chain;
+  // workspaces
+  inl::DevBuf h, xn, qkv, attn, ids, cu, pos, work, out, pooled, tmp;
+  int* h_stage = nullptr;  // pinned staging for cu + work list
+  size_t h_stage_bytes = 0;
+  // profiling / launch accounting
+  bool profiling = false;
+  std::vector<inl::ProfileRec> prof;
+  std::vector<cudaEvent_t> event_pool;
+  long long launches = 0;
+};

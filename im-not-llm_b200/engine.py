@@ -1,0 +1,268 @@
+"""Engine facades over libinl_cuda, mirroring the reference's engine API.
+
+* ``TextEmbedder`` — the DenseEngine contract (load / token_counts / embed /
+  unload / is_loaded; crates/inl-core/src/engine.rs:66-84) as
+  crates/inl-text/src/native.rs implements it: truncate to ``max_length``,
+  plan batches, one forward at a time behind a gate, each forward under a
+  ``BatchDeadline``, vectors returned in input order, count mismatch is an
+  error, Matryoshka ``output_dim`` only for EmbeddingGemma-style models.
+* ``LateEncoder`` — the LateEngine contract (crates/inl-late/src/lib.rs:38-55;
+  encode path crates/inl-late/src/native.rs:317-374,631-683): longest-first
+  planning, per-token vectors, non-finite output is an error.
+* ``DataParallelEmbedder`` — one model per GPU, one host thread per GPU,
+  packed batches assigned longest-processing-time first; no collective.
+
+Inputs are token-id lists: tokenization is the caller's (the reference's
+tokenizer front end is not part of this library).
+"""
+from __future__ import annotations
+
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Sequence
+
+import numpy as np
+
+from .errors import InlError
+from .model import CudaModel
+from .planner import assign_lpt, batch_cost, longest_first, pack, plan_packed
+
+DEFAULT_MAX_LENGTH = 2048          # crates/inl-text/src/native.rs:23
+DEFAULT_BATCH_SIZE = 64            # crates/inl-text/src/native.rs:26
+DEFAULT_TIMEOUT_SECONDS = 60       # crates/inl-text/src/native.rs:32
+DEFAULT_PACKED_TOKENS = 65536      # packed real tokens per forward on one B200
+MATRYOSHKA_DIMS = (128, 256, 512, 768)  # crates/inl-text/src/native.rs:82-88
+
+
+class BatchDeadline:
+    """Deadline for non-cancellable forward passes (crates/inl-core/src/deadline.rs:17-60).
+
+    ``run`` executes ``task`` on a worker thread and waits at most ``budget``
+    seconds; after one expiry the deadline is wedged and every later call fails
+    fast with a timeout error without running its task.
+    """
+
+    def __init__(self):
+        self._wedged = threading.Event()
+
+    def ensure_healthy(self, what: str) -> None:
+        if self._wedged.is_set():
+            raise InlError.timeout(
+                f"{what}: an earlier call timed out and its thread is still stuck; restart the process")
+
+    @property
+    def wedged(self) -> bool:
+        return self._wedged.is_set()
+
+    def run(self, what: str, budget: float, task: Callable[[], object]):
+        self.ensure_healthy(what)
+        box: dict = {}
+
+        def body():
+            try:
+                box["value"] = task()
+            except BaseException as e:  # surfaced to the caller below
+                box["error"] = e
+
+        t = threading.Thread(target=body, name=f"inl-forward:{what}", daemon=True)
+        t.start()
+        t.join(budget)
+        if t.is_alive():
+            self._wedged.set()
+            raise InlError.timeout(
+                f"{what} exceeded {budget:.3f}s; its thread cannot be cancelled — restart the process")
+        if "error" in box:
+            e = box["error"]
+            if isinstance(e, InlError):
+                raise e
+            raise InlError.inference(f"{what}: blocking task failed: {e}") from e
+        return box.get("value")
+
+
+@dataclass
+class EngineInfo:
+    """crates/inl-core/src/engine.rs:10-26."""
+    model_id: str
+    dimension: int
+    dtype: str
+    device: str
+    attention: str
+    max_length: int
+    modalities: list = field(default_factory=lambda: ["text"])
+
+
+@dataclass
+class TextOptions:
+    """Subset of TextOptions (crates/inl-text/src/native.rs:172-287) that the
+    packed GPU path uses."""
+    id: str = "synthetic"
+    batch_size: int = 4096               # texts per packed forward
+    max_batch_tokens: int = DEFAULT_PACKED_TOKENS
+    max_length: int = DEFAULT_MAX_LENGTH
+    timeout_seconds: float = DEFAULT_TIMEOUT_SECONDS
+    per_batch_timeout_seconds: float | None = None
+    output_dim: int | None = None
+
+    def batch_timeout(self) -> float:
+        """crates/inl-text/src/native.rs:739-752."""
+        s = self.per_batch_timeout_seconds if self.per_batch_timeout_seconds is not None else self.timeout_seconds
+        if not s or s <= 0:
+            raise InlError.config("timeout_seconds / per_batch_timeout_seconds must be greater than 0")
+        return float(s)
+
+
+def _truncate(tokens: Sequence[Sequence[int]], max_length: int) -> list[np.ndarray]:
+    return [np.asarray(t, dtype=np.uint32)[:max_length] for t in tokens]
+
+
+class _Loaded:
+    def __init__(self, model: CudaModel):
+        self.model = model
+        self.gate = threading.Lock()
+
+
+class _EngineBase:
+    def __init__(self, loader: Callable[[], CudaModel], options: TextOptions):
+        self._loader = loader
+        self.options = options
+        self.deadline = BatchDeadline()
+        self._load_lock = threading.Lock()
+        self._loaded: _Loaded | None = None
+
+    def _model(self) -> _Loaded:
+        with self._load_lock:  # concurrent callers share one load; failures are not cached
+            if self._loaded is None:
+                self._loaded = _Loaded(self._loader())
+            return self._loaded
+
+    def is_loaded(self) -> bool:
+        return self._loaded is not None
+
+    def unload(self) -> bool:
+        with self._load_lock:
+            if self._loaded is None:
+                return False
+            with self._loaded.gate:
+                self._loaded.model.close()
+            self._loaded = None
+            return True
+
+    def token_counts(self, tokens: Sequence[Sequence[int]]) -> list[int]:
+        return [len(t) for t in tokens]
+
+    def _run_batches(self, what: str, texts: list[np.ndarray], forward) -> list:
+        if not texts:
+            return []
+        self.deadline.ensure_healthy(what)
+        loaded = self._model()
+        budget = self.options.batch_timeout()
+        lengths = [len(t) for t in texts]
+        order = longest_first(lengths)
+        sorted_lengths = [lengths[i] for i in order]
+        results: list = [None] * len(texts)
+        for r in plan_packed(sorted_lengths, self.options.max_batch_tokens, self.options.batch_size):
+            members = [order[k] for k in r]
+            ids, cu = pack(texts, members)
+            with loaded.gate:  # queue before the deadline starts (crates/inl-text/src/native.rs:668)
+                out = self.deadline.run(f"{what} batch", budget, lambda: forward(loaded.model, ids, cu))
+            if len(out) != len(members):
+                raise InlError.inference(f"{what} returned {len(out)} results for {len(members)} inputs")
+            for i, v in zip(members, out):
+                results[i] = v
+        return results
+
+
+class TextEmbedder(_EngineBase):
+    """DenseEngine over a CudaModel (Qwen3 last-token or Gemma-style mean pooling)."""
+
+    def load(self) -> EngineInfo:
+        m = self._model().model
+        info = m.info()
+        dim = self.options.output_dim or info["dense_dim"]
+        return EngineInfo(self.options.id, dim, m.dtype, f"cuda:{m.device}", "fused", self.options.max_length)
+
+    def _output_dim(self, model: CudaModel) -> int:
+        """resolve_output_dim (crates/inl-text/src/native.rs:793-817)."""
+        dim = self.options.output_dim
+        if dim is None:
+            return 0
+        if model.info()["arch"] != 2:
+            raise InlError.config("output_dim is only supported for EmbeddingGemma 2 models")
+        if dim not in MATRYOSHKA_DIMS:
+            raise InlError.config(f"output_dim {dim} is not supported by EmbeddingGemma 2: use one of "
+                                  f"{list(MATRYOSHKA_DIMS)}")
+        if dim > model.info()["dense_dim"]:
+            raise InlError.config(f"output_dim {dim} exceeds the model's embeddings")
+        return dim
+
+    def embed(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
+        texts = _truncate(tokens, self.options.max_length)
+        if not texts:
+            return []
+        out_dim = self._output_dim(self._model().model)
+
+        def forward(model: CudaModel, ids, cu):
+            return list(model.embed(ids, cu, out_dim=out_dim))
+
+        return self._run_batches("native embedding", texts, forward)
+
+
+class LateEncoder(_EngineBase):
+    """LateEngine over a CudaModel with a Dense head attached."""
+
+    def load(self) -> EngineInfo:
+        m = self._model().model
+        return EngineInfo(self.options.id, m.info()["multivector_dim"], m.dtype, f"cuda:{m.device}", "fused",
+                          self.options.max_length)
+
+    def encode(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
+        texts = _truncate(tokens, self.options.max_length)
+
+        def forward(model: CudaModel, ids, cu):
+            flat = model.encode_multivector(ids, cu)
+            if not np.all(np.isfinite(flat)):  # crates/inl-late/src/native.rs:675-679
+                raise InlError.inference("native late encoder produced non-finite values")
+            return [flat[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
+
+        return self._run_batches("native late", texts, forward)
+
+
+class DataParallelEmbedder:
+    """Dense embedding over several GPUs: one CudaModel replica and one host
+    thread per device, batches assigned longest-processing-time first, no
+    collective; results gathered on the host by input index."""
+
+    def __init__(self, models: Sequence[CudaModel], max_batch_tokens: int = DEFAULT_PACKED_TOKENS):
+        self.models = list(models)
+        self.max_batch_tokens = max_batch_tokens
+
+    def embed(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
+        texts = [np.asarray(t, dtype=np.uint32) for t in tokens]
+        lengths = [len(t) for t in texts]
+        order = longest_first(lengths)
+        batches = [[order[k] for k in r] for r in plan_packed([lengths[i] for i in order], self.max_batch_tokens)]
+        causal = bool(self.models[0].info()["is_causal"]) if self.models else True
+        costs = [batch_cost([lengths[i] for i in b], causal) for b in batches]
+        plan = assign_lpt(costs, len(self.models))
+        results: list = [None] * len(texts)
+        errors: list = []
+
+        def worker(w: int):
+            try:
+                for b in plan[w]:
+                    ids, cu = pack(texts, batches[b])
+                    out = self.models[w].embed(ids, cu)
+                    for i, v in zip(batches[b], out):
+                        results[i] = v
+            except BaseException as e:
+                errors.append(e)
+
+        threads = [threading.Thread(target=worker, args=(w,)) for w in range(len(self.models))]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return results

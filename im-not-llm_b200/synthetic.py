@@ -1,0 +1,149 @@
+"""Seeded synthetic checkpoints and inputs for the five benchmark configurations.
+
+No network and no real checkpoints are available, so every configuration runs
+on random-init weights of the named architecture and seeded token ids:
+
+* weights: numpy PCG64 ``default_rng(seed)`` (seed 0), tensors drawn in the
+  order ``tensor_specs`` lists them; linear and embedding weights
+  N(0, 0.02) as float32 (``standard_normal(dtype=float32) * 0.02``); norm
+  weights 1.0 (``norm_jitter`` > 0 gives ``1 + norm_jitter * N(0,1)`` instead,
+  used by the small test models so a mis-applied norm weight shows);
+* inputs: ``default_rng(config seed)`` as each ``*_inputs`` function states.
+
+Tensor names follow the Hugging Face checkpoints the reference loads
+(crates/inl-text/src/qwen3/mod.rs:180-330), so the same dictionaries can be
+written to safetensors and read by both the library and the CPU oracle.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+# --------------------------------------------------------------------- configs
+# Config 1/3/5 tower: Qwen3-Embedding-0.6B architecture.
+QWEN3_0_6B = {
+    "model_type": "qwen3",
+    "hidden_size": 1024,
+    "intermediate_size": 3072,
+    "num_attention_heads": 16,
+    "num_key_value_heads": 8,
+    "head_dim": 128,
+    "num_hidden_layers": 28,
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1_000_000.0,
+    "vocab_size": 151669,
+    "hidden_act": "silu",
+    "attention_bias": False,
+    "max_position_embeddings": 32768,
+}
+
+# Small Qwen3-shaped models for fast kernel parity (same code paths).
+QWEN3_TINY = dict(QWEN3_0_6B, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=128, num_hidden_layers=2, vocab_size=1000,
+                  rope_theta=10_000.0, max_position_embeddings=4096)
+QWEN3_TINY_D64 = dict(QWEN3_TINY, hidden_size=192, num_attention_heads=6, num_key_value_heads=3, head_dim=64,
+                      intermediate_size=384)
+
+LATE_PROJ_OUT = 128
+
+
+@dataclass
+class Spec:
+    name: str
+    shape: tuple
+    kind: str  # "linear" | "norm"
+
+
+def qwen3_specs(cfg: dict) -> list[Spec]:
+    H, I = cfg["hidden_size"], cfg["intermediate_size"]
+    hq, hkv = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    d = cfg.get("head_dim") or H // hq
+    specs = [Spec("embed_tokens.weight", (cfg["vocab_size"], H), "linear")]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"layers.{i}."
+        specs += [
+            Spec(p + "self_attn.q_proj.weight", (hq * d, H), "linear"),
+            Spec(p + "self_attn.k_proj.weight", (hkv * d, H), "linear"),
+            Spec(p + "self_attn.v_proj.weight", (hkv * d, H), "linear"),
+            Spec(p + "self_attn.o_proj.weight", (H, hq * d), "linear"),
+            Spec(p + "self_attn.q_norm.weight", (d,), "norm"),
+            Spec(p + "self_attn.k_norm.weight", (d,), "norm"),
+            Spec(p + "mlp.gate_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.up_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.down_proj.weight", (H, I), "linear"),
+            Spec(p + "input_layernorm.weight", (H,), "norm"),
+            Spec(p + "post_attention_layernorm.weight", (H,), "norm"),
+        ]
+    specs.append(Spec("norm.weight", (H,), "norm"))
+    return specs
+
+
+def generate(specs: list[Spec], seed: int = 0, std: float = 0.02, norm_jitter: float = 0.0) -> dict:
+    """Draw every tensor of ``specs`` in order from one PCG64 stream."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for s in specs:
+        n = int(np.prod(s.shape))
+        if s.kind == "norm":
+            if norm_jitter > 0:
+                v = 1.0 + norm_jitter * rng.standard_normal(n, dtype=np.float32)
+            else:
+                v = np.ones(n, dtype=np.float32)
+        else:
+            v = rng.standard_normal(n, dtype=np.float32)
+            v *= np.float32(std)
+        out[s.name] = v.astype(np.float32, copy=False).reshape(s.shape)
+    return out
+
+
+def qwen3_weights(cfg: dict = QWEN3_0_6B, seed: int = 0, norm_jitter: float = 0.0) -> dict:
+    return generate(qwen3_specs(cfg), seed=seed, norm_jitter=norm_jitter)
+
+
+def late_projection(cfg: dict = QWEN3_0_6B, out: int = LATE_PROJ_OUT, seed: int = 0) -> np.ndarray:
+    """Dense 1024->128 ``linear.weight`` [out, H], drawn from ``default_rng(seed + 1000)``
+    so that it does not shift the tower's stream."""
+    rng = np.random.default_rng(seed + 1000)
+    w = rng.standard_normal(out * cfg["hidden_size"], dtype=np.float32) * np.float32(0.02)
+    return w.reshape(out, cfg["hidden_size"])
+
+
+# ---------------------------------------------------------------------- inputs
+def packed(lengths: np.ndarray, ids: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    cu = np.zeros(len(lengths) + 1, dtype=np.int32)
+    np.cumsum(lengths, out=cu[1:])
+    return np.ascontiguousarray(ids, dtype=np.uint32), cu
+
+
+def cfg1_inputs(vocab: int = QWEN3_0_6B["vocab_size"]):
+    """Config 1: 8 texts x 128 ids uniform in [0, vocab), default_rng(1).integers."""
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, vocab, size=(8, 128))
+    return packed(np.full(8, 128), ids.reshape(-1))
+
+
+def cfg3_inputs(vocab: int = QWEN3_0_6B["vocab_size"]):
+    """Config 3: 64 texts x 512 ids, default_rng(3).integers."""
+    rng = np.random.default_rng(3)
+    ids = rng.integers(0, vocab, size=(64, 512))
+    return packed(np.full(64, 512), ids.reshape(-1))
+
+
+def cfg5_corpus(n_texts: int = 65536, vocab: int = QWEN3_0_6B["vocab_size"], seed: int = 5):
+    """Config 5: lengths clip(round(exp(ln 256 + 0.6 N(0,1))), 8, 2048) then ids
+    uniform in [0, vocab), both from default_rng(5) in that order."""
+    rng = np.random.default_rng(seed)
+    z = rng.standard_normal(n_texts)
+    lengths = np.clip(np.rint(np.exp(math.log(256.0) + 0.6 * z)), 8, 2048).astype(np.int64)
+    ids = rng.integers(0, vocab, size=int(lengths.sum()), dtype=np.int64)
+    return lengths, ids.astype(np.uint32)
+
+
+def random_texts(n: int, lo: int, hi: int, vocab: int, seed: int):
+    """Ragged test inputs: lengths uniform in [lo, hi], ids uniform."""
+    rng = np.random.default_rng(seed)
+    lengths = rng.integers(lo, hi + 1, size=n)
+    ids = rng.integers(0, vocab, size=int(lengths.sum()))
+    return packed(lengths, ids)

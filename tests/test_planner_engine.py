@@ -1,0 +1,242 @@
+"""Host logic: batch planners (restating the reference's planner tests,
+crates/inl-text/src/native.rs:911-1108 and the sparse/late planners), the
+packed planner and LPT assignment, the BatchDeadline semantics
+(crates/inl-core/src/deadline.rs:71-130) and the engine facade contract
+(crates/inl-text/src/native.rs:1368-1547) on a fake model (no GPU)."""
+import threading
+import time
+
+import numpy as np
+import pytest
+
+import im_not_llm_b200 as inl
+from im_not_llm_b200 import planner as P
+
+
+def test_longest_first_is_stable():
+    assert P.longest_first([3, 5, 3, 9, 5]) == [3, 1, 4, 0, 2]
+
+
+def test_plan_batches_contiguous_cover_and_caps():
+    lengths = [10, 9, 9, 8, 3, 3, 2, 1, 1]
+    b = P.plan_batches(lengths, batch_size=3, max_batch_tokens=20)
+    flat = [i for r in b for i in r]
+    assert flat == list(range(len(lengths)))
+    for r in b:
+        assert len(r) <= 3
+        if len(r) > 1:
+            assert len(r) * max(lengths[i] for i in r) <= 20
+
+
+def test_single_oversized_input_forms_its_own_batch():
+    assert P.plan_batches([50, 1], batch_size=8, max_batch_tokens=10) == [range(0, 1), range(1, 2)]
+    assert P.plan_packed([50, 1], 10) == [range(0, 1), range(1, 2)]
+
+
+def test_empty_input_plans_no_batches():
+    assert P.plan_batches([], 4, 10) == []
+    assert P.plan_packed([], 10) == []
+    assert P.plan_dense_batches([], 4, 10, 1, 1, 10) == []
+
+
+def test_dense_planner_pads_to_longest_member():
+    # crates/inl-text/src/native.rs:1034-1051: budget checked against the padded longest member
+    b = P.plan_dense_batches([100, 1, 1, 1], batch_size=64, max_length=2048, per_row_bytes=64,
+                             budget_bytes=1 << 30, max_batch_tokens=300, slack=8)
+    assert b == [range(0, 2), range(2, 4)]
+
+
+def test_plan_packed_counts_real_tokens():
+    lengths = [1000, 600, 500, 300, 100, 50]
+    b = P.plan_packed(lengths, 1100)
+    assert [list(r) for r in b] == [[0], [1, 2], [3, 4, 5]]
+    for r in b:
+        assert sum(lengths[i] for i in r) <= 1100 or len(r) == 1
+
+
+def test_lpt_balances_and_covers():
+    costs = [10, 9, 8, 7, 6, 5, 4, 3, 2, 1]
+    plan = P.assign_lpt(costs, 3)
+    assert sorted(i for w in plan for i in w) == list(range(10))
+    loads = [sum(costs[i] for i in w) for w in plan]
+    assert max(loads) - min(loads) <= max(costs)
+
+
+def test_pack_roundtrip():
+    texts = [np.arange(n, dtype=np.uint32) + 10 * n for n in (3, 0, 5)]
+    ids, cu = P.pack(texts, [2, 0, 1])
+    assert cu.tolist() == [0, 5, 8, 8]
+    assert ids[:5].tolist() == texts[2].tolist() and ids[5:8].tolist() == texts[0].tolist()
+
+
+def test_cfg5_corpus_shape_and_determinism():
+    lengths, ids = inl.synthetic.cfg5_corpus(n_texts=4096)
+    assert lengths.min() >= 8 and lengths.max() <= 2048
+    assert 200 < np.median(lengths) < 320
+    assert len(ids) == lengths.sum() and ids.max() < inl.synthetic.QWEN3_0_6B["vocab_size"]
+    l2, i2 = inl.synthetic.cfg5_corpus(n_texts=4096)
+    assert np.array_equal(lengths, l2) and np.array_equal(ids, i2)
+
+
+def test_weights_are_seeded_and_named_like_the_checkpoint():
+    cfg = inl.synthetic.QWEN3_TINY
+    a = inl.synthetic.qwen3_weights(cfg, seed=0)
+    b = inl.synthetic.qwen3_weights(cfg, seed=0)
+    assert a.keys() == b.keys() and all(np.array_equal(a[k], b[k]) for k in a)
+    assert "layers.1.self_attn.q_norm.weight" in a and a["norm.weight"].tolist() == [1.0] * cfg["hidden_size"]
+    assert abs(float(a["layers.0.mlp.up_proj.weight"].std()) - 0.02) < 1e-3
+
+
+# ------------------------------------------------------------------ deadline
+def test_stuck_batch_returns_timeout_within_deadline_and_wedges():
+    d = inl.BatchDeadline()
+    ran = []
+    t0 = time.time()
+    with pytest.raises(inl.TimeoutError_):
+        d.run("batch", 0.2, lambda: time.sleep(3))
+    assert time.time() - t0 < 0.4
+    with pytest.raises(inl.TimeoutError_):
+        d.run("batch", 5, lambda: ran.append(1))
+    assert not ran  # later calls fail fast without running
+
+
+def test_healthy_batches_return_values_and_errors_propagate():
+    d = inl.BatchDeadline()
+    assert d.run("x", 1, lambda: 42) == 42
+    with pytest.raises(inl.InferenceError):
+        d.run("x", 1, lambda: 1 / 0)
+    with pytest.raises(inl.InvalidInputError):
+        d.run("x", 1, lambda: (_ for _ in ()).throw(inl.InvalidInputError("bad")))
+    assert not d.wedged
+
+
+# ------------------------------------------------------------------ facade
+class FakeModel:
+    """Stands in for CudaModel: embeds a text as [len, first id, 0...]."""
+
+    def __init__(self, delay=0.0, drop=False):
+        self.delay = delay
+        self.drop = drop
+        self.dtype = "bf16"
+        self.device = 0
+        self.calls = 0
+        self.closed = False
+
+    def info(self):
+        return {"dense_dim": 4, "arch": 0, "multivector_dim": 2, "is_causal": 1}
+
+    def embed(self, ids, cu, out_dim=0):
+        self.calls += 1
+        time.sleep(self.delay)
+        n = len(cu) - 1 - (1 if self.drop else 0)
+        out = np.zeros((n, 4), dtype=np.float32)
+        for i in range(n):
+            out[i, 0] = cu[i + 1] - cu[i]
+            out[i, 1] = ids[cu[i]] if cu[i + 1] > cu[i] else -1
+        return out
+
+    def close(self):
+        self.closed = True
+
+
+def _texts(n, seed=0):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, 100, size=int(rng.integers(1, 30))).astype(np.uint32) for _ in range(n)]
+
+
+def test_embedder_returns_vectors_in_input_order():
+    texts = _texts(50)
+    e = inl.TextEmbedder(lambda: FakeModel(), inl.TextOptions(max_batch_tokens=64, batch_size=7))
+    out = e.embed(texts)
+    for t, v in zip(texts, out):
+        assert v[0] == len(t) and v[1] == t[0]
+    assert e.embed([]) == []
+
+
+def test_truncation_to_max_length():
+    e = inl.TextEmbedder(lambda: FakeModel(), inl.TextOptions(max_length=5))
+    out = e.embed([np.arange(20, dtype=np.uint32)])
+    assert out[0][0] == 5
+
+
+def test_vector_count_mismatch_is_an_inference_error():
+    e = inl.TextEmbedder(lambda: FakeModel(drop=True), inl.TextOptions())
+    with pytest.raises(inl.InferenceError):
+        e.embed(_texts(3))
+
+
+def test_stuck_forward_times_out_and_later_calls_fail_fast():
+    model = FakeModel(delay=2.0)
+    e = inl.TextEmbedder(lambda: model, inl.TextOptions(per_batch_timeout_seconds=0.2))
+    with pytest.raises(inl.TimeoutError_):
+        e.embed(_texts(2))
+    calls = model.calls
+    with pytest.raises(inl.TimeoutError_):
+        e.embed(_texts(2))
+    assert model.calls == calls
+
+
+def test_waiting_for_the_gate_does_not_count_against_the_deadline():
+    model = FakeModel(delay=0.3)
+    e = inl.TextEmbedder(lambda: model, inl.TextOptions(per_batch_timeout_seconds=0.5))
+    errs = []
+
+    def call():
+        try:
+            e.embed(_texts(1))
+        except Exception as x:  # pragma: no cover - failure path
+            errs.append(x)
+
+    ts = [threading.Thread(target=call) for _ in range(3)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errs and model.calls == 3
+
+
+def test_zero_timeout_and_output_dim_are_validated():
+    with pytest.raises(inl.ConfigError):
+        inl.TextEmbedder(lambda: FakeModel(), inl.TextOptions(timeout_seconds=0)).embed(_texts(1))
+    with pytest.raises(inl.ConfigError):  # output_dim refused for Qwen3
+        inl.TextEmbedder(lambda: FakeModel(), inl.TextOptions(output_dim=128)).embed(_texts(1))
+
+
+def test_unload_releases_and_next_call_reloads():
+    made = []
+
+    def loader():
+        made.append(FakeModel())
+        return made[-1]
+
+    e = inl.TextEmbedder(loader, inl.TextOptions())
+    e.embed(_texts(2))
+    assert e.is_loaded() and e.unload() and made[0].closed and not e.is_loaded()
+    assert not e.unload()
+    e.embed(_texts(2))
+    assert len(made) == 2
+
+
+def test_failed_load_is_not_cached():
+    state = {"n": 0}
+
+    def loader():
+        state["n"] += 1
+        if state["n"] == 1:
+            raise inl.InferenceError("boom")
+        return FakeModel()
+
+    e = inl.TextEmbedder(loader, inl.TextOptions())
+    with pytest.raises(inl.InferenceError):
+        e.embed(_texts(1))
+    assert len(e.embed(_texts(1))) == 1
+
+
+def test_data_parallel_embedder_gathers_by_index():
+    models = [FakeModel(), FakeModel(), FakeModel()]
+    dp = inl.DataParallelEmbedder(models, max_batch_tokens=40)
+    texts = _texts(60, seed=3)
+    out = dp.embed(texts)
+    for t, v in zip(texts, out):
+        assert v[0] == len(t) and v[1] == t[0]
+    assert all(m.calls > 0 for m in models)
