@@ -183,7 +183,15 @@ def run_ours(args, world, rank, local):
     texts, batches, lengths = corpus_batches()
     mine = batches[rank::world]
     need = args.warmup + args.steps
-    sel = [mine[i % len(mine)] for i in range(need)]
+    # Timed steps: the rank's whole share when K covers it, else K batches
+    # spaced evenly over it (the share runs longest to shortest, so a prefix
+    # would over-weight the attention-heavy 2k-token texts). Warm-up batches
+    # come from the same spread.
+    if args.steps >= len(mine):
+        timed = [mine[i % len(mine)] for i in range(args.steps)]
+    else:
+        timed = [mine[int(i)] for i in np.linspace(0, len(mine) - 1, args.steps)]
+    sel = [timed[i % len(timed)] for i in range(args.warmup)] + timed
     packed = [inl.planner.pack(texts, b) for b in sel]
     # inputs resident in HBM for the device-timed leg
     dev_ids = [torch.from_numpy(p[0].view(np.int32)).cuda() for p in packed]
@@ -285,14 +293,79 @@ def run_ours(args, world, rank, local):
     model.close()
 
 
+KERNEL_CASES = {
+    # name: (M tokens, N, K, epilogue) — the four projections of one Qwen3-0.6B layer
+    "gemm_qkv": (32768, 4096, 1024, 0),
+    "gemm_o": (32768, 1024, 2048, 1),
+    "gemm_gateup": (32768, 6144, 1024, 2),
+    "gemm_down": (32768, 1024, 3072, 1),
+}
+
+
+def run_kernel_case(name: str, reps: int = 3):
+    """A single kernel on a small case (a few hundred MB on the device), for
+    ncu captures and quick timing: `python bench.py --case gemm_gateup`."""
+    import ctypes
+
+    import torch
+
+    from im_not_llm_b200 import _native as N
+
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if name.startswith("gemm"):
+        M, Nn, K, epi = KERNEL_CASES[name]
+        A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+        W = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
+        out = torch.empty(M, Nn // 2 if epi == 2 else Nn, device="cuda", dtype=torch.bfloat16)
+        resid = out if epi == 1 else None
+
+        def launch():
+            N.check(N.lib().inl_cuda_gemm_bf16(A.data_ptr(), K, W.data_ptr(), K, M, Nn, K, epi, 0, 128,
+                                               out.data_ptr(), out.stride(0),
+                                               None if resid is None else resid.data_ptr(), out.stride(0), 0, None,
+                                               s), name)
+        flops = 2.0 * M * Nn * K
+    elif name == "attention":
+        import numpy as np
+
+        lengths = [2048] * 4 + [512] * 8 + [256] * 16
+        cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+        T = int(cu[-1])
+        qkv = torch.randn(T, 4096, device="cuda").to(torch.bfloat16)
+        o = torch.empty(T, 2048, device="cuda", dtype=torch.bfloat16)
+
+        def launch():
+            N.check(N.lib().inl_cuda_attention(qkv.data_ptr(), qkv.data_ptr() + 2048 * 2, qkv.data_ptr() + 3072 * 2,
+                                               4096, 4096, 4096, o.data_ptr(), 2048, 1, 16, 8, 128, 128 ** -0.5, 1,
+                                               -1, cu.ctypes.data, len(lengths), s), name)
+        flops = sum(4.0 * 2048 * L * (L + 1) / 2 for L in lengths)
+    else:
+        raise SystemExit(f"unknown case {name}")
+    launch()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(reps):
+        launch()
+    en.record()
+    torch.cuda.synchronize()
+    ms = st.elapsed_time(en) / reps
+    print(json.dumps({"case": name, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention"], default=None,
+                    help="time one kernel on a small case instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.case:
+        run_kernel_case(args.case)
+        return
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))
     if args.impl == "reference":

@@ -30,7 +30,8 @@ EXPORTED = (
     "inl_cuda_forward_hidden", "inl_cuda_model_info", "inl_cuda_model_destroy", "inl_cuda_last_error",
     "inl_cuda_device_count", "inl_cuda_version", "inl_cuda_gemm_bf16", "inl_cuda_gemm_f32",
     "inl_cuda_attention", "inl_cuda_model_set_profiling", "inl_cuda_model_profile",
-    "inl_cuda_model_launch_count", "inl_cuda_model_stream",
+    "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
+    "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2",
 )
 
 
@@ -73,6 +74,15 @@ def _declare(lib: ctypes.CDLL) -> None:
         "inl_cuda_model_profile": (c_int, [c_void_p, c_int, P(c_int), P(c_double), P(c_double)]),
         "inl_cuda_model_launch_count": (ctypes.c_longlong, [c_void_p, c_int]),
         "inl_cuda_model_stream": (c_void_p, [c_void_p]),
+        "inl_cuda_embed_gather": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_float, c_void_p, c_int,
+                                          c_void_p, c_void_p]),
+        "inl_cuda_norm": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
+                                  c_int, c_i64, c_void_p]),
+        "inl_cuda_qk_norm_rope": (c_int, [c_void_p, c_int, c_i64, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                          c_int, c_float, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+        "inl_cuda_token_positions": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+        "inl_cuda_last_token_norm_l2": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_int, c_void_p, c_float, c_int,
+                                                c_void_p, c_void_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

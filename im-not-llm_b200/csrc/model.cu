@@ -219,7 +219,9 @@ struct Loader {
                                          std::to_string(static_cast<long long>(rows) * cols));
     const size_t bytes = static_cast<size_t>(s->numel) * (s->bf16 ? 2 : 4);
     INL_CUDA_TRY(staging.ensure(bytes), "staging allocation");
-    INL_CUDA_TRY(cudaMemcpy(staging.p, s->data, bytes, cudaMemcpyHostToDevice), "weight upload");
+    // Stream-ordered copy: a pageable cudaMemcpy may return before its DMA lands,
+    // and the model's non-blocking stream does not wait for the legacy stream.
+    INL_CUDA_TRY(cudaMemcpyAsync(staging.p, s->data, bytes, cudaMemcpyHostToDevice, m->stream), "weight upload");
     int r = s->bf16 ? inl::convert_bf16_rows(staging.as<__nv_bfloat16>(), rows, cols, dst, dst_bf16, ld_dst, blk,
                                              blk_stride, off, m->stream)
                     : inl::convert_rows(staging.as<float>(), rows, cols, dst, dst_bf16, ld_dst, blk, blk_stride, off,
@@ -241,7 +243,9 @@ struct Loader {
     if (!find(name)) {
       if (!optional) return fail(INL_ERR_INFERENCE, "missing weight " + prefix + name);
       std::vector<float> v(n, fill);
-      INL_CUDA_TRY(cudaMemcpy(*out, v.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "fill");
+      INL_CUDA_TRY(cudaMemcpyAsync(*out, v.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, m->stream),
+                   "fill");
+      INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "fill");
       return INL_OK;
     }
     return upload(name, 1, n, *out, 0, n, 1, 0, 0);
@@ -267,8 +271,9 @@ int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out) {
   m->allocs.push_back(dc);
   INL_CUDA_TRY(cudaMalloc(&ds, bytes), "rope table");
   m->allocs.push_back(ds);
-  INL_CUDA_TRY(cudaMemcpy(dc, c.data(), bytes, cudaMemcpyHostToDevice), "rope upload");
-  INL_CUDA_TRY(cudaMemcpy(ds, s.data(), bytes, cudaMemcpyHostToDevice), "rope upload");
+  INL_CUDA_TRY(cudaMemcpyAsync(dc, c.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
+  INL_CUDA_TRY(cudaMemcpyAsync(ds, s.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
+  INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "rope upload");
   *cos_out = static_cast<float*>(dc);
   *sin_out = static_cast<float*>(ds);
   return INL_OK;
@@ -944,6 +949,62 @@ int inl_cuda_gemm_f32(const float* A, int64_t lda, const float* W, int64_t ldw, 
   if (r == -1) return fail(INL_ERR_INVALID_INPUT, "gemm_f32: unsupported shape / epilogue");
   if (r != 0) return fail(INL_ERR_INFERENCE, "gemm_f32 launch failed");
   return INL_OK;
+}
+
+static int hook_status(int r, const char* what) {
+  if (r == -1) return fail(INL_ERR_INVALID_INPUT, std::string(what) + ": unsupported arguments");
+  if (r != 0) return fail(INL_ERR_INFERENCE, std::string(what) + " launch failed");
+  return INL_OK;
+}
+
+int inl_cuda_embed_gather(const uint32_t* ids, int T, const void* table, int table_dtype, int vocab, int H,
+                          float scale, void* out, int out_dtype, int* status, void* stream) {
+  return hook_status(inl::embed_gather(ids, T, table, table_dtype == INL_DTYPE_BF16, vocab, H, scale, out,
+                                       out_dtype == INL_DTYPE_BF16, status, static_cast<cudaStream_t>(stream)),
+                     "embed_gather");
+}
+
+int inl_cuda_norm(const void* x, int x_dtype, int64_t ldx, const float* w, const float* b, float eps, int layer_norm,
+                  int rows, int H, void* out, int out_dtype, int64_t ldo, void* stream) {
+  const int xb = x_dtype == INL_DTYPE_BF16, ob = out_dtype == INL_DTYPE_BF16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return hook_status(layer_norm ? inl::layer_norm(x, xb, ldx, w, b, eps, rows, H, out, ob, ldo, s)
+                                : inl::rms_norm(x, xb, ldx, w, eps, rows, H, out, ob, ldo, s),
+                     "norm");
+}
+
+int inl_cuda_qk_norm_rope(void* qkv, int dtype, int64_t ld, int T, int hq, int hkv, int d, const float* qw,
+                          const float* kw, int v_norm, float eps, const int32_t* pos, const float* cos,
+                          const float* sin, int max_pos, int* status, void* stream) {
+  inl::QkRopeArgs a;
+  a.qkv = qkv;
+  a.bf16 = dtype == INL_DTYPE_BF16;
+  a.ld = ld;
+  a.T = T;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.d = d;
+  a.qw = qw;
+  a.kw = kw;
+  a.v_norm = v_norm;
+  a.eps = eps;
+  a.pos = pos;
+  a.cos = cos;
+  a.sin = sin;
+  a.max_pos = max_pos;
+  a.status = status;
+  return hook_status(inl::qk_norm_rope(a, static_cast<cudaStream_t>(stream)), "qk_norm_rope");
+}
+
+int inl_cuda_token_positions(const int32_t* cu, int n, int T, int32_t* pos, void* stream) {
+  return hook_status(inl::token_positions(cu, n, T, pos, static_cast<cudaStream_t>(stream)), "token_positions");
+}
+
+int inl_cuda_last_token_norm_l2(const void* h, int h_dtype, int64_t ldh, const int32_t* cu, int n, const float* w,
+                                float eps, int H, float* out, void* stream) {
+  return hook_status(inl::last_token_norm_l2(h, h_dtype == INL_DTYPE_BF16, ldh, cu, n, w, eps, H, out,
+                                             static_cast<cudaStream_t>(stream)),
+                     "last_token_norm_l2");
 }
 
 int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq, int64_t ldk, int64_t ldv, void* out,

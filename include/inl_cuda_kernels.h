@@ -52,6 +52,37 @@ INL_API int inl_cuda_attention(const void* q, const void* k, const void* v, int6
                        int64_t ldo, int dtype, int hq, int hkv, int d, float scale, int causal, int window,
                        const int32_t* cu_seqlens_host, int n_texts, void* stream);
 
+/* Row gather table[ids[t]] * scale -> out [T, H]; dtypes INL_DTYPE_*. An id
+ * >= vocab writes zeros and sets *status. Replaces candle's Embedding::forward
+ * (index_select) at crates/inl-text/src/qwen3/mod.rs:352. */
+INL_API int inl_cuda_embed_gather(const uint32_t* ids, int T, const void* table, int table_dtype, int vocab, int H,
+                                  float scale, void* out, int out_dtype, int* status, void* stream);
+
+/* Row RMSNorm (layer_norm = 0): x / sqrt(mean x^2 + eps) * w, or LayerNorm
+ * (layer_norm = 1): (x - mean) / sqrt(var + eps) * w (+ b). w, b f32, may be
+ * NULL. Replaces candle_nn::ops::rms_norm (crates/inl-text/src/qwen3/mod.rs:86-90)
+ * and the reference LayerNorm (crates/inl-sparse/src/modernbert.rs:176-209). */
+INL_API int inl_cuda_norm(const void* x, int x_dtype, int64_t ldx, const float* w, const float* b, float eps,
+                          int layer_norm, int rows, int H, void* out, int out_dtype, int64_t ldo, void* stream);
+
+/* In place on packed q|k|v rows [T, ld]: per-head RMSNorm of q heads (qw) and
+ * k heads (kw) (NULL weight = no norm), weightless RMSNorm of v heads when
+ * v_norm, then half-split RoPE of q and k at position pos[t] (device int32)
+ * from tables cos/sin [max_pos, d/2] (device f32). Replaces q_norm/k_norm +
+ * candle_nn::rotary_emb::rope (crates/inl-text/src/qwen3/mod.rs:236-249). */
+INL_API int inl_cuda_qk_norm_rope(void* qkv, int dtype, int64_t ld, int T, int hq, int hkv, int d, const float* qw,
+                                  const float* kw, int v_norm, float eps, const int32_t* pos, const float* cos,
+                                  const float* sin, int max_pos, int* status, void* stream);
+
+/* pos[t] = t - cu[i] for the text i holding packed token t (cu device int32 [n+1]). */
+INL_API int inl_cuda_token_positions(const int32_t* cu, int n, int T, int32_t* pos, void* stream);
+
+/* Last-token head: out[i] = L2(RMSNorm(h[cu[i+1]-1]) * w) in f32 (cu device).
+ * Replaces forward_last's narrow + norm and the f32 L2 of
+ * crates/inl-text/src/qwen3/mod.rs:339-358,467-469. */
+INL_API int inl_cuda_last_token_norm_l2(const void* h, int h_dtype, int64_t ldh, const int32_t* cu, int n,
+                                        const float* w, float eps, int H, float* out, void* stream);
+
 /* Measurement hooks: with profiling on, every GEMM launch of the model is
  * bracketed by CUDA events on the model's stream. kind: 0 qkv, 1 o, 2 gate/up,
  * 3 down, 4 Dense head, -1 all. The reference has no counterpart (its
