@@ -31,8 +31,24 @@ EXPORTED = (
     "inl_cuda_device_count", "inl_cuda_version", "inl_cuda_gemm_bf16", "inl_cuda_gemm_f32",
     "inl_cuda_attention", "inl_cuda_model_set_profiling", "inl_cuda_model_profile",
     "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
-    "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2",
+    "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2", "inl_cuda_gemm_bf16_ex",
 )
+
+
+class GemmEx(ctypes.Structure):
+    """Mirror of inl_gemm_ex (include/inl_cuda_kernels.h)."""
+    _fields_ = [
+        ("A", ctypes.c_void_p), ("lda", ctypes.c_int64), ("W", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+        ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int),
+        ("epi", ctypes.c_int), ("act", ctypes.c_int), ("gate_block", ctypes.c_int),
+        ("out", ctypes.c_void_p), ("ldo", ctypes.c_int64), ("resid", ctypes.c_void_p), ("ldr", ctypes.c_int64),
+        ("ss_in", ctypes.c_void_p), ("ss_in_parts", ctypes.c_int), ("ss_dim", ctypes.c_int),
+        ("ss_eps", ctypes.c_float), ("ss_out", ctypes.c_void_p),
+        ("qn", ctypes.c_void_p), ("kn", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p), ("hq", ctypes.c_int), ("hkv", ctypes.c_int), ("d", ctypes.c_int),
+        ("max_pos", ctypes.c_int), ("qk_eps", ctypes.c_float), ("force_bn", ctypes.c_int),
+        ("status", ctypes.c_void_p),
+    ]
 
 
 class ModelInfo(ctypes.Structure):
@@ -74,6 +90,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "inl_cuda_model_profile": (c_int, [c_void_p, c_int, P(c_int), P(c_double), P(c_double)]),
         "inl_cuda_model_launch_count": (ctypes.c_longlong, [c_void_p, c_int]),
         "inl_cuda_model_stream": (c_void_p, [c_void_p]),
+        "inl_cuda_gemm_bf16_ex": (c_int, [P(GemmEx), c_void_p]),
         "inl_cuda_embed_gather": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_float, c_void_p, c_int,
                                           c_void_p, c_void_p]),
         "inl_cuda_norm": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,

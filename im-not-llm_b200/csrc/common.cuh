@@ -203,7 +203,21 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// Hardware approximations (MUFU): ex2.approx / rcp.approx, relative error ~2^-22.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// silu(x) = x * sigmoid(x); two MUFU operations per element.
+__device__ __forceinline__ float silu_f(float x) {
+  return x * rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f));
+}
 __device__ __forceinline__ float gelu_erf_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float c = 0.7978845608028654f;  // sqrt(2/pi)

@@ -60,29 +60,41 @@ __device__ __forceinline__ void st8<float>(float* p, const float (&v)[8]) {
 // ------------------------------------------------------------ embedding
 template <typename TT, typename TO>
 __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T, const TT* __restrict__ table,
-                                    int vocab, int H, float scale, TO* __restrict__ out, int* status) {
+                                    int vocab, int H, float scale, TO* __restrict__ out, float* __restrict__ ss_out,
+                                    int* status) {
   const int warps = blockDim.x >> 5;
   const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const uint32_t id = ids[row];
   TO* o = out + row * H;
-  if (id >= static_cast<uint32_t>(vocab)) {
-    if (lane == 0 && status) atomicCAS(status, 0, INL_DEV_BAD_INDEX);
-    for (int c = lane; c < H; c += 32) st_f<TO>(o, c, 0.f);
-    return;
-  }
-  const TT* src = table + static_cast<long long>(id) * H;
+  const bool bad = id >= static_cast<uint32_t>(vocab);
+  if (bad && lane == 0 && status) atomicCAS(status, 0, INL_DEV_BAD_INDEX);
+  const TT* src = table + static_cast<long long>(bad ? 0u : id) * H;
   if ((H & 7) == 0) {
-    for (int c = lane * 8; c < H; c += 256) {
-      float v[8];
-      ld8<TT>(src + c, v);
+    const int parts = (H + INL_SS_COLS - 1) / INL_SS_COLS;
+    for (int base = 0; base < H; base += 256) {
+      const int c = base + lane * 8;
+      float s = 0.f;
+      if (c < H) {
+        float v[8];
+        ld8<TT>(src + c, v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= scale;
-      st8<TO>(o + c, v);
+        for (int j = 0; j < 8; ++j) {
+          v[j] = bad ? 0.f : v[j] * scale;
+          const float r = sizeof(TO) == 2 ? bf16_round(v[j]) : v[j];
+          s = fmaf(r, r, s);
+        }
+        st8<TO>(o + c, v);
+      }
+      // 8 lanes x 8 values = one 64-column partial sum of squares
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (ss_out && (lane & 7) == 0 && c < H) ss_out[row * parts + c / INL_SS_COLS] = s;
     }
   } else {
-    for (int c = lane; c < H; c += 32) st_f<TO>(o, c, ld_f<TT>(src, c) * scale);
+    for (int c = lane; c < H; c += 32) st_f<TO>(o, c, bad ? 0.f : ld_f<TT>(src, c) * scale);
   }
 }
 
@@ -308,14 +320,16 @@ __global__ void truncate_normalize_kernel(const float* __restrict__ x, int n, in
 
 template <typename TS, typename TD>
 __global__ void convert_rows_kernel(const TS* __restrict__ src, int rows, int cols, TD* __restrict__ dst,
-                                    long long ld_dst, int blk, long long blk_stride, long long off) {
+                                    long long ld_dst, int blk, long long blk_stride, long long off,
+                                    const float* __restrict__ col_scale) {
   const long long total = static_cast<long long>(rows) * cols;
   for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int r = static_cast<int>(idx / cols);
     const int c = static_cast<int>(idx - static_cast<long long>(r) * cols);
     const long long dr = static_cast<long long>(r / blk) * blk_stride + off + (r % blk);
-    st_f<TD>(dst, dr * ld_dst + c, ld_f<TS>(src, idx));
+    const float v = ld_f<TS>(src, idx);
+    st_f<TD>(dst, dr * ld_dst + c, col_scale ? v * col_scale[c] : v);
   }
 }
 
@@ -328,21 +342,22 @@ inline int ok(cudaError_t e) { return e == cudaSuccess ? 0 : -3; }
 }  // namespace
 
 int embed_gather(const uint32_t* ids, int T, const void* table, int table_bf16, int vocab, int H, float scale,
-                 void* out, int out_bf16, int* status, cudaStream_t s) {
+                 void* out, int out_bf16, int* status, cudaStream_t s, float* ss_out) {
   if (T <= 0) return 0;
+  if (ss_out && (H % INL_SS_COLS) != 0) return -1;
   const int grid = rows_grid(T, 4);
   if (table_bf16 && out_bf16)
     embed_gather_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 128, 0, s>>>(
-        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), status);
+        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), ss_out, status);
   else if (table_bf16)
     embed_gather_kernel<__nv_bfloat16, float><<<grid, 128, 0, s>>>(
-        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<float*>(out), status);
+        ids, T, static_cast<const __nv_bfloat16*>(table), vocab, H, scale, static_cast<float*>(out), ss_out, status);
   else if (out_bf16)
     embed_gather_kernel<float, __nv_bfloat16><<<grid, 128, 0, s>>>(
-        ids, T, static_cast<const float*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), status);
+        ids, T, static_cast<const float*>(table), vocab, H, scale, static_cast<__nv_bfloat16*>(out), ss_out, status);
   else
     embed_gather_kernel<float, float><<<grid, 128, 0, s>>>(ids, T, static_cast<const float*>(table), vocab, H,
-                                                           scale, static_cast<float*>(out), status);
+                                                           scale, static_cast<float*>(out), ss_out, status);
   return ok(cudaGetLastError());
 }
 
@@ -438,30 +453,30 @@ int truncate_normalize(const float* x, int n, int D, int dim, float* out, cudaSt
 }
 
 int convert_rows(const float* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
-                 long long blk_stride, long long off, cudaStream_t s) {
+                 long long blk_stride, long long off, cudaStream_t s, const float* col_scale) {
   if (rows <= 0 || cols <= 0) return 0;
   const long long total = static_cast<long long>(rows) * cols;
   const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
   if (dst_bf16)
     convert_rows_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<__nv_bfloat16*>(dst),
-                                                                    ld_dst, blk, blk_stride, off);
+                                                                    ld_dst, blk, blk_stride, off, col_scale);
   else
     convert_rows_kernel<float, float><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<float*>(dst), ld_dst, blk,
-                                                           blk_stride, off);
+                                                           blk_stride, off, col_scale);
   return ok(cudaGetLastError());
 }
 
 int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst,
-                      int blk, long long blk_stride, long long off, cudaStream_t s) {
+                      int blk, long long blk_stride, long long off, cudaStream_t s, const float* col_scale) {
   if (rows <= 0 || cols <= 0) return 0;
   const long long total = static_cast<long long>(rows) * cols;
   const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
   if (dst_bf16)
     convert_rows_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(
-        src, rows, cols, static_cast<__nv_bfloat16*>(dst), ld_dst, blk, blk_stride, off);
+        src, rows, cols, static_cast<__nv_bfloat16*>(dst), ld_dst, blk, blk_stride, off, col_scale);
   else
     convert_rows_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<float*>(dst), ld_dst,
-                                                                   blk, blk_stride, off);
+                                                                   blk, blk_stride, off, col_scale);
   return ok(cudaGetLastError());
 }
 

@@ -28,7 +28,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half of the tile's columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct GemmCfg {
@@ -45,7 +46,19 @@ struct EpiArgs {
   long long ldo;
   const __nv_bfloat16* resid;
   long long ldr;
-  const float* row_scale;
+  const float* ss_in;
+  int ss_in_parts, ss_dim;
+  float ss_eps;
+  float* ss_out;
+  int ss_out_parts;
+  const float* qn;
+  const float* kn;
+  const int* pos;
+  const float* cos;
+  const float* sin;
+  int hq, hkv, d, max_pos;
+  float qk_eps;
+  int* status;
   int M, N;
 };
 
@@ -92,47 +105,139 @@ __device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* src, float 
   }
 }
 
+// Sum of squares of the bf16-rounded values (what the next GEMM reads back).
+__device__ __forceinline__ float ss_bf16_32(const float (&v)[32]) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float2 r = unpack_bf16x2(pack_bf16x2(v[j], v[j + 1]));
+    s = fmaf(r.x, r.x, s);
+    s = fmaf(r.y, r.y, s);
+  }
+  return s;
+}
+
+// One q or k head of width D in TMEM columns [c0, c0 + D) of this thread's row:
+// RMSNorm with weight w, then half-split RoPE at position p, stored at dst.
+template <int D>
+__device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const float* w, float eps, const float* cr,
+                                        const float* sr, bool row_ok, __nv_bfloat16* dst) {
+  uint32_t r[32], u[32];
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < D; c += 32) {
+    tmem_ld32(t_row + c0 + c, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x = __uint_as_float(r[j]) * rs;
+      ss = fmaf(x, x, ss);
+    }
+  }
+  const float inv = rsqrtf(ss / static_cast<float>(D) + eps) * rs;
+  constexpr int HALF = D / 2;
+#pragma unroll 1
+  for (int c = 0; c < HALF; c += 32) {
+    tmem_ld32(t_row + c0 + c, r);
+    tmem_ld32(t_row + c0 + HALF + c, u);
+    tmem_ld_wait();
+    if (!row_ok) continue;
+    float lo[32], hi[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x1 = __uint_as_float(r[j]) * inv * w[c + j];
+      const float x2 = __uint_as_float(u[j]) * inv * w[HALF + c + j];
+      const float cs = cr[c + j], sn = sr[c + j];
+      lo[j] = x1 * cs - x2 * sn;
+      hi[j] = x2 * cs + x1 * sn;
+    }
+    store_row32_bf16(dst + c, lo, 32);
+    store_row32_bf16(dst + HALF + c, hi, 32);
+  }
+}
+
+// Epilogue of one tile for one warp: TMEM lanes = tile rows (one per thread),
+// columns [half * BN/2, (half + 1) * BN/2) of the tile.
 template <int BN, int EPI, int ACT>
-__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, const EpiArgs& e) {
+__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, int half, const EpiArgs& e) {
+  constexpr int HW = BN / 2;
   const bool row_ok = row < e.M;
-  const float rs = (e.row_scale != nullptr && row_ok) ? e.row_scale[row] : 1.0f;
+  float rs = 1.0f;
+  if (e.ss_in != nullptr && row_ok) {
+    const float* sp = e.ss_in + static_cast<long long>(row) * e.ss_in_parts;
+    float t = 0.f;
+    for (int j = 0; j < e.ss_in_parts; ++j) t += sp[j];
+    rs = rsqrtf(t / static_cast<float>(e.ss_dim) + e.ss_eps);
+  }
   uint32_t r[32];
   float v[32];
   if constexpr (EPI == INL_EPI_GATED_BF16) {
-    // Columns [0, BN/2) of the tile are the gate half, [BN/2, BN) the up half
-    // (weights interleaved in BN/2-row blocks at load time). Output width N/2.
-    constexpr int H = BN / 2;
+    // Tile columns [0, BN/2) are gate, [BN/2, BN) up (weights interleaved in
+    // BN/2-row blocks at load time); this warp makes output columns
+    // [half * BN/4, (half + 1) * BN/4) of the tile's BN/2.
+    constexpr int Q = BN / 4;
     const int out_n = e.N / 2;
-    const int o0 = n0 / 2;
+    const int o0 = n0 / 2 + half * Q;
 #pragma unroll 1
-    for (int c = 0; c < H; c += 32) {
+    for (int c = 0; c < Q; c += 32) {
       uint32_t u[32];
-      tmem_ld32(t_row + c, r);
-      tmem_ld32(t_row + H + c, u);
+      tmem_ld32(t_row + half * Q + c, r);
+      tmem_ld32(t_row + HW + half * Q + c, u);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float g = bf16_round(__uint_as_float(r[j]) * rs);
-        const float up = bf16_round(__uint_as_float(u[j]) * rs);
-        v[j] = gate_act<ACT>(g) * up;
-      }
+      for (int j = 0; j < 32; ++j) v[j] = gate_act<ACT>(__uint_as_float(r[j]) * rs) * (__uint_as_float(u[j]) * rs);
       if (row_ok) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + o0 + c;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo + o0 + c;
         store_row32_bf16(dst, v, out_n - (o0 + c));
+      }
+    }
+  } else if constexpr (EPI == INL_EPI_QKV) {
+    // Heads of width d inside this warp's BN/2 columns; q heads first, then k, then v.
+    const int c_begin = n0 + half * HW;
+    int p = 0;
+    if (row_ok) {
+      p = e.pos[row];
+      if (p < 0 || p >= e.max_pos) {
+        if (e.status) atomicCAS(e.status, 0, INL_DEV_BAD_INDEX);
+        p = 0;
+      }
+    }
+    const int hd = e.d;
+    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo;
+#pragma unroll 1
+    for (int hc = 0; hc < HW; hc += hd) {
+      const int col = c_begin + hc;
+      if (col >= e.N) break;
+      const int head = col / hd;
+      if (head < e.hq + e.hkv) {
+        const float* w = head < e.hq ? e.qn : e.kn;
+        const float* cr = e.cos + static_cast<long long>(p) * (hd / 2);
+        const float* sr = e.sin + static_cast<long long>(p) * (hd / 2);
+        if (hd == 128) qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, cr, sr, row_ok, orow + col);
+        else qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, cr, sr, row_ok, orow + col);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < hd; c += 32) {
+          tmem_ld32(t_row + half * HW + hc + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
+          if (row_ok) store_row32_bf16(orow + col + c, v, 32);
+        }
       }
     }
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      tmem_ld32(t_row + c, r);
+    for (int c = 0; c < HW; c += 32) {
+      tmem_ld32(t_row + half * HW + c, r);
       tmem_ld_wait();
-      const int col = n0 + c;
+      const int col = n0 + half * HW + c;
       const int left = e.N - col;
       if (!row_ok || left <= 0) continue;  // loads above stay warp-uniform
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
       if constexpr (EPI == INL_EPI_F32) {
-        float* dst = reinterpret_cast<float*>(e.out) + (long long)row * e.ldo + col;
+        float* dst = reinterpret_cast<float*>(e.out) + static_cast<long long>(row) * e.ldo + col;
         if (left >= 32) {
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -143,11 +248,18 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, c
       } else {
         if constexpr (EPI == INL_EPI_RESID_BF16) {
           float rr[32];
-          load_row32_bf16(e.resid + (long long)row * e.ldr + col, rr, left);
+          load_row32_bf16(e.resid + static_cast<long long>(row) * e.ldr + col, rr, left);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]) + rr[j];
+          for (int j = 0; j < 32; ++j) v[j] += rr[j];
+          if (e.ss_out != nullptr) {
+            // two 32-column chunks per INL_SS_COLS partial: combine in registers
+            const float s = ss_bf16_32(v);
+            float* so = e.ss_out + static_cast<long long>(row) * e.ss_out_parts + col / INL_SS_COLS;
+            if ((c & 32) == 0) *so = s;
+            else *so += s;
+          }
         }
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + (long long)row * e.ldo + col;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo + col;
         store_row32_bf16(dst, v, left);
       }
     }
@@ -183,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * kEpiWarps);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -270,8 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5.
+    // Epilogue warps 2..9: lane quadrant warp % 4, column half (warp - 2) / 4.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -280,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = mb * kBM + quad * 32 + lane;
-      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, e);
+      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
@@ -384,14 +497,24 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     bn = g.gate_block * 2;
     if ((bn != 128 && bn != 256) || (g.N % bn) != 0) return -1;
   }
+  if (g.epi == INL_EPI_QKV) {
+    // Each epilogue warp owns 128 columns = whole heads of width 64 or 128.
+    bn = 256;
+    if ((g.d != 64 && g.d != 128) || (g.N % 256) != 0 || g.N != (g.hq + 2 * g.hkv) * g.d || !g.pos || !g.cos ||
+        !g.sin || g.max_pos <= 0)
+      return -1;
+  }
   if (g.force_bn == 128 || g.force_bn == 256) {
-    if (g.epi == INL_EPI_GATED_BF16 && g.force_bn != bn) return -1;
+    if ((g.epi == INL_EPI_GATED_BF16 || g.epi == INL_EPI_QKV) && g.force_bn != bn) return -1;
     bn = g.force_bn;
   }
+  if (g.ss_in && (g.ss_in_parts <= 0 || g.ss_dim <= 0)) return -1;
   CUtensorMap ta, tb;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, bn)) return -2;
-  EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.row_scale, g.M, g.N};
+  EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.ss_in, g.ss_in_parts, g.ss_dim, g.ss_eps, g.ss_out,
+            (g.N + INL_SS_COLS - 1) / INL_SS_COLS, g.qn, g.kn, g.pos, g.cos, g.sin, g.hq, g.hkv, g.d, g.max_pos,
+            g.qk_eps, g.status, g.M, g.N};
   cudaError_t err;
   if (bn == 256) {
     switch (g.epi) {
@@ -399,6 +522,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_QKV: err = launch_gemm<256, INL_EPI_QKV, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: return -1;
     }
   } else {

@@ -6,13 +6,20 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// Every bf16 epilogue first multiplies the accumulator by the row scale
+// r = rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps) when ss_in is given (the
+// RMSNorm of the A rows, folded: RMSNorm(x) W^T = r * (x (W diag(w))^T)).
 enum InlEpilogue : int {
-  INL_EPI_BF16 = 0,        // out = bf16(acc * row_scale)
-  INL_EPI_RESID_BF16 = 1,  // out = bf16(bf16(acc * row_scale) + resid)   (out may alias resid)
-  INL_EPI_GATED_BF16 = 2,  // out[:, n/2] = act(gate) * up, gate/up interleaved in gate_block-row blocks
-  INL_EPI_F32 = 3,         // out = acc * row_scale (f32)
-  INL_EPI_F32_ROWL2 = 4,   // out = v / max(|v|, 1e-12), v = acc (f32), needs N <= tile width (SIMT path only)
+  INL_EPI_BF16 = 0,        // out = bf16(r * acc)
+  INL_EPI_RESID_BF16 = 1,  // out = bf16(r * acc + resid) (out may alias resid); ss_out gets the
+                           // per-64-column sums of squares of the stored row
+  INL_EPI_GATED_BF16 = 2,  // out[:, n/2] = act(r * gate) * (r * up), gate/up interleaved in gate_block rows
+  INL_EPI_F32 = 3,         // out = r * acc (f32)
+  INL_EPI_QKV = 4,         // q|k|v heads: per-head RMSNorm of q/k (qn/kn) + half-split RoPE at pos[row]
 };
+
+// Columns per partial sum of squares written by the residual epilogue.
+constexpr int INL_SS_COLS = 64;
 
 enum InlAct : int { INL_ACT_SILU = 0, INL_ACT_GELU_ERF = 1, INL_ACT_GELU_TANH = 2 };
 
@@ -31,7 +38,21 @@ struct GemmArgs {
   long long ldo = 0;
   const __nv_bfloat16* resid = nullptr;
   long long ldr = 0;
-  const float* row_scale = nullptr;
+  // folded RMSNorm of the A rows: partial sums of squares [M, ss_in_parts]
+  const float* ss_in = nullptr;
+  int ss_in_parts = 0;
+  int ss_dim = 0;
+  float ss_eps = 0.f;
+  // residual epilogue: partial sums of squares of the output rows [M, ceil(N / INL_SS_COLS)]
+  float* ss_out = nullptr;
+  // QKV epilogue
+  const float* qn = nullptr;
+  const float* kn = nullptr;
+  const int* pos = nullptr;
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  int hq = 0, hkv = 0, d = 0, max_pos = 0;
+  float qk_eps = 1e-6f;
   int* status = nullptr;
   int max_ctas = 0;   // 0 = one CTA per SM
   int force_bn = 0;   // 0 = automatic tile width
@@ -61,8 +82,9 @@ int gemm_f32_tn(const GemmF32Args& g, cudaStream_t stream);
 
 // ---------------------------------------------------------------- elementwise
 // out[t, :] = table[ids[t], :] * scale ; ids >= vocab set *status = BAD_INDEX and write zeros.
+// ss_out (optional, needs H % INL_SS_COLS == 0): per-64-column sums of squares of the stored rows.
 int embed_gather(const uint32_t* ids, int T, const void* table, int table_bf16, int vocab, int H, float scale,
-                 void* out, int out_bf16, int* status, cudaStream_t s);
+                 void* out, int out_bf16, int* status, cudaStream_t s, float* ss_out = nullptr);
 
 // out = x / sqrt(mean(x^2) + eps) * w   (w f32, may be null)  rows x H
 int rms_norm(const void* x, int x_bf16, long long ldx, const float* w, float eps, int rows, int H, void* out,
@@ -111,11 +133,13 @@ int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n,
 // Truncate rows of [n, D] f32 to `dim` and renormalise (Matryoshka); out [n, dim].
 int truncate_normalize(const float* x, int n, int D, int dim, float* out, cudaStream_t s);
 
-// f32 -> bf16/f32 conversion with row remapping: dst_row(r) = (r / blk) * blk_stride + off + r % blk.
+// f32 -> bf16/f32 conversion with row remapping dst_row(r) = (r / blk) * blk_stride + off + r % blk
+// and an optional per-column scale (a folded norm weight).
 int convert_rows(const float* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
-                 long long blk_stride, long long off, cudaStream_t s);
+                 long long blk_stride, long long off, cudaStream_t s, const float* col_scale = nullptr);
 int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, int dst_bf16, long long ld_dst,
-                      int blk, long long blk_stride, long long off, cudaStream_t s);
+                      int blk, long long blk_stride, long long off, cudaStream_t s,
+                      const float* col_scale = nullptr);
 
 // ---------------------------------------------------------------- attention
 struct AttnArgs {

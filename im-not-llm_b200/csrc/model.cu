@@ -211,7 +211,7 @@ struct Loader {
 
   // Upload `name` ([rows, cols]) into dst rows remapped as (r / blk) * blk_stride + off + r % blk.
   int upload(const std::string& name, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
-             long long blk_stride, long long off) {
+             long long blk_stride, long long off, const float* col_scale = nullptr) {
     const TensorSrc* s = find(name);
     if (!s) return fail(INL_ERR_INFERENCE, "missing weight " + prefix + name);
     if (s->numel != static_cast<int64_t>(rows) * cols)
@@ -223,9 +223,9 @@ struct Loader {
     // and the model's non-blocking stream does not wait for the legacy stream.
     INL_CUDA_TRY(cudaMemcpyAsync(staging.p, s->data, bytes, cudaMemcpyHostToDevice, m->stream), "weight upload");
     int r = s->bf16 ? inl::convert_bf16_rows(staging.as<__nv_bfloat16>(), rows, cols, dst, dst_bf16, ld_dst, blk,
-                                             blk_stride, off, m->stream)
+                                             blk_stride, off, m->stream, col_scale)
                     : inl::convert_rows(staging.as<float>(), rows, cols, dst, dst_bf16, ld_dst, blk, blk_stride, off,
-                                        m->stream);
+                                        m->stream, col_scale);
     if (r != 0) return fail(INL_ERR_INFERENCE, "weight conversion launch failed");
     INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "weight conversion");
     return INL_OK;
@@ -287,6 +287,8 @@ int load_qwen3(inl_model* m, Loader& L) {
   const int gb = m->gate_block;
   if (c.I % gb != 0)
     return fail(INL_ERR_CONFIG, "intermediate_size must be a multiple of " + std::to_string(gb));
+  // Fused bf16 layer: folded input norms, q/k norm + RoPE in the QKV epilogue.
+  m->fused = bf && (c.d == 64 || c.d == 128) && c.H % INL_SS_COLS == 0 && qkv % 256 == 0;
   int r;
   if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
   m->layers.resize(c.layers);
@@ -299,18 +301,23 @@ int load_qwen3(inl_model* m, Loader& L) {
     w.wgu = L.alloc(static_cast<size_t>(2) * c.I * c.H * es);
     w.wd = L.alloc(static_cast<size_t>(c.H) * c.I * es);
     if (!w.wqkv || !w.wo || !w.wgu || !w.wd) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
-    if ((r = L.upload(p + "self_attn.q_proj.weight", q_out, c.H, w.wqkv, bf, c.H, q_out, 0, 0))) return r;
-    if ((r = L.upload(p + "self_attn.k_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out))) return r;
-    if ((r = L.upload(p + "self_attn.v_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out + kv_out)))
-      return r;
-    if ((r = L.upload(p + "self_attn.o_proj.weight", c.H, q_out, w.wo, bf, q_out, c.H, 0, 0))) return r;
-    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, 0))) return r;
-    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, gb))) return r;
-    if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
     if ((r = L.vec(p + "self_attn.q_norm.weight", c.d, &w.qn))) return r;
     if ((r = L.vec(p + "self_attn.k_norm.weight", c.d, &w.kn))) return r;
     if ((r = L.vec(p + "input_layernorm.weight", c.H, &w.ln1))) return r;
     if ((r = L.vec(p + "post_attention_layernorm.weight", c.H, &w.ln2))) return r;
+    // bf16: the input norms are folded into the projections that read them
+    // (RMSNorm(x) W^T = rsqrt(mean x^2 + eps) * x (W diag(w))^T); the row scale
+    // is applied in the GEMM epilogue from sums of squares the producer wrote.
+    const float* f1 = m->fused ? w.ln1 : nullptr;
+    const float* f2 = m->fused ? w.ln2 : nullptr;
+    if ((r = L.upload(p + "self_attn.q_proj.weight", q_out, c.H, w.wqkv, bf, c.H, q_out, 0, 0, f1))) return r;
+    if ((r = L.upload(p + "self_attn.k_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out, f1))) return r;
+    if ((r = L.upload(p + "self_attn.v_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out + kv_out, f1)))
+      return r;
+    if ((r = L.upload(p + "self_attn.o_proj.weight", c.H, q_out, w.wo, bf, q_out, c.H, 0, 0))) return r;
+    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, 0, f2))) return r;
+    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, gb, f2))) return r;
+    if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
   }
   if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
   if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;
@@ -420,6 +427,9 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->qkv.ensure(T * std::max(qkv_cols, act_cols) * e), "workspace");
   INL_CUDA_TRY(m->attn.ensure(T * static_cast<size_t>(c.hq) * c.d * e), "workspace");
   INL_CUDA_TRY(m->ids.ensure(T * 4), "workspace");
+  const size_t parts = static_cast<size_t>((c.H + INL_SS_COLS - 1) / INL_SS_COLS);
+  INL_CUDA_TRY(m->ss_a.ensure(T * parts * 4), "workspace");
+  INL_CUDA_TRY(m->ss_b.ensure(T * parts * 4), "workspace");
   INL_CUDA_TRY(m->pos.ensure(T * 4), "workspace");
   INL_CUDA_TRY(m->cu.ensure(static_cast<size_t>(b.n + 1) * 4), "workspace");
   INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
@@ -540,6 +550,143 @@ int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int
   return r;
 }
 
+// bf16 tcgen05 GEMM with every epilogue field (folded norm, QKV, residual sums).
+int gemm(inl_model* m, inl::GemmArgs g, int kind) {
+  ProfileRec rec{};
+  if (m->profiling) {
+    rec.start = take_event(m);
+    rec.stop = take_event(m);
+    rec.flops = 2.0 * g.M * g.N * g.K;
+    rec.kind = kind;
+    cudaEventRecord(rec.start, m->stream);
+  }
+  g.status = m->d_status;
+  g.gate_block = m->gate_block;
+  if (g.ldw == 0) g.ldw = g.K;
+  const int r = inl::gemm_bf16_tn(g, m->stream);
+  m->launches++;
+  if (m->profiling) {
+    cudaEventRecord(rec.stop, m->stream);
+    m->prof.push_back(rec);
+  }
+  return r;
+}
+
+// Fused bf16 layer stack: 4 GEMMs + attention per layer. The input RMSNorms
+// are folded (weights scaled by the norm weight at load, row scale from the
+// sums of squares the previous residual epilogue wrote); q/k RMSNorm + RoPE
+// run in the QKV epilogue.
+int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const int T = b.T;
+  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv_cols = q_out + 2 * kv_out;
+  const int parts = (c.H + INL_SS_COLS - 1) / INL_SS_COLS;
+  cudaStream_t s = m->stream;
+  INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, 1, c.V, c.H, 1.0f, m->h.p, 1, m->d_status, s,
+                              m->ss_a.as<float>()),
+            "embedding");
+  m->launches++;
+  const __nv_bfloat16* h = m->h.as<__nv_bfloat16>();
+  for (int l = 0; l < c.layers; ++l) {
+    const inl::LayerWeights& w = m->layers[l];
+    inl::GemmArgs g;
+    g.A = h;
+    g.lda = c.H;
+    g.W = static_cast<const __nv_bfloat16*>(w.wqkv);
+    g.M = T;
+    g.N = qkv_cols;
+    g.K = c.H;
+    g.epi = INL_EPI_QKV;
+    g.out = m->qkv.p;
+    g.ldo = qkv_cols;
+    g.ss_in = m->ss_a.as<float>();
+    g.ss_in_parts = parts;
+    g.ss_dim = c.H;
+    g.ss_eps = c.eps;
+    g.qn = w.qn;
+    g.kn = w.kn;
+    g.pos = m->pos.as<int>();
+    g.cos = m->cos0;
+    g.sin = m->sin0;
+    g.hq = c.hq;
+    g.hkv = c.hkv;
+    g.d = c.d;
+    g.max_pos = c.max_pos;
+    g.qk_eps = c.eps;
+    INL_K_TRY(gemm(m, g, 0), "qkv projection");
+
+    inl::AttnArgs aa;
+    aa.q = m->qkv.p;
+    aa.k = m->qkv.as<__nv_bfloat16>() + q_out;
+    aa.v = m->qkv.as<__nv_bfloat16>() + q_out + kv_out;
+    aa.ldq = aa.ldk = aa.ldv = qkv_cols;
+    aa.out = m->attn.p;
+    aa.ldo = q_out;
+    aa.bf16 = 1;
+    aa.hq = c.hq;
+    aa.hkv = c.hkv;
+    aa.d = c.d;
+    aa.scale = 1.0f / std::sqrt(static_cast<float>(c.d));
+    aa.causal = c.causal ? 1 : 0;
+    aa.window = -1;
+    aa.cu = m->cu.as<int>();
+    aa.n = b.n;
+    aa.work = m->work.as<int2>();
+    aa.n_work = n_work;
+    aa.q_block = inl::attention_q_block(1, c.d);
+    INL_K_TRY(inl::attention(aa, s), "attention");
+    m->launches++;
+
+    inl::GemmArgs o;
+    o.A = m->attn.as<__nv_bfloat16>();
+    o.lda = q_out;
+    o.W = static_cast<const __nv_bfloat16*>(w.wo);
+    o.M = T;
+    o.N = c.H;
+    o.K = q_out;
+    o.epi = INL_EPI_RESID_BF16;
+    o.out = m->h.p;
+    o.ldo = c.H;
+    o.resid = h;
+    o.ldr = c.H;
+    o.ss_out = m->ss_b.as<float>();
+    INL_K_TRY(gemm(m, o, 1), "o projection");
+
+    inl::GemmArgs gu;
+    gu.A = h;
+    gu.lda = c.H;
+    gu.W = static_cast<const __nv_bfloat16*>(w.wgu);
+    gu.M = T;
+    gu.N = 2 * c.I;
+    gu.K = c.H;
+    gu.epi = INL_EPI_GATED_BF16;
+    gu.act = INL_ACT_SILU;
+    gu.out = m->qkv.p;
+    gu.ldo = c.I;
+    gu.ss_in = m->ss_b.as<float>();
+    gu.ss_in_parts = parts;
+    gu.ss_dim = c.H;
+    gu.ss_eps = c.eps;
+    INL_K_TRY(gemm(m, gu, 2), "gate/up projection");
+
+    inl::GemmArgs dn;
+    dn.A = m->qkv.as<__nv_bfloat16>();
+    dn.lda = c.I;
+    dn.W = static_cast<const __nv_bfloat16*>(w.wd);
+    dn.M = T;
+    dn.N = c.H;
+    dn.K = c.I;
+    dn.epi = INL_EPI_RESID_BF16;
+    dn.out = m->h.p;
+    dn.ldo = c.H;
+    dn.resid = h;
+    dn.ldr = c.H;
+    dn.ss_out = m->ss_a.as<float>();
+    INL_K_TRY(gemm(m, dn, 3), "down projection");
+  }
+  return INL_OK;
+}
+
 // Embedding + every layer; leaves the last hidden state in m->h.
 int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
   const ModelConfig& c = m->c;
@@ -620,7 +767,7 @@ int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu,
     INL_CUDA_TRY(cudaMemcpyAsync(m->ids.p, ids, static_cast<size_t>(b.T) * 4, cudaMemcpyDeviceToDevice, m->stream),
                  "ids copy");
   switch (m->c.arch) {
-    case inl::ARCH_QWEN3: return qwen3_tower(m, b, n_work);
+    case inl::ARCH_QWEN3: return m->fused ? qwen3_tower_fused(m, b, n_work) : qwen3_tower(m, b, n_work);
     default: return fail(INL_ERR_CONFIG, "model_type not built");
   }
 }
@@ -830,7 +977,7 @@ void inl_cuda_model_destroy(inl_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (void* p : m->allocs) cudaFree(p);
   for (DevBuf* d : {&m->h, &m->xn, &m->qkv, &m->attn, &m->ids, &m->cu, &m->pos, &m->work, &m->out, &m->pooled,
-                    &m->tmp})
+                    &m->tmp, &m->ss_a, &m->ss_b})
     d->release();
   for (auto& r : m->prof) {
     cudaEventDestroy(r.start);
@@ -923,6 +1070,46 @@ int inl_cuda_gemm_bf16(const void* A, int64_t lda, const void* W, int64_t ldw, i
   g.ldr = ldr;
   g.status = status;
   g.force_bn = force_bn;
+  const int r = inl::gemm_bf16_tn(g, static_cast<cudaStream_t>(stream));
+  if (r == -1) return fail(INL_ERR_INVALID_INPUT, "gemm: unsupported shape / alignment / epilogue");
+  if (r != 0) return fail(INL_ERR_INFERENCE, std::string("gemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+  return INL_OK;
+}
+
+int inl_cuda_gemm_bf16_ex(const inl_gemm_ex* a, void* stream) {
+  if (!a) return fail(INL_ERR_CONFIG, "NULL args");
+  inl::GemmArgs g;
+  g.A = static_cast<const __nv_bfloat16*>(a->A);
+  g.lda = a->lda;
+  g.W = static_cast<const __nv_bfloat16*>(a->W);
+  g.ldw = a->ldw;
+  g.M = a->M;
+  g.N = a->N;
+  g.K = a->K;
+  g.epi = a->epi;
+  g.act = a->act;
+  g.gate_block = a->gate_block;
+  g.out = a->out;
+  g.ldo = a->ldo;
+  g.resid = static_cast<const __nv_bfloat16*>(a->resid);
+  g.ldr = a->ldr;
+  g.ss_in = a->ss_in;
+  g.ss_in_parts = a->ss_in_parts;
+  g.ss_dim = a->ss_dim;
+  g.ss_eps = a->ss_eps;
+  g.ss_out = a->ss_out;
+  g.qn = a->qn;
+  g.kn = a->kn;
+  g.pos = a->pos;
+  g.cos = a->cos;
+  g.sin = a->sin;
+  g.hq = a->hq;
+  g.hkv = a->hkv;
+  g.d = a->d;
+  g.max_pos = a->max_pos;
+  g.qk_eps = a->qk_eps;
+  g.force_bn = a->force_bn;
+  g.status = a->status;
   const int r = inl::gemm_bf16_tn(g, static_cast<cudaStream_t>(stream));
   if (r == -1) return fail(INL_ERR_INVALID_INPUT, "gemm: unsupported shape / alignment / epilogue");
   if (r != 0) return fail(INL_ERR_INFERENCE, std::string("gemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));

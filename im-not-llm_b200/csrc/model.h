@@ -124,6 +124,8 @@ struct inl_model {
   std::vector<void*> dense_chain;
   // workspaces
   inl::DevBuf h, xn, qkv, attn, ids, cu, pos, work, out, pooled, tmp;
+  inl::DevBuf ss_a, ss_b;  // per-64-column sums of squares of h (folded RMSNorm)
+  bool fused = false;      // bf16 fused layer (folded norms, QKV epilogue)
   int* h_stage = nullptr;  // pinned staging for cu + work list
   size_t h_stage_bytes = 0;
   // profiling / launch accounting

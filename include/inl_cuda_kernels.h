@@ -21,7 +21,7 @@ extern "C" {
 
 /* Epilogues of the GEMM entry points. */
 #define INL_GEMM_EPI_BF16 0       /* out = bf16(acc) */
-#define INL_GEMM_EPI_RESID 1      /* out = bf16(bf16(acc) + resid), out may alias resid */
+#define INL_GEMM_EPI_RESID 1      /* out = bf16(acc + resid), out may alias resid */
 #define INL_GEMM_EPI_GATED 2      /* out[:, n/2] = act(gate) * up, gate/up interleaved in gate_block rows */
 #define INL_GEMM_EPI_F32 3        /* out = acc (f32) */
 
@@ -38,6 +38,45 @@ extern "C" {
 INL_API int inl_cuda_gemm_bf16(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K, int epi, int act,
                        int gate_block, void* out, int64_t ldo, const void* resid, int64_t ldr, int force_bn,
                        int* status, void* stream);
+
+/* Every field of the fused GEMM epilogues (see INL_GEMM_EPI_*):
+ *  ss_in/ss_in_parts/ss_dim/ss_eps: folded RMSNorm of the A rows; the
+ *    accumulator is scaled by rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps);
+ *  ss_out: [M, ceil(N / 64)] sums of squares of the stored bf16 rows (RESID);
+ *  qn, kn, pos, cos, sin, hq, hkv, d, max_pos, qk_eps: the QKV epilogue
+ *    (per-head RMSNorm of q/k heads, half-split RoPE at pos[row]). */
+typedef struct inl_gemm_ex {
+  const void* A;
+  int64_t lda;
+  const void* W;
+  int64_t ldw;
+  int M, N, K;
+  int epi, act, gate_block;
+  void* out;
+  int64_t ldo;
+  const void* resid;
+  int64_t ldr;
+  const float* ss_in;
+  int ss_in_parts, ss_dim;
+  float ss_eps;
+  float* ss_out;
+  const float* qn;
+  const float* kn;
+  const int32_t* pos;
+  const float* cos;
+  const float* sin;
+  int hq, hkv, d, max_pos;
+  float qk_eps;
+  int force_bn;
+  int* status;
+} inl_gemm_ex;
+
+#define INL_GEMM_EPI_QKV 4
+
+/* The fused-epilogue GEMM of one encoder layer: replaces the candle sequence
+ * RMSNorm -> Linear (-> q/k RMSNorm -> rope) (-> residual add) of
+ * crates/inl-text/src/qwen3/mod.rs:227-297 with one launch. */
+INL_API int inl_cuda_gemm_bf16_ex(const inl_gemm_ex* args, void* stream);
 
 /* f32 SIMT version (epilogues INL_GEMM_EPI_F32, _RESID (f32 residual), _GATED
  * with gate_block 64). Replaces the f32 cuBLAS sgemm of the same call sites. */

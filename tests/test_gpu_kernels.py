@@ -82,7 +82,7 @@ def test_gemm_bf16_residual_in_place(gpu):
     A = torch.randn(700, 2048, device="cuda").to(torch.bfloat16)
     W = (torch.randn(1024, 2048, device="cuda") * 0.02).to(torch.bfloat16)
     h = torch.randn(700, 1024, device="cuda").to(torch.bfloat16)
-    ref = (A.float() @ W.float().T).to(torch.bfloat16).float() + h.float()
+    ref = (A.float() @ W.float().T) + h.float()
     N_ = _lib()
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     st = N_.lib().inl_cuda_gemm_bf16(A.data_ptr(), 2048, W.data_ptr(), 2048, 700, 1024, 2048, EPI_RESID, 0, 128,
@@ -194,3 +194,108 @@ def test_attention_varlen(gpu, dtype, d, hq, hkv, causal, window):
     ref = _attn_ref(torch, q, k, v, cu, hq, hkv, d, scale, causal, window)
     err = (out.double() - ref).abs().max().item()
     assert err < (2e-2 if dtype == "bf16" else 2e-5), err
+
+
+# ---------------------------------------------------------------- fused epilogues
+def _ex(torch, **kw):
+    N_ = _lib()
+    a = N_.GemmEx()
+    for k, v in kw.items():
+        if hasattr(v, "data_ptr"):
+            v = v.data_ptr()
+        setattr(a, k, v)
+    if not a.ldw:
+        a.ldw = a.K
+    N_.check(N_.lib().inl_cuda_gemm_bf16_ex(ctypes.byref(a), _stream(torch)), "gemm_ex")
+    torch.cuda.synchronize()
+
+
+def _row_scale(ss_parts, dim, eps):
+    return torch_rsqrt(ss_parts.double().sum(-1, keepdim=True) / dim + eps)
+
+
+def torch_rsqrt(x):
+    return 1.0 / x.sqrt()
+
+
+def test_gemm_residual_writes_row_sums_of_squares(gpu):
+    import torch
+
+    M, N, K = 777, 1024, 2048
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    h = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    ref = (A.float() @ W.float().T) + h.float()
+    ss = torch.full((M, N // 64), -1.0, device="cuda")
+    _ex(torch, A=A, lda=K, W=W, M=M, N=N, K=K, epi=EPI_RESID, out=h, ldo=N, resid=h, ldr=N, ss_out=ss)
+    err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 8e-3, err
+    ss_ref = (h.double() ** 2).view(M, N // 64, 64).sum(-1)
+    assert torch.allclose(ss.double(), ss_ref, rtol=1e-5, atol=1e-6)
+
+
+def test_gemm_gated_with_folded_norm(gpu):
+    import torch
+    import torch.nn.functional as F
+
+    M, K, I, gb = 300, 1024, 512, 128
+    x = (torch.randn(M, K, device="cuda") * 3).to(torch.bfloat16)
+    nw = torch.rand(K, device="cuda") + 0.5
+    gate = torch.randn(I, K, device="cuda") * 0.03
+    up = torch.randn(I, K, device="cuda") * 0.03
+    ss = (x.double() ** 2).view(M, K // 64, 64).sum(-1).float()
+    W = torch.empty(2 * I, K, device="cuda")
+    for b in range(I // gb):
+        W[2 * b * gb:(2 * b + 1) * gb] = gate[b * gb:(b + 1) * gb]
+        W[(2 * b + 1) * gb:(2 * b + 2) * gb] = up[b * gb:(b + 1) * gb]
+    Wf = (W * nw[None]).to(torch.bfloat16)  # norm weight folded into the columns
+    out = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
+    _ex(torch, A=x, lda=K, W=Wf, M=M, N=2 * I, K=K, epi=EPI_GATED, act=0, gate_block=gb, out=out, ldo=I,
+        ss_in=ss, ss_in_parts=K // 64, ss_dim=K, ss_eps=1e-6)
+    xn = x.double() / (x.double().pow(2).mean(-1, keepdim=True) + 1e-6).sqrt() * nw.double()
+    ref = F.silu(xn @ gate.double().T) * (xn @ up.double().T)
+    err = (out.double() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("d,hq,hkv", [(128, 16, 8), (64, 6, 3), (128, 4, 4)])
+def test_gemm_qkv_epilogue(gpu, d, hq, hkv):
+    import torch
+
+    M, K = 333, 1024
+    N = (hq + 2 * hkv) * d
+    x = (torch.randn(M, K, device="cuda") * 2).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda") * 0.03).to(torch.bfloat16)
+    qn = torch.rand(d, device="cuda") + 0.5
+    kn = torch.rand(d, device="cuda") + 0.5
+    ss = (x.double() ** 2).view(M, K // 64, 64).sum(-1).float()
+    max_pos = 1024
+    pos = torch.randint(0, max_pos, (M,), device="cuda", dtype=torch.int32)
+    half = d // 2
+    inv = 1.0 / (1e6 ** (torch.arange(half, dtype=torch.float64) * 2 / d))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
+    cos, sin = ang.cos().float().cuda(), ang.sin().float().cuda()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _ex(torch, A=x, lda=K, W=W, M=M, N=N, K=K, epi=4, out=out, ldo=N, ss_in=ss, ss_in_parts=K // 64, ss_dim=K,
+        ss_eps=1e-6, qn=qn, kn=kn, pos=pos, cos=cos, sin=sin, hq=hq, hkv=hkv, d=d, max_pos=max_pos, qk_eps=1e-6,
+        status=st)
+    assert st.item() == 0
+    r = 1.0 / (x.double().pow(2).mean(-1, keepdim=True) + 1e-6).sqrt()
+    y = (x.double() @ W.double().T) * r
+
+    def norm(t, w):
+        return t / (t.pow(2).mean(-1, keepdim=True) + 1e-6).sqrt() * w.double()
+
+    def rope(t):
+        c = cos.double()[pos.long()][:, None]
+        s_ = sin.double()[pos.long()][:, None]
+        return torch.cat([t[..., :half] * c - t[..., half:] * s_, t[..., half:] * c + t[..., :half] * s_], -1)
+
+    q = rope(norm(y[:, :hq * d].view(M, hq, d), qn)).reshape(M, -1)
+    k = rope(norm(y[:, hq * d:(hq + hkv) * d].view(M, hkv, d), kn)).reshape(M, -1)
+    v = y[:, (hq + hkv) * d:]
+    ref = torch.cat([q, k, v], -1)
+    for name, sl in (("q", slice(0, hq * d)), ("k", slice(hq * d, (hq + hkv) * d)), ("v", slice((hq + hkv) * d, N))):
+        err = (out[:, sl].double() - ref[:, sl]).abs().max().item() / ref[:, sl].abs().max().item()
+        assert err < 1e-2, (name, err)
