@@ -227,6 +227,7 @@ def run_ours(args, world, rank, local):
     ms = start.elapsed_time(stop)
     launches = model.launch_count()
     prof = model.profile(-1)
+    kinds = {name: model.profile(k) for k, name in enumerate(("qkv", "o", "gate_up", "down"))}
     model.set_profiling(False)
 
     # ---------------- end-to-end leg (e2e): pinned host ids -> host embeddings
@@ -278,7 +279,10 @@ def run_ours(args, world, rank, local):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} bf16 sustained", "traffic": None,
                          "gemm_launches": prof["launches"], "gemm_ms": prof["ms"],
-                         "gemm_share_of_step": prof["ms"] / ms if ms > 0 else None},
+                         "gemm_share_of_step": prof["ms"] / ms if ms > 0 else None,
+                         "by_projection": {k: {"ms_per_step": v["ms"] / args.steps,
+                                               "tflops": v["flops"] / (v["ms"] / 1000.0) / 1e12 if v["ms"] else 0.0}
+                                           for k, v in kinds.items()}},
             "e2e": {"value": tokens_all / (e2e_max / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "gpu_launches": launches,
@@ -312,7 +316,31 @@ def run_kernel_case(name: str, reps: int = 3):
     from im_not_llm_b200 import _native as N
 
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    if name.startswith("gemm"):
+    if name in ("gemm_qkv_fused", "gemm_gateup_fused"):
+        M, K = 32768, 1024
+        fused_qkv = name == "gemm_qkv_fused"
+        Nn = 4096 if fused_qkv else 6144
+        A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+        W = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
+        out = torch.empty(M, Nn if fused_qkv else Nn // 2, device="cuda", dtype=torch.bfloat16)
+        ss = torch.rand(M, K // 64, device="cuda") + 1.0
+        pos = (torch.arange(M, device="cuda", dtype=torch.int32) % 2048)  # packed texts: consecutive positions
+        cs = torch.rand(64, 2048, device="cuda")  # frequency-major [d/2, max_pos]
+        qn = torch.ones(128, device="cuda")
+        a = N.GemmEx()
+        a.A, a.lda, a.W, a.ldw, a.M, a.N, a.K = A.data_ptr(), K, W.data_ptr(), K, M, Nn, K
+        a.epi, a.act, a.gate_block = (4 if fused_qkv else 2), 0, 128
+        a.out, a.ldo = out.data_ptr(), out.stride(0)
+        a.ss_in, a.ss_in_parts, a.ss_dim, a.ss_eps = ss.data_ptr(), K // 64, K, 1e-6
+        if fused_qkv:
+            a.qn = a.kn = qn.data_ptr()
+            a.pos, a.cos, a.sin = pos.data_ptr(), cs.data_ptr(), cs.data_ptr()
+            a.hq, a.hkv, a.d, a.max_pos, a.qk_eps = 16, 8, 128, 2048, 1e-6
+
+        def launch():
+            N.check(N.lib().inl_cuda_gemm_bf16_ex(ctypes.byref(a), s), name)
+        flops = 2.0 * M * Nn * K
+    elif name.startswith("gemm"):
         M, Nn, K, epi = KERNEL_CASES[name]
         A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
         W = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
@@ -355,7 +383,8 @@ def run_kernel_case(name: str, reps: int = 3):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention"], default=None,
+    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention", "gemm_qkv_fused", "gemm_gateup_fused"],
+                    default=None,
                     help="time one kernel on a small case instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

@@ -377,11 +377,15 @@ int launch_f32(const AttnArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-int attention_q_block(int bf16, int /*d*/) { return bf16 ? kBM : kFQ; }
+int attention_q_block(int bf16, int d) {
+  if (bf16) return attention_tc_supported(d) ? 128 : kBM;
+  return kFQ;
+}
 
 int attention(const AttnArgs& a, cudaStream_t s) {
   if (a.n_work <= 0) return 0;
   if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv != 0) return -1;
+  if (a.bf16 && attention_tc_supported(a.d)) return attention_tc(a, a.total_rows, s);
   if (a.bf16) {
     if (a.q_block != kBM) return -1;
     switch (a.d) {

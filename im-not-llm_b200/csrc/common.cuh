@@ -98,6 +98,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Warp-uniform bounded wait: every lane polls, and the result is the AND over
+// the warp, so the warp-collective tcgen05.ld / tcgen05.st that follow are
+// always executed by all 32 lanes together (a divergent .sync.aligned tcgen05
+// instruction is undefined behaviour and can stall the warp for good).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
+  const bool ok = mbar_wait(bar, parity, status, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -167,13 +176,35 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B, f32 D, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+// Instruction descriptor for kind::f16 with bf16 A/B, f32 D; A K-major, B
+// K-major (b_mn_major = 0) or MN-major (1: N contiguous in shared memory).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int b_mn_major = 0) {
   return (1u << 4)                                   // D format f32
          | (1u << 7)                                 // A format bf16
          | (1u << 10)                                // B format bf16
+         | (static_cast<uint32_t>(b_mn_major) << 16) // B major
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+// Shared-memory descriptor of an MN-major operand in the 128-byte swizzle
+// layout of TMA boxes [rows = K, 64 elements of MN per 128-byte row]: 8-row
+// atoms at a 1024-byte stride (SBO) along K, successive 64-element MN blocks
+// `mn_block_bytes` apart (LBO).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t mn_block_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((mn_block_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (tensor core / TMA reads of the same bytes).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
@@ -190,6 +221,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 registers per thread -> 32 lanes x 32 consecutive TMEM columns.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+      "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float warp_sum(float v) {

@@ -119,9 +119,13 @@ __device__ __forceinline__ float ss_bf16_32(const float (&v)[32]) {
 
 // One q or k head of width D in TMEM columns [c0, c0 + D) of this thread's row:
 // RMSNorm with weight w, then half-split RoPE at position p, stored at dst.
+// cosT / sinT are [D/2, max_pos] (frequency-major), so the 32 threads of a
+// warp (consecutive tokens, mostly consecutive positions) read one line per
+// frequency instead of 32.
 template <int D>
-__device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const float* w, float eps, const float* cr,
-                                        const float* sr, bool row_ok, __nv_bfloat16* dst) {
+__device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const float* __restrict__ w, float eps,
+                                        const float* __restrict__ cosT, const float* __restrict__ sinT, int p,
+                                        int max_pos, bool row_ok, __nv_bfloat16* dst) {
   uint32_t r[32], u[32];
   float ss = 0.f;
 #pragma unroll 1
@@ -147,7 +151,8 @@ __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const 
     for (int j = 0; j < 32; ++j) {
       const float x1 = __uint_as_float(r[j]) * inv * w[c + j];
       const float x2 = __uint_as_float(u[j]) * inv * w[HALF + c + j];
-      const float cs = cr[c + j], sn = sr[c + j];
+      const long long ti = static_cast<long long>(c + j) * max_pos + p;
+      const float cs = cosT[ti], sn = sinT[ti];
       lo[j] = x1 * cs - x2 * sn;
       hi[j] = x2 * cs + x1 * sn;
     }
@@ -166,7 +171,14 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
   if (e.ss_in != nullptr && row_ok) {
     const float* sp = e.ss_in + static_cast<long long>(row) * e.ss_in_parts;
     float t = 0.f;
-    for (int j = 0; j < e.ss_in_parts; ++j) t += sp[j];
+    if ((e.ss_in_parts & 3) == 0) {
+      for (int j = 0; j < e.ss_in_parts; j += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(sp + j);
+        t += (v4.x + v4.y) + (v4.z + v4.w);
+      }
+    } else {
+      for (int j = 0; j < e.ss_in_parts; ++j) t += sp[j];
+    }
     rs = rsqrtf(t / static_cast<float>(e.ss_dim) + e.ss_eps);
   }
   uint32_t r[32];
@@ -211,10 +223,10 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       const int head = col / hd;
       if (head < e.hq + e.hkv) {
         const float* w = head < e.hq ? e.qn : e.kn;
-        const float* cr = e.cos + static_cast<long long>(p) * (hd / 2);
-        const float* sr = e.sin + static_cast<long long>(p) * (hd / 2);
-        if (hd == 128) qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, cr, sr, row_ok, orow + col);
-        else qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, cr, sr, row_ok, orow + col);
+        if (hd == 128)
+          qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, e.cos, e.sin, p, e.max_pos, row_ok, orow + col);
+        else
+          qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, e.cos, e.sin, p, e.max_pos, row_ok, orow + col);
       } else {
 #pragma unroll 1
         for (int c = 0; c < hd; c += 32) {
@@ -389,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
-      if (!mbar_wait(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = mb * kBM + quad * 32 + lane;
@@ -428,19 +440,9 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] bf16 with row stride `ld` elements; box = [box_rows, 64].
 bool make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
                      int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  return make_tma_2d_bf16(map, base, rows, cols, ld, box_rows, kBK);
 }
 
 int num_sms() {
@@ -484,6 +486,24 @@ cudaError_t dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, 
 }
 
 }  // namespace
+
+// Row-major [rows, cols] bf16 with row stride `ld` elements; box [box_rows, box_cols]
+// (box_cols * 2 = 128 bytes for the 128-byte swizzle), out-of-range reads fill zeros.
+bool make_tma_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                      int box_rows, int box_cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms_cached() { return num_sms(); }
 
 int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0) return 0;

@@ -2,6 +2,7 @@
 // libinl_cuda.so; the public C ABI is include/inl_cuda.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -45,7 +46,7 @@ struct GemmArgs {
   float ss_eps = 0.f;
   // residual epilogue: partial sums of squares of the output rows [M, ceil(N / INL_SS_COLS)]
   float* ss_out = nullptr;
-  // QKV epilogue
+  // QKV epilogue; cos / sin are FREQUENCY-MAJOR tables [d/2, max_pos]
   const float* qn = nullptr;
   const float* kn = nullptr;
   const int* pos = nullptr;
@@ -60,6 +61,11 @@ struct GemmArgs {
 
 // tcgen05 bf16 GEMM; returns 0 on success, <0 on bad arguments / launch error.
 int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream);
+
+// 2D TMA descriptor of a row-major bf16 matrix, 128-byte swizzle, box [box_rows, box_cols].
+bool make_tma_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                      int box_rows, int box_cols);
+int num_sms_cached();
 
 struct GemmF32Args {
   const float* A = nullptr;
@@ -159,8 +165,14 @@ struct AttnArgs {
   const int2* work = nullptr;  // device [n_work] = (text, q_block)
   int n_work = 0;
   int q_block = 64;
+  long long total_rows = 0;    // rows of q/k/v (packed tokens), bounds the TMA maps
+  int* status = nullptr;
 };
 int attention(const AttnArgs& a, cudaStream_t s);
+
+// tcgen05 flash attention (bf16, head_dim 64 / 128, 128-query work items).
+bool attention_tc_supported(int d);
+int attention_tc(const AttnArgs& a, long long total_rows, cudaStream_t s);
 
 // Number of query rows per work item the attention kernels expect.
 int attention_q_block(int bf16, int d);

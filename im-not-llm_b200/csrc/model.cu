@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -252,7 +253,8 @@ struct Loader {
   }
 };
 
-int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out) {
+int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, float** cosT_out = nullptr,
+               float** sinT_out = nullptr) {
   const int half = m->c.d / 2;
   const int P = m->c.max_pos;
   std::vector<float> c(static_cast<size_t>(P) * half), s(static_cast<size_t>(P) * half);
@@ -276,6 +278,25 @@ int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out) {
   INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "rope upload");
   *cos_out = static_cast<float*>(dc);
   *sin_out = static_cast<float*>(ds);
+  if (cosT_out && sinT_out) {
+    // frequency-major copies [half, P] for the GEMM epilogue
+    std::vector<float> ct(c.size()), st(s.size());
+    for (int p = 0; p < P; ++p)
+      for (int i = 0; i < half; ++i) {
+        ct[static_cast<size_t>(i) * P + p] = c[static_cast<size_t>(p) * half + i];
+        st[static_cast<size_t>(i) * P + p] = s[static_cast<size_t>(p) * half + i];
+      }
+    void *dct = nullptr, *dst = nullptr;
+    INL_CUDA_TRY(cudaMalloc(&dct, bytes), "rope table");
+    m->allocs.push_back(dct);
+    INL_CUDA_TRY(cudaMalloc(&dst, bytes), "rope table");
+    m->allocs.push_back(dst);
+    INL_CUDA_TRY(cudaMemcpyAsync(dct, ct.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
+    INL_CUDA_TRY(cudaMemcpyAsync(dst, st.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
+    INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "rope upload");
+    *cosT_out = static_cast<float*>(dct);
+    *sinT_out = static_cast<float*>(dst);
+  }
   return INL_OK;
 }
 
@@ -320,7 +341,7 @@ int load_qwen3(inl_model* m, Loader& L) {
     if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
   }
   if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
-  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0, &m->cos0T, &m->sin0T))) return r;
   return INL_OK;
 }
 
@@ -435,11 +456,15 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
   const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work) * 8 + 64;
   if (stage > m->h_stage_bytes) {
-    if (m->h_stage) cudaFreeHost(m->h_stage);
+    const size_t want = std::max({stage * 2, m->h_stage_bytes * 2, size_t(1) << 20});
+    if (m->h_stage) {
+      cudaStreamSynchronize(m->stream);  // the previous forward's copies may still read it
+      cudaFreeHost(m->h_stage);
+    }
     m->h_stage = nullptr;
     m->h_stage_bytes = 0;
-    INL_CUDA_TRY(cudaMallocHost(&m->h_stage, stage * 2), "pinned staging");
-    m->h_stage_bytes = stage * 2;
+    INL_CUDA_TRY(cudaMallocHost(&m->h_stage, want), "pinned staging");
+    m->h_stage_bytes = want;
   }
   return INL_OK;
 }
@@ -606,8 +631,8 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
     g.qn = w.qn;
     g.kn = w.kn;
     g.pos = m->pos.as<int>();
-    g.cos = m->cos0;
-    g.sin = m->sin0;
+    g.cos = m->cos0T;
+    g.sin = m->sin0T;
     g.hq = c.hq;
     g.hkv = c.hkv;
     g.d = c.d;
@@ -634,6 +659,8 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
     aa.work = m->work.as<int2>();
     aa.n_work = n_work;
     aa.q_block = inl::attention_q_block(1, c.d);
+    aa.total_rows = T;
+    aa.status = m->d_status;
     INL_K_TRY(inl::attention(aa, s), "attention");
     m->launches++;
 
@@ -741,6 +768,8 @@ int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
     aa.work = m->work.as<int2>();
     aa.n_work = n_work;
     aa.q_block = inl::attention_q_block(bf, c.d);
+    aa.total_rows = T;
+    aa.status = m->d_status;
     INL_K_TRY(inl::attention(aa, s), "attention");
     m->launches++;
     INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, c.H, q_out, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 1),
@@ -1206,10 +1235,15 @@ int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq,
     if (L < 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
     for (int b = 0; b * qb < L; ++b) work.push_back(make_int2(i, b));
   }
-  int* dcu = nullptr;
-  int2* dwork = nullptr;
-  INL_CUDA_TRY(cudaMalloc(&dcu, static_cast<size_t>(n_texts + 1) * 4), "alloc");
-  INL_CUDA_TRY(cudaMalloc(&dwork, std::max<size_t>(work.size(), 1) * 8), "alloc");
+  // Hook scratch (device cu + work list), cached across calls so a timing
+  // loop measures the kernel, not allocations; calls are serialised.
+  static std::mutex hook_mu;
+  static DevBuf hook_cu, hook_work;
+  std::lock_guard<std::mutex> lock(hook_mu);
+  INL_CUDA_TRY(hook_cu.ensure(static_cast<size_t>(n_texts + 1) * 4), "alloc");
+  INL_CUDA_TRY(hook_work.ensure(std::max<size_t>(work.size(), 1) * 8), "alloc");
+  int* dcu = hook_cu.as<int>();
+  int2* dwork = hook_work.as<int2>();
   cudaMemcpyAsync(dcu, cu_seqlens_host, static_cast<size_t>(n_texts + 1) * 4, cudaMemcpyHostToDevice, s);
   if (!work.empty()) cudaMemcpyAsync(dwork, work.data(), work.size() * 8, cudaMemcpyHostToDevice, s);
   inl::AttnArgs a;
@@ -1233,10 +1267,9 @@ int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq,
   a.work = dwork;
   a.n_work = static_cast<int>(work.size());
   a.q_block = qb;
+  a.total_rows = cu_seqlens_host[n_texts];
   const int r = inl::attention(a, s);
-  cudaStreamSynchronize(s);
-  cudaFree(dcu);
-  cudaFree(dwork);
+  cudaStreamSynchronize(s);  // the host work list must outlive the copy
   if (r == -1) return fail(INL_ERR_INVALID_INPUT, "attention: unsupported head_dim / heads");
   if (r != 0) return fail(INL_ERR_INFERENCE, "attention launch failed");
   return INL_OK;

@@ -54,13 +54,23 @@ using TensorMap = std::map<std::string, TensorSrc>;
 struct DevBuf {
   void* p = nullptr;
   size_t bytes = 0;
+  // Grow-only, geometric (x2, at least 1 MiB) so that a stream of batches of
+  // varying size reallocates O(log) times, never inside steady-state runs.
   cudaError_t ensure(size_t n) {
     if (n <= bytes) return cudaSuccess;
+    size_t want = n;
+    if (want < 2 * bytes) want = 2 * bytes;
+    if (want < (size_t(1) << 20)) want = size_t(1) << 20;
     if (p) cudaFree(p);
     p = nullptr;
     bytes = 0;
-    cudaError_t e = cudaMalloc(&p, n);
-    if (e == cudaSuccess) bytes = n;
+    cudaError_t e = cudaMalloc(&p, want);
+    if (e != cudaSuccess) {
+      e = cudaMalloc(&p, n);  // no headroom available: exact size
+      if (e != cudaSuccess) return e;
+      want = n;
+    }
+    bytes = want;
     return e;
   }
   void release() {
@@ -112,6 +122,8 @@ struct inl_model {
   float* sin0 = nullptr;
   float* cos1 = nullptr;
   float* sin1 = nullptr;
+  float* cos0T = nullptr;  // frequency-major [d/2, max_pos] copies for the QKV epilogue
+  float* sin0T = nullptr;
   // late Dense head
   void* proj = nullptr;
   float* proj_bias = nullptr;

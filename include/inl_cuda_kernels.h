@@ -44,7 +44,8 @@ INL_API int inl_cuda_gemm_bf16(const void* A, int64_t lda, const void* W, int64_
  *    accumulator is scaled by rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps);
  *  ss_out: [M, ceil(N / 64)] sums of squares of the stored bf16 rows (RESID);
  *  qn, kn, pos, cos, sin, hq, hkv, d, max_pos, qk_eps: the QKV epilogue
- *    (per-head RMSNorm of q/k heads, half-split RoPE at pos[row]). */
+ *    (per-head RMSNorm of q/k heads, half-split RoPE at pos[row]); cos / sin
+ *    are frequency-major tables [d/2, max_pos]. */
 typedef struct inl_gemm_ex {
   const void* A;
   int64_t lda;

@@ -275,10 +275,11 @@ def test_gemm_qkv_epilogue(gpu, d, hq, hkv):
     inv = 1.0 / (1e6 ** (torch.arange(half, dtype=torch.float64) * 2 / d))
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
     cos, sin = ang.cos().float().cuda(), ang.sin().float().cuda()
+    cosT, sinT = cos.t().contiguous(), sin.t().contiguous()  # frequency-major for the epilogue
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     _ex(torch, A=x, lda=K, W=W, M=M, N=N, K=K, epi=4, out=out, ldo=N, ss_in=ss, ss_in_parts=K // 64, ss_dim=K,
-        ss_eps=1e-6, qn=qn, kn=kn, pos=pos, cos=cos, sin=sin, hq=hq, hkv=hkv, d=d, max_pos=max_pos, qk_eps=1e-6,
+        ss_eps=1e-6, qn=qn, kn=kn, pos=pos, cos=cosT, sin=sinT, hq=hq, hkv=hkv, d=d, max_pos=max_pos, qk_eps=1e-6,
         status=st)
     assert st.item() == 0
     r = 1.0 / (x.double().pow(2).mean(-1, keepdim=True) + 1e-6).sqrt()
@@ -299,3 +300,29 @@ def test_gemm_qkv_epilogue(gpu, d, hq, hkv):
     for name, sl in (("q", slice(0, hq * d)), ("k", slice(hq * d, (hq + hkv) * d)), ("v", slice((hq + hkv) * d, N))):
         err = (out[:, sl].double() - ref[:, sl]).abs().max().item() / ref[:, sl].abs().max().item()
         assert err < 1e-2, (name, err)
+
+
+@pytest.mark.parametrize("causal,window", [(1, -1), (0, -1), (0, 300)])
+def test_attention_long_texts(gpu, causal, window):
+    """Several 128-key blocks per query tile, GQA 16/8, head_dim 128 (the
+    Qwen3-0.6B shape), texts up to 2048 tokens."""
+    import torch
+
+    N_ = _lib()
+    lengths = [2048, 1537, 129, 5]
+    cu = np.zeros(len(lengths) + 1, dtype=np.int32)
+    np.cumsum(lengths, out=cu[1:])
+    T, hq, hkv, d = int(cu[-1]), 16, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", generator=g).to(torch.bfloat16)
+    q, k, v = qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:]
+    out = torch.full((T, hq * d), float("nan"), device="cuda", dtype=torch.bfloat16)
+    ld = (hq + 2 * hkv) * d
+    st = N_.lib().inl_cuda_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, ld, ld, out.data_ptr(), hq * d, 1,
+                                     hq, hkv, d, d ** -0.5, causal, window, cu.ctypes.data, len(lengths),
+                                     _stream(torch))
+    N_.check(st, "attention")
+    torch.cuda.synchronize()
+    ref = _attn_ref(torch, q, k, v, cu, hq, hkv, d, d ** -0.5, causal, window)
+    err = (out.double() - ref).abs().max().item()
+    assert err < 2e-2, err
