@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -48,28 +47,55 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, sampled
+    in-process through NVML every 100 ms while the timed region runs (the same
+    fields as `nvidia-smi --query-gpu=clocks.sm,clocks.max.sm,power.draw,
+    clocks_event_reasons.*`, without spawning a process per sample)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.rows: list[list[str]] = []
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.sm: list[float] = []
+        self.reasons: set = set()
+        self.max_mhz = None
         self._stop = threading.Event()
         self._t = threading.Thread(target=self._run, daemon=True)
+        self._h = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(cuda_index)
+            bus = getattr(props, "pci_bus_id", None)
+            dom = getattr(props, "pci_domain_id", 0)
+            dev = getattr(props, "pci_device_id", 0)
+            if bus is not None:
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0".encode())
+            else:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self._nv = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._h = None
 
     def _run(self):
-        while not self._stop.is_set():
+        nv = getattr(self, "_nv", None)
+        while not self._stop.is_set() and self._h is not None:
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                for line in out.stdout.strip().splitlines():
-                    self.rows.append([x.strip() for x in line.split(",")])
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)))
+                try:
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.1)
 
     def __enter__(self):
         self._t.start()
@@ -80,16 +106,8 @@ class ClockSampler:
         self._t.join(timeout=10)
 
     def summary(self) -> dict:
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            for j, n in enumerate(names):
-                if len(r) > 5 + j and r[5 + j].lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml"}
 
 
 def corpus_batches():
@@ -216,13 +234,21 @@ def run_ours(args, world, rank, local):
     tokens = 0
     barrier()
     torch.cuda.synchronize()
+    step_ms = []
+    step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
         start.record(stream)
-        for i in range(args.warmup, need):
+        for k, i in enumerate(range(args.warmup, need)):
+            t0 = time.perf_counter()
+            step_ev[k][0].record(stream)
             model.embed(dev_ids[i].data_ptr(), packed[i][1], out=dev_out.data_ptr())
+            step_ev[k][1].record(stream)
+            step_ms.append(round((time.perf_counter() - t0) * 1000.0, 2))
             tokens += int(packed[i][1][-1])
         stop.record(stream)
         torch.cuda.synchronize()
+    step_dev_ms = [round(a.elapsed_time(b), 2) for a, b in step_ev]
     barrier()
     ms = start.elapsed_time(stop)
     launches = model.launch_count()
@@ -286,6 +312,8 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": tokens_all / (e2e_max / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "gpu_launches": launches,
+            "host_step_ms": step_ms,
+            "device_step_ms": step_dev_ms,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -219,10 +219,14 @@ __global__ void __launch_bounds__(192, 1)
       const int key0 = (kb_lo + j) * kTK;
       const bool full_block = key0 + kTK <= L && (!p.causal || key0 + kTK - 1 <= q0) &&
                               (p.window < 0 || (q0 + kTQ - 1 - key0 <= p.window && key0 + kTK - 1 - q0 <= p.window));
-      float mx = -INFINITY;
+      // Row max with 8 independent partial maxima (a single 128-long chain of
+      // fmaxf would serialise on its latency).
+      float mp[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mp[t] = -INFINITY;
       if (full_block) {
 #pragma unroll
-        for (int c = 0; c < kTK; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+        for (int c = 0; c < kTK; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sv[c]));
       } else {
 #pragma unroll
         for (int c = 0; c < kTK; ++c) {
@@ -231,9 +235,11 @@ __global__ void __launch_bounds__(192, 1)
           if (p.causal) valid = valid && key <= q;
           if (p.window >= 0) valid = valid && abs(q - key) <= p.window;
           if (!valid) sv[c] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sv[c]));
+          mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sv[c]));
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       const float m_blk = mx * p.scale_log2;
       // P_j goes into buffer j & 1: wait until PV_{j-2} released it.
       if (!wait_warp(&p_free[sb], ((j >> 1) & 1) ^ 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
@@ -263,24 +269,31 @@ __global__ void __launch_bounds__(192, 1)
         m = m_blk;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      float rowsum = 0.f;
+      float rs8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) rs8[t] = 0.f;
       uint8_t* pb = prow_base + sb * C::P_BYTES;
 #pragma unroll
       for (int c = 0; c < kTK; c += 8) {
-        float e[8];
+        uint32_t hb[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          e[t] = ex2_approx(fmaf(__uint_as_float(sv[c + t]), p.scale_log2, -m_use));
-          rowsum += e[t];
+          const float e = ex2_approx(fmaf(__uint_as_float(sv[c + t]), p.scale_log2, -m_use));
+          rs8[t] += e;
+          // bf16 round-to-nearest-even on the integer pipe (e >= 0 and finite),
+          // keeping the conversion off the MUFU/XU pipe the exp2 needs.
+          const uint32_t b = __float_as_uint(e);
+          hb[t] = b + 0x7FFFu + ((b >> 16) & 1u);
         }
         uint4 w;
-        w.x = pack_bf16x2(e[0], e[1]);
-        w.y = pack_bf16x2(e[2], e[3]);
-        w.z = pack_bf16x2(e[4], e[5]);
-        w.w = pack_bf16x2(e[6], e[7]);
+        w.x = __byte_perm(hb[0], hb[1], 0x7632);
+        w.y = __byte_perm(hb[2], hb[3], 0x7632);
+        w.z = __byte_perm(hb[4], hb[5], 0x7632);
+        w.w = __byte_perm(hb[6], hb[7], 0x7632);
         const int chunk = c >> 3;  // 16-byte chunk index 0..15 over 128 keys
         *reinterpret_cast<uint4*>(pb + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
       }
+      const float rowsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l += rowsum;
       fence_proxy_async_smem();
       tc_fence_before();

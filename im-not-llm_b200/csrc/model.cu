@@ -1047,6 +1047,12 @@ int inl_cuda_model_set_profiling(inl_model* m, int enable) {
   }
   m->prof.clear();
   m->profiling = enable != 0;
+  // pre-create events so that timed runs never call cudaEventCreate
+  while (m->profiling && m->event_pool.size() < 8192) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) break;
+    m->event_pool.push_back(e);
+  }
   return INL_OK;
 }
 
