@@ -1,0 +1,41 @@
+"""Copy the reference's own golden fixtures for the encoder path into
+tests/golden/, so that the parity tests run where the reference tree is absent.
+
+    python tests/golden/make_golden.py [REFERENCE_ROOT]
+
+Copied as-is (no regeneration): each fixture is a tiny random Hugging Face
+checkpoint plus the golden outputs the reference's tests assert against.
+  * tiny_splade            crates/inl-sparse/tests/fixtures/tiny_splade/
+                           (ModernBERT MLM + ShiftedTopKSpladePooling; asserted by
+                           crates/inl-sparse/src/modernbert.rs:1034-1057, |dw| <= 1e-4,
+                           identical term sets)
+  * tiny_embeddinggemma2   crates/inl-text/tests/fixtures/tiny_embeddinggemma2/
+                           (EmbeddingGemma 2 text tower; asserted by
+                           crates/inl-text/src/gemma2.rs:941-967, |d| < 2e-5)
+"""
+import shutil
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+FIXTURES = {
+    "tiny_splade": ("crates/inl-sparse/tests/fixtures/tiny_splade",
+                    ["config.json", "model.safetensors", "golden.json", "1_ShiftedTopKSpladePooling/config.json"]),
+    "tiny_embeddinggemma2": ("crates/inl-text/tests/fixtures/tiny_embeddinggemma2",
+                             ["config.json", "model.safetensors", "golden.json", "tokenizer.json"]),
+}
+
+
+def main(ref_root: str) -> None:
+    ref = Path(ref_root)
+    for name, (rel, files) in FIXTURES.items():
+        for f in files:
+            src = ref / rel / f
+            dst = HERE / name / f.replace("/", "__")
+            dst.parent.mkdir(parents=True, exist_ok=True)
+            shutil.copyfile(src, dst)
+            print(f"{src} -> {dst.relative_to(HERE)}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
