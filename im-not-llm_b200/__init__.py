@@ -5,11 +5,11 @@ from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  
                      TimeoutError_)
 from .model import CudaModel  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder,  # noqa: F401
-                     TextEmbedder, TextOptions)
+                     SparseEncoder, SparseVector, TextEmbedder, TextOptions)
 from . import planner, synthetic  # noqa: F401
 
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "InferenceError",
-    "InlError", "InvalidInputError", "LateEncoder", "TextEmbedder", "TextOptions", "TimeoutError_",
+    "InlError", "InvalidInputError", "LateEncoder", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions", "TimeoutError_",
     "planner", "synthetic",
 ]

@@ -237,6 +237,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- misc
+// Order-preserving map of f32 onto int32 (for atomicMax over floats of any
+// sign): non-negative floats keep their bits, negative ones flip the 31
+// magnitude bits. decode_ordered inverts it.
+__host__ __device__ __forceinline__ int encode_ordered(float f) {
+#ifdef __CUDA_ARCH__
+  const int i = __float_as_int(f);
+#else
+  int i;
+  __builtin_memcpy(&i, &f, 4);
+#endif
+  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float decode_ordered(int i) { return __int_as_float(i >= 0 ? i : (i ^ 0x7FFFFFFF)); }
+constexpr int kOrderedNegInf = static_cast<int>(0x807FFFFF);  // encode_ordered(-inf)
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

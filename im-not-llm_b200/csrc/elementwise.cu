@@ -99,7 +99,13 @@ __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T, con
 }
 
 // ------------------------------------------------------------ norms
-template <typename TI, typename TO, bool LN>
+template <bool ACT>
+__device__ __forceinline__ float pre_act(float v) {
+  if constexpr (ACT) return gelu_erf_f(v);
+  else return v;
+}
+
+template <typename TI, typename TO, bool LN, bool ACT = false>
 __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const float* __restrict__ w,
                                  const float* __restrict__ b, float eps, int rows, int H, TO* __restrict__ out,
                                  long long ldo) {
@@ -118,10 +124,10 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const 
         float v[8];
         ld8<TI>(xr + c, v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s += v[j];
+        for (int j = 0; j < 8; ++j) s += pre_act<ACT>(v[j]);
       }
     } else {
-      for (int c = lane; c < H; c += 32) s += ld_f<TI>(xr, c);
+      for (int c = lane; c < H; c += 32) s += pre_act<ACT>(ld_f<TI>(xr, c));
     }
     mean = warp_sum(s) / static_cast<float>(H);
   }
@@ -132,13 +138,13 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const 
       ld8<TI>(xr + c, v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float t = v[j] - mean;
+        const float t = pre_act<ACT>(v[j]) - mean;
         ss += t * t;
       }
     }
   } else {
     for (int c = lane; c < H; c += 32) {
-      const float t = ld_f<TI>(xr, c) - mean;
+      const float t = pre_act<ACT>(ld_f<TI>(xr, c)) - mean;
       ss += t * t;
     }
   }
@@ -149,7 +155,7 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const 
       ld8<TI>(xr + c, v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float t = (v[j] - mean) * inv;
+        float t = (pre_act<ACT>(v[j]) - mean) * inv;
         if (w) t *= w[c + j];
         if (b) t += b[c + j];
         v[j] = t;
@@ -158,7 +164,7 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const 
     }
   } else {
     for (int c = lane; c < H; c += 32) {
-      float t = (ld_f<TI>(xr, c) - mean) * inv;
+      float t = (pre_act<ACT>(ld_f<TI>(xr, c)) - mean) * inv;
       if (w) t *= w[c];
       if (b) t += b[c];
       st_f<TO>(orow, c, t);
@@ -288,8 +294,8 @@ __global__ void rows_l2_kernel(const float* __restrict__ x, long long ldx, int r
   const float* xr = x + row * ldx;
   float ss = 0.f;
   for (int c = lane; c < D; c += 32) ss += xr[c] * xr[c];
-  const float nrm = sqrtf(warp_sum(ss));
-  const float inv = 1.0f / fmaxf(nrm, clamp_min);
+  const float tot = warp_sum(ss);
+  const float inv = clamp_min >= 0.f ? 1.0f / fmaxf(sqrtf(tot), clamp_min) : 1.0f / sqrtf(tot - clamp_min);
   for (int c = lane; c < D; c += 32) out[row * ldo + c] = xr[c] * inv;
 }
 
@@ -330,6 +336,88 @@ __global__ void convert_rows_kernel(const TS* __restrict__ src, int rows, int co
     const long long dr = static_cast<long long>(r / blk) * blk_stride + off + (r % blk);
     const float v = ld_f<TS>(src, idx);
     st_f<TD>(dst, dr * ld_dst + c, col_scale ? v * col_scale[c] : v);
+  }
+}
+
+// h[r] += RMSNorm(a[r]) * w   (the Gemma post-attention / post-feedforward norms)
+template <typename T>
+__global__ void add_rms_norm_kernel(T* __restrict__ h, const T* __restrict__ a, const float* __restrict__ w,
+                                    float eps, int rows, int H) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* ar = a + row * H;
+  T* hr = h + row * H;
+  float ss = 0.f;
+  for (int c = lane; c < H; c += 32) {
+    const float v = ld_f<T>(ar, c);
+    ss += v * v;
+  }
+  const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(H) + eps);
+  const bool is_bf16 = sizeof(T) == 2;
+  for (int c = lane; c < H; c += 32) {
+    float n = ld_f<T>(ar, c) * inv * w[c];
+    if (is_bf16) n = bf16_round(n);  // the normed branch in the model dtype, then the add
+    st_f<T>(hr, c, ld_f<T>(hr, c) + n);
+  }
+}
+
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ src, long long lds, const int* __restrict__ idx, int n,
+                                   int H, T* __restrict__ dst) {
+  const int warps = blockDim.x >> 5;
+  const long long r = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= n) return;
+  const T* s = src + static_cast<long long>(idx[r]) * lds;
+  T* d = dst + r * H;
+  for (int c = lane; c < H; c += 32) d[c] = s[c];
+}
+
+__global__ void fill_i32_kernel(int* __restrict__ p, long long n, int value) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    p[i] = value;
+}
+
+// SPLADE finish + fold: w = ln(1 + relu(m + bias - shift) * open); with a canonical
+// map, out[i][canon[v]] = max over v (w >= 0, so the int bits order as the floats).
+__global__ void splade_finish_kernel(const int* __restrict__ pooled, int n, int V, const float* __restrict__ bias,
+                                     float shift, const float* __restrict__ open, const int* __restrict__ canon,
+                                     int dim, float* __restrict__ out) {
+  const long long total = static_cast<long long>(n) * V;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / V);
+    const int v = static_cast<int>(i - static_cast<long long>(row) * V);
+    const float m = decode_ordered(pooled[i]);
+    float x = m + (bias ? bias[v] : 0.f) - shift;
+    x = fmaxf(x, 0.f);  // relu before the mask: -inf never meets a zero
+    if (open) x *= open[v];
+    const float w = logf(1.0f + x);
+    if (canon) {
+      atomicMax(reinterpret_cast<int*>(out) + static_cast<long long>(row) * dim + canon[v], __float_as_int(w));
+    } else {
+      out[i] = w;
+    }
+  }
+}
+
+// out[r, j] = act(x[r, j]) * x[r, I + j]: the gated MLP when gate / up are not interleaved.
+template <typename T, int ACT>
+__global__ void act_mul_kernel(const T* __restrict__ x, int rows, int I, T* __restrict__ out) {
+  const long long total = static_cast<long long>(rows) * I;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / I;
+    const int j = static_cast<int>(i - r * I);
+    const float g = ld_f<T>(x, r * 2 * I + j), u = ld_f<T>(x, r * 2 * I + I + j);
+    float a;
+    if constexpr (ACT == INL_ACT_SILU) a = silu_f(g);
+    else if constexpr (ACT == INL_ACT_GELU_ERF) a = gelu_erf_f(g);
+    else a = gelu_tanh_f(g);
+    st_f<T>(out, i, a * u);
   }
 }
 
@@ -477,6 +565,82 @@ int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, i
   else
     convert_rows_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(src, rows, cols, static_cast<float*>(dst), ld_dst,
                                                                    blk, blk_stride, off, col_scale);
+  return ok(cudaGetLastError());
+}
+
+int norm_act(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
+             void* out, int out_bf16, long long ldo, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const int grid = rows_grid(rows, 4);
+  if (x_bf16 && out_bf16)
+    norm_rows_kernel<__nv_bfloat16, __nv_bfloat16, true, true><<<grid, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, w, b, eps, rows, H, static_cast<__nv_bfloat16*>(out), ldo);
+  else if (!x_bf16 && !out_bf16)
+    norm_rows_kernel<float, float, true, true><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, w, b, eps,
+                                                                     rows, H, static_cast<float*>(out), ldo);
+  else
+    return -1;
+  return ok(cudaGetLastError());
+}
+
+int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const int grid = rows_grid(rows, 4);
+  if (bf16)
+    add_rms_norm_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<__nv_bfloat16*>(h),
+                                                             static_cast<const __nv_bfloat16*>(a), w, eps, rows, H);
+  else
+    add_rms_norm_kernel<float><<<grid, 128, 0, s>>>(static_cast<float*>(h), static_cast<const float*>(a), w, eps,
+                                                     rows, H);
+  return ok(cudaGetLastError());
+}
+
+int gather_rows(const void* src, int bf16, long long lds, const int* idx, int n, int H, void* dst, cudaStream_t s) {
+  if (n <= 0) return 0;
+  const int grid = rows_grid(n, 4);
+  if (bf16)
+    gather_rows_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(src), lds, idx, n, H,
+                                                            static_cast<__nv_bfloat16*>(dst));
+  else
+    gather_rows_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(src), lds, idx, n, H,
+                                                   static_cast<float*>(dst));
+  return ok(cudaGetLastError());
+}
+
+int fill_i32(int* p, long long n, int value, cudaStream_t s) {
+  if (n <= 0) return 0;
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148LL * 16));
+  fill_i32_kernel<<<grid, 256, 0, s>>>(p, n, value);
+  return ok(cudaGetLastError());
+}
+
+int splade_finish(const int* pooled, int n, int V, const float* bias, float shift, const float* open,
+                  const int* canon, int dim, float* out, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (canon) {
+    if (cudaMemsetAsync(out, 0, static_cast<size_t>(n) * dim * 4, s) != cudaSuccess) return -3;
+  }
+  const long long total = static_cast<long long>(n) * V;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  splade_finish_kernel<<<grid, 256, 0, s>>>(pooled, n, V, bias, shift, open, canon, dim, out);
+  return ok(cudaGetLastError());
+}
+
+int act_mul(const void* x, int bf16, int rows, int I, int act, void* out, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const long long total = static_cast<long long>(rows) * I;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+#define INL_AM(T, A) act_mul_kernel<T, A><<<grid, 256, 0, s>>>(static_cast<const T*>(x), rows, I, static_cast<T*>(out))
+  if (bf16) {
+    if (act == INL_ACT_SILU) INL_AM(__nv_bfloat16, INL_ACT_SILU);
+    else if (act == INL_ACT_GELU_ERF) INL_AM(__nv_bfloat16, INL_ACT_GELU_ERF);
+    else INL_AM(__nv_bfloat16, INL_ACT_GELU_TANH);
+  } else {
+    if (act == INL_ACT_SILU) INL_AM(float, INL_ACT_SILU);
+    else if (act == INL_ACT_GELU_ERF) INL_AM(float, INL_ACT_GELU_ERF);
+    else INL_AM(float, INL_ACT_GELU_TANH);
+  }
+#undef INL_AM
   return ok(cudaGetLastError());
 }
 

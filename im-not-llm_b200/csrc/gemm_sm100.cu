@@ -60,6 +60,9 @@ struct EpiArgs {
   float qk_eps;
   int* status;
   int M, N;
+  const int* seg;
+  int* pooled;
+  long long ldp;
 };
 
 template <int ACT>
@@ -203,6 +206,32 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
         store_row32_bf16(dst, v, out_n - (o0 + c));
       }
     }
+  } else if constexpr (EPI == INL_EPI_SEGMAX) {
+    // Rows are vocabulary entries, columns are packed tokens of segment seg[col]:
+    // a running max per segment run, flushed with one atomicMax per run.
+    // seg[col] is the same for every lane, so the branches stay warp-uniform.
+    int cur = -1;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < HW; c += 32) {
+      tmem_ld32(t_row + half * HW + c, r);
+      tmem_ld_wait();
+      const int c0 = n0 + half * HW + c;
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int col = c0 + j;
+        const int sg = col < e.N ? __ldg(e.seg + col) : -1;
+        const float v = __uint_as_float(r[j]);
+        if (sg != cur) {
+          if (cur >= 0 && row_ok) atomicMax(e.pooled + static_cast<long long>(cur) * e.ldp + row, encode_ordered(mx));
+          cur = sg;
+          mx = v;
+        } else {
+          mx = fmaxf(mx, v);
+        }
+      }
+    }
+    if (cur >= 0 && row_ok) atomicMax(e.pooled + static_cast<long long>(cur) * e.ldp + row, encode_ordered(mx));
   } else if constexpr (EPI == INL_EPI_QKV) {
     // Heads of width d inside this warp's BN/2 columns; q heads first, then k, then v.
     const int c_begin = n0 + half * HW;
@@ -509,7 +538,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0) return 0;
   if (g.K <= 0 || (g.K % 8) != 0 || (g.lda % 8) != 0 || (g.ldw % 8) != 0) return -1;
   if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.W) & 15)) return -1;
-  if ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.ldo % 8) != 0) return -1;
+  if (g.epi != INL_EPI_SEGMAX && ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.ldo % 8) != 0)) return -1;
   if (g.epi == INL_EPI_RESID_BF16 && ((reinterpret_cast<uintptr_t>(g.resid) & 15) || (g.ldr % 8) != 0)) return -1;
   int bn = (g.N <= 128 || (g.N % 256) != 0) ? 128 : 256;
   if (g.epi == INL_EPI_GATED_BF16) {
@@ -529,12 +558,16 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     bn = g.force_bn;
   }
   if (g.ss_in && (g.ss_in_parts <= 0 || g.ss_dim <= 0)) return -1;
+  if (g.epi == INL_EPI_SEGMAX) {
+    if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
+    bn = 256;
+  }
   CUtensorMap ta, tb;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, bn)) return -2;
   EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.ss_in, g.ss_in_parts, g.ss_dim, g.ss_eps, g.ss_out,
             (g.N + INL_SS_COLS - 1) / INL_SS_COLS, g.qn, g.kn, g.pos, g.cos, g.sin, g.hq, g.hkv, g.d, g.max_pos,
-            g.qk_eps, g.status, g.M, g.N};
+            g.qk_eps, g.status, g.M, g.N, g.seg, g.pooled, g.ldp};
   cudaError_t err;
   if (bn == 256) {
     switch (g.epi) {
@@ -543,6 +576,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_QKV: err = launch_gemm<256, INL_EPI_QKV, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_SEGMAX: err = launch_gemm<256, INL_EPI_SEGMAX, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: return -1;
     }
   } else {

@@ -17,6 +17,7 @@ enum InlEpilogue : int {
   INL_EPI_GATED_BF16 = 2,  // out[:, n/2] = act(r * gate) * (r * up), gate/up interleaved in gate_block rows
   INL_EPI_F32 = 3,         // out = r * acc (f32)
   INL_EPI_QKV = 4,         // q|k|v heads: per-head RMSNorm of q/k (qn/kn) + half-split RoPE at pos[row]
+  INL_EPI_SEGMAX = 5,      // pooled[seg[col]][row] = max over columns of the segment (order-encoded atomicMax)
 };
 
 // Columns per partial sum of squares written by the residual epilogue.
@@ -54,6 +55,10 @@ struct GemmArgs {
   const float* sin = nullptr;
   int hq = 0, hkv = 0, d = 0, max_pos = 0;
   float qk_eps = 1e-6f;
+  // SEGMAX epilogue: column segments and the [segments, ldp] order-encoded maxima
+  const int* seg = nullptr;
+  int* pooled = nullptr;
+  long long ldp = 0;
   int* status = nullptr;
   int max_ctas = 0;   // 0 = one CTA per SM
   int force_bn = 0;   // 0 = automatic tile width
@@ -85,6 +90,11 @@ struct GemmF32Args {
 
 // SIMT f32 GEMM (f32-accurate path for the f32 configurations).
 int gemm_f32_tn(const GemmF32Args& g, cudaStream_t stream);
+
+// f32 X[M,K] . W[N,K]^T reduced to pooled[seg[r]][n] = max over rows r of the segment
+// (order-encoded int32, atomicMax; pooled pre-filled with the encoding of -inf).
+int gemm_f32_segmax(const float* A, long long lda, const float* W, long long ldw, int M, int N, int K,
+                    const int* seg, int* pooled, long long ldp, cudaStream_t s);
 
 // ---------------------------------------------------------------- elementwise
 // out[t, :] = table[ids[t], :] * scale ; ids >= vocab set *status = BAD_INDEX and write zeros.
@@ -128,7 +138,27 @@ int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s);
 int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, int n, const float* w, float eps,
                        int H, float* out, cudaStream_t s);
 
-// Row L2: out = x / max(|x|, clamp) for f32 rows (x may alias out).
+// LayerNorm of gelu_erf(x) (the SPLADE MLM head: LN(gelu(dense(h)))); same dtypes in and out.
+int norm_act(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
+             void* out, int out_bf16, long long ldo, cudaStream_t s);
+
+// h[r] += RMSNorm(a[r]) * w (row-wise, rows x H, both in the model dtype).
+int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s);
+
+// dst[r] = src[idx[r]] for r < n (rows of H values).
+int gather_rows(const void* src, int bf16, long long lds, const int* idx, int n, int H, void* dst, cudaStream_t s);
+
+int fill_i32(int* p, long long n, int value, cudaStream_t s);
+
+// out[r, j] = act(x[r, j]) * x[r, I + j]  (x [rows, 2I], out [rows, I], same dtype).
+int act_mul(const void* x, int bf16, int rows, int I, int act, void* out, cudaStream_t s);
+
+// SPLADE finish + fold from order-encoded per-(text, term) maxima [n, V]:
+// out = ln(1 + relu(m + bias - shift) * open), folded by max onto canon[v] (dim terms) when canon != null.
+int splade_finish(const int* pooled, int n, int V, const float* bias, float shift, const float* open,
+                  const int* canon, int dim, float* out, cudaStream_t s);
+
+// Row L2: out = x / max(|x|, clamp) for f32 rows (x may alias out); clamp < 0 means x / sqrt(sum x^2 - clamp).
 int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min, float* out, long long ldo,
                 cudaStream_t s);
 

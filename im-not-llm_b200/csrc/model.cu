@@ -66,6 +66,25 @@ std::string str_or(const inl::json::Value& v, const char* key, const std::string
   return (x && x->kind == inl::json::Value::String) ? x->str : def;
 }
 
+std::vector<int> int_list(const inl::json::Value* v) {
+  std::vector<int> out;
+  if (v && v->kind == inl::json::Value::Array)
+    for (const auto& x : v->arr) out.push_back(static_cast<int>(x.num));
+  return out;
+}
+
+// rope_parameters.{full_attention|sliding_attention}.rope_theta, when present.
+bool nested_theta(const inl::json::Value& root, const char* kind, double* out) {
+  const inl::json::Value* rp = root.get("rope_parameters");
+  if (!rp) return false;
+  const inl::json::Value* k = rp->get(kind);
+  if (!k) return false;
+  const inl::json::Value* t = k->get("rope_theta");
+  if (!t || !t->is_num()) return false;
+  *out = t->num;
+  return true;
+}
+
 int parse_config(const std::string& text, ModelConfig& c) {
   inl::json::Value root;
   try {
@@ -74,13 +93,23 @@ int parse_config(const std::string& text, ModelConfig& c) {
     return fail(INL_ERR_CONFIG, std::string("config: ") + e.what());
   }
   if (root.kind != inl::json::Value::Object) return fail(INL_ERR_CONFIG, "config: not a JSON object");
-  // Qwen3-VL style nesting (crates/inl-text/src/qwen3/mod.rs:55-69).
-  if (const inl::json::Value* tc = root.get("text_config"); tc && tc->kind == inl::json::Value::Object)
-    root = *tc;
-  const std::string mt = str_or(root, "model_type", "qwen3");
+  std::string mt = str_or(root, "model_type", "qwen3");
+  // Nested text configs: Qwen3-VL (crates/inl-text/src/qwen3/mod.rs:55-69) and
+  // EmbeddingGemma 2 (crates/inl-text/src/gemma2.rs:108-112).
+  if (const inl::json::Value* tc = root.get("text_config"); tc && tc->kind == inl::json::Value::Object) {
+    inl::json::Value inner = *tc;
+    if (!inner.get("model_type")) {
+      inl::json::Value name;
+      name.kind = inl::json::Value::String;
+      name.str = mt;
+      inner.obj.emplace_back("model_type", name);
+    }
+    root = inner;
+    mt = str_or(root, "model_type", mt);
+  }
   if (mt == "qwen3") c.arch = inl::ARCH_QWEN3;
   else if (mt == "modernbert") c.arch = inl::ARCH_MODERNBERT;
-  else if (mt == "gemma_style" || mt == "gemma3_text" || mt == "embeddinggemma")
+  else if (mt == "gemma_style" || mt == "gemma3_text" || mt == "embedding_gemma2" || mt == "embeddinggemma")
     c.arch = inl::ARCH_GEMMA;
   else
     return fail(INL_ERR_CONFIG, "config: unsupported model_type '" + mt + "'");
@@ -101,24 +130,82 @@ int parse_config(const std::string& text, ModelConfig& c) {
   c.theta = num_or(root, "rope_theta", 10000.0);
   c.max_pos = static_cast<int>(std::min(32768.0, num_or(root, "max_position_embeddings", 32768.0)));
   c.pad_token_id = static_cast<int>(num_or(root, "pad_token_id", 0));
+  c.layer_global.assign(c.layers, 1);
   if (c.arch == inl::ARCH_QWEN3) {
     c.causal = bool_or(root, "is_causal", true);
     c.theta_local = c.theta;
   } else if (c.arch == inl::ARCH_MODERNBERT) {
+    // crates/inl-sparse/src/modernbert.rs:28-166
     c.causal = false;
-    c.norm_eps = static_cast<float>(num_or(root, "norm_eps", 1e-5));
-    c.theta = num_or(root, "global_rope_theta", 160000.0);
-    c.theta_local = num_or(root, "local_rope_theta", 10000.0);
+    c.norm_eps = static_cast<float>(num_or(root, "norm_eps", num_or(root, "layer_norm_eps", 1e-5)));
+    double g = num_or(root, "global_rope_theta", 160000.0), l = num_or(root, "local_rope_theta", 10000.0);
+    nested_theta(root, "full_attention", &g);
+    nested_theta(root, "sliding_attention", &l);
+    c.theta = g;
+    c.theta_local = l;
     c.global_every = static_cast<int>(num_or(root, "global_attn_every_n_layers", 3));
     c.local_half_window = static_cast<int>(num_or(root, "local_attention", 128)) / 2;
-    c.logit_shift = static_cast<float>(num_or(root, "splade_logit_shift", 0.0));
+    if (c.global_every <= 0) return fail(INL_ERR_CONFIG, "config: global_attn_every_n_layers must be positive");
+    for (int i = 0; i < c.layers; ++i) c.layer_global[i] = (i % c.global_every) == 0;
+    if (bool_or(root, "mlp_bias", false) || bool_or(root, "norm_bias", false) ||
+        bool_or(root, "classifier_bias", false))
+      return fail(INL_ERR_CONFIG, "config: biased ModernBERT mlp/norm/classifier weights are not supported");
+    c.decoder_bias = bool_or(root, "decoder_bias", true);
+    if (c.H % c.hq != 0) return fail(INL_ERR_CONFIG, "config: hidden_size must be a multiple of num_attention_heads");
+    // SPLADE pooling (ShiftedTopKSpladePooling module config), nested under "splade"
+    if (const inl::json::Value* sp = root.get("splade"); sp && sp->kind == inl::json::Value::Object) {
+      c.logit_shift = static_cast<float>(num_or(*sp, "logit_shift", 0.0));
+      c.prefix_ids = int_list(sp->get("prefix_token_ids"));
+      c.masked_vocab_ids = int_list(sp->get("masked_vocab_ids"));
+      c.canonical_ids = int_list(sp->get("canonical_ids"));
+      if (!c.canonical_ids.empty() && static_cast<int>(c.canonical_ids.size()) != c.V)
+        return fail(INL_ERR_CONFIG, "config: splade.canonical_ids must have vocab_size entries");
+      for (int id : c.prefix_ids)
+        if (id < 0 || id >= c.V) return fail(INL_ERR_CONFIG, "config: a prefix token id is outside the vocabulary");
+      for (int id : c.masked_vocab_ids)
+        if (id < 0 || id >= c.V) return fail(INL_ERR_CONFIG, "config: a masked vocab id is outside the vocabulary");
+      for (int id : c.canonical_ids)
+        if (id < 0) return fail(INL_ERR_CONFIG, "config: negative canonical id");
+      const std::string strategy = str_or(*sp, "pooling_strategy", "max");
+      const std::string act = str_or(*sp, "activation_function", "relu");
+      if (strategy != "max" || act != "relu")
+        return fail(INL_ERR_CONFIG, "config: only max pooling with relu activation is supported");
+      if (num_or(*sp, "top_k", 0) > 0) return fail(INL_ERR_CONFIG, "config: SPLADE top_k is not supported");
+    }
   } else {
+    // EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:78-211)
     c.causal = false;
     c.sliding_window = static_cast<int>(num_or(root, "sliding_window", 512));
-    c.full_every = static_cast<int>(num_or(root, "full_attention_every_n_layers", 6));
-    c.theta_local = num_or(root, "rope_local_base_freq", 10000.0);
-    c.attn_scale = static_cast<float>(num_or(root, "query_pre_attn_scalar_inverse", 1.0));
-    c.embed_scale = static_cast<float>(std::sqrt(static_cast<double>(c.H)));
+    double full = num_or(root, "rope_theta", 1000000.0), slide = num_or(root, "rope_local_base_freq", 10000.0);
+    nested_theta(root, "full_attention", &full);
+    nested_theta(root, "sliding_attention", &slide);
+    c.theta = full;
+    c.theta_local = slide;
+    c.attn_scale = 1.0f;  // unscaled scores: q and k are RMS-normalised per head
+    const inl::json::Value* kinds = root.get("layer_types");
+    if (kinds && kinds->kind == inl::json::Value::Array) {
+      if (static_cast<int>(kinds->arr.size()) != c.layers)
+        return fail(INL_ERR_CONFIG, "config: layer_types length differs from num_hidden_layers");
+      for (int i = 0; i < c.layers; ++i) {
+        const std::string& k = kinds->arr[i].str;
+        if (k != "full_attention" && k != "sliding_attention")
+          return fail(INL_ERR_CONFIG, "config: unknown layer type '" + k + "'");
+        c.layer_global[i] = k == "full_attention";
+      }
+    } else {
+      c.full_every = static_cast<int>(num_or(root, "full_attention_every_n_layers", 6));
+      if (c.full_every <= 0) return fail(INL_ERR_CONFIG, "config: full_attention_every_n_layers must be positive");
+      for (int i = 0; i < c.layers; ++i) c.layer_global[i] = (i % c.full_every) == c.full_every - 1;
+    }
+    if (const inl::json::Value* plc = root.get("per_layer_config"); plc && !plc->obj.empty())
+      return fail(INL_ERR_CONFIG, "config: per-layer head shapes are not supported by the CUDA tower");
+    if (num_or(root, "hidden_size_per_layer_input", 0) > 0)
+      return fail(INL_ERR_CONFIG, "config: per-layer embeddings (PLE) are not supported by the CUDA tower");
+    const std::string act = str_or(root, "hidden_activation", "gelu_pytorch_tanh");
+    if (act != "gelu_pytorch_tanh") return fail(INL_ERR_CONFIG, "config: hidden_activation must be gelu_pytorch_tanh");
+    c.dense_dims = int_list(root.get("dense_dims"));
+    if (c.dense_dims.empty() && num_or(root, "embedding_dim", 0) > 0)
+      c.dense_dims.push_back(static_cast<int>(num_or(root, "embedding_dim", 0)));
   }
   return INL_OK;
 }
@@ -213,16 +300,24 @@ struct Loader {
   // Upload `name` ([rows, cols]) into dst rows remapped as (r / blk) * blk_stride + off + r % blk.
   int upload(const std::string& name, int rows, int cols, void* dst, int dst_bf16, long long ld_dst, int blk,
              long long blk_stride, long long off, const float* col_scale = nullptr) {
+    return upload_part(name, rows, cols, 0, rows, dst, dst_bf16, ld_dst, blk, blk_stride, off, col_scale);
+  }
+
+  // Rows [row0, row0 + rows) of `name` ([total_rows, cols]) only.
+  int upload_part(const std::string& name, int total_rows, int cols, int row0, int rows, void* dst, int dst_bf16,
+                  long long ld_dst, int blk, long long blk_stride, long long off, const float* col_scale = nullptr) {
     const TensorSrc* s = find(name);
     if (!s) return fail(INL_ERR_INFERENCE, "missing weight " + prefix + name);
-    if (s->numel != static_cast<int64_t>(rows) * cols)
+    if (s->numel != static_cast<int64_t>(total_rows) * cols)
       return fail(INL_ERR_INFERENCE, "weight " + name + " has " + std::to_string(s->numel) + " values, expected " +
-                                         std::to_string(static_cast<long long>(rows) * cols));
-    const size_t bytes = static_cast<size_t>(s->numel) * (s->bf16 ? 2 : 4);
+                                         std::to_string(static_cast<long long>(total_rows) * cols));
+    const size_t es_src = s->bf16 ? 2 : 4;
+    const size_t bytes = static_cast<size_t>(rows) * cols * es_src;
+    const char* src = static_cast<const char*>(s->data) + static_cast<size_t>(row0) * cols * es_src;
     INL_CUDA_TRY(staging.ensure(bytes), "staging allocation");
     // Stream-ordered copy: a pageable cudaMemcpy may return before its DMA lands,
     // and the model's non-blocking stream does not wait for the legacy stream.
-    INL_CUDA_TRY(cudaMemcpyAsync(staging.p, s->data, bytes, cudaMemcpyHostToDevice, m->stream), "weight upload");
+    INL_CUDA_TRY(cudaMemcpyAsync(staging.p, src, bytes, cudaMemcpyHostToDevice, m->stream), "weight upload");
     int r = s->bf16 ? inl::convert_bf16_rows(staging.as<__nv_bfloat16>(), rows, cols, dst, dst_bf16, ld_dst, blk,
                                              blk_stride, off, m->stream, col_scale)
                     : inl::convert_rows(staging.as<float>(), rows, cols, dst, dst_bf16, ld_dst, blk, blk_stride, off,
@@ -230,6 +325,12 @@ struct Loader {
     if (r != 0) return fail(INL_ERR_INFERENCE, "weight conversion launch failed");
     INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "weight conversion");
     return INL_OK;
+  }
+
+  bool has(const std::string& name) const { return find(name) != nullptr; }
+
+  int matrix_into(const std::string& name, int rows, int cols, void* dst, int as_bf16) {
+    return upload(name, rows, cols, dst, as_bf16, cols, rows, 0, 0);
   }
 
   int matrix(const std::string& name, int rows, int cols, void** out, int as_bf16) {
@@ -305,11 +406,14 @@ int load_qwen3(inl_model* m, Loader& L) {
   const ModelConfig& c = m->c;
   const int bf = m->dtype == INL_DTYPE_BF16;
   const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv = q_out + 2 * kv_out;
-  const int gb = m->gate_block;
-  if (c.I % gb != 0)
-    return fail(INL_ERR_CONFIG, "intermediate_size must be a multiple of " + std::to_string(gb));
+  // gate/up interleaved in gate_block rows for the gated epilogue, else stored
+  // [gate; up] and combined by a separate kernel.
+  m->gated_split = (c.I % m->gate_block) != 0;
+  const int gb = m->gated_split ? c.I : m->gate_block;
+  const long long gstride = m->gated_split ? 0 : 2LL * gb;
+  const long long up_off = m->gated_split ? c.I : gb;
   // Fused bf16 layer: folded input norms, q/k norm + RoPE in the QKV epilogue.
-  m->fused = bf && (c.d == 64 || c.d == 128) && c.H % INL_SS_COLS == 0 && qkv % 256 == 0;
+  m->fused = bf && !m->gated_split && (c.d == 64 || c.d == 128) && c.H % INL_SS_COLS == 0 && qkv % 256 == 0;
   int r;
   if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
   m->layers.resize(c.layers);
@@ -336,12 +440,140 @@ int load_qwen3(inl_model* m, Loader& L) {
     if ((r = L.upload(p + "self_attn.v_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out + kv_out, f1)))
       return r;
     if ((r = L.upload(p + "self_attn.o_proj.weight", c.H, q_out, w.wo, bf, q_out, c.H, 0, 0))) return r;
-    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, 0, f2))) return r;
-    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, 2LL * gb, gb, f2))) return r;
+    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, 0, f2))) return r;
+    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, up_off, f2))) return r;
     if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
   }
   if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
   if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0, &m->cos0T, &m->sin0T))) return r;
+  return INL_OK;
+}
+
+int upload_host(inl_model* m, void** dst, const void* src, size_t bytes) {
+  void* p = nullptr;
+  INL_CUDA_TRY(cudaMalloc(&p, std::max<size_t>(bytes, 4)), "device table");
+  m->allocs.push_back(p);
+  if (bytes) {
+    INL_CUDA_TRY(cudaMemcpyAsync(p, src, bytes, cudaMemcpyHostToDevice, m->stream), "table upload");
+    INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "table upload");
+  }
+  *dst = p;
+  return INL_OK;
+}
+
+// ModernBERT MLM (crates/inl-sparse/src/modernbert.rs:469-520 tensor names);
+// the decoder is tied to the token embeddings.
+int load_modernbert(inl_model* m, Loader& L) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  m->gated_split = (c.I % m->gate_block) != 0;
+  const int gb = m->gated_split ? c.I : m->gate_block;
+  const long long gstride = m->gated_split ? 0 : 2LL * gb;
+  const long long up_off = m->gated_split ? c.I : gb;
+  if (c.d % 32 != 0) return fail(INL_ERR_CONFIG, "head_dim must be a multiple of 32");
+  const size_t es = bf ? 2 : 4;
+  int r;
+  if ((r = L.matrix("model.embeddings.tok_embeddings.weight", c.V, c.H, &m->embed, bf))) return r;
+  if ((r = L.vec("model.embeddings.norm.weight", c.H, &m->emb_norm))) return r;
+  m->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    inl::LayerWeights& w = m->layers[l];
+    w.wqkv = L.alloc(static_cast<size_t>(3) * c.H * c.H * es);
+    w.wo = L.alloc(static_cast<size_t>(c.H) * c.H * es);
+    w.wgu = L.alloc(static_cast<size_t>(2) * c.I * c.H * es);
+    w.wd = L.alloc(static_cast<size_t>(c.H) * c.I * es);
+    if (!w.wqkv || !w.wo || !w.wgu || !w.wd) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+    if (l > 0 && (r = L.vec(p + "attn_norm.weight", c.H, &w.ln1))) return r;  // layer 0: identity
+    if ((r = L.vec(p + "mlp_norm.weight", c.H, &w.ln2))) return r;
+    if ((r = L.matrix_into(p + "attn.Wqkv.weight", 3 * c.H, c.H, w.wqkv, bf))) return r;
+    if ((r = L.matrix_into(p + "attn.Wo.weight", c.H, c.H, w.wo, bf))) return r;
+    // Wi = [input (activated) ; gate] -> the gated epilogue's layout
+    if ((r = L.upload_part(p + "mlp.Wi.weight", 2 * c.I, c.H, 0, c.I, w.wgu, bf, c.H, gb, gstride, 0))) return r;
+    if ((r = L.upload_part(p + "mlp.Wi.weight", 2 * c.I, c.H, c.I, c.I, w.wgu, bf, c.H, gb, gstride, up_off)))
+      return r;
+    if ((r = L.matrix_into(p + "mlp.Wo.weight", c.H, c.I, w.wd, bf))) return r;
+  }
+  if ((r = L.vec("model.final_norm.weight", c.H, &m->final_norm))) return r;
+  if ((r = L.matrix("head.dense.weight", c.H, c.H, &m->head_dense, bf))) return r;
+  if ((r = L.vec("head.norm.weight", c.H, &m->head_norm))) return r;
+  m->decoder_bias = nullptr;
+  if (c.decoder_bias && L.has("decoder.bias") && (r = L.vec("decoder.bias", c.V, &m->decoder_bias))) return r;
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;
+  if ((r = build_rope(m, c.theta_local, &m->cos1, &m->sin1))) return r;
+  // SPLADE tables
+  std::vector<float> open(c.V, 1.f);
+  for (int id : c.masked_vocab_ids) open[id] = 0.f;
+  void* p = nullptr;
+  if ((r = upload_host(m, &p, open.data(), open.size() * 4))) return r;
+  m->open_mask = static_cast<float*>(p);
+  m->sparse_dim = c.V;
+  if (!c.canonical_ids.empty()) {
+    if ((r = upload_host(m, &p, c.canonical_ids.data(), c.canonical_ids.size() * 4))) return r;
+    m->canon = static_cast<int*>(p);
+    m->sparse_dim = *std::max_element(c.canonical_ids.begin(), c.canonical_ids.end()) + 1;
+  }
+  return INL_OK;
+}
+
+// EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:233-494 tensor names),
+// uniform head shape, no per-layer embeddings; dense head chain kept in f32.
+int load_gemma(inl_model* m, Loader& L) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  m->gated_split = (c.I % m->gate_block) != 0;
+  const int gb = m->gated_split ? c.I : m->gate_block;
+  const long long gstride = m->gated_split ? 0 : 2LL * gb;
+  const long long up_off = m->gated_split ? c.I : gb;
+  if (c.d % 32 != 0) return fail(INL_ERR_CONFIG, "head_dim must be a multiple of 32");
+  if (L.has("ple.per_layer_model_projection.weight"))
+    return fail(INL_ERR_CONFIG, "per-layer embeddings (PLE) are not supported by the CUDA tower");
+  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv = q_out + 2 * kv_out;
+  const size_t es = bf ? 2 : 4;
+  int r;
+  if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
+  m->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    inl::LayerWeights& w = m->layers[l];
+    w.wqkv = L.alloc(static_cast<size_t>(qkv) * c.H * es);
+    w.wo = L.alloc(static_cast<size_t>(c.H) * q_out * es);
+    w.wgu = L.alloc(static_cast<size_t>(2) * c.I * c.H * es);
+    w.wd = L.alloc(static_cast<size_t>(c.H) * c.I * es);
+    if (!w.wqkv || !w.wo || !w.wgu || !w.wd) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+    if ((r = L.upload(p + "self_attn.q_proj.weight", q_out, c.H, w.wqkv, bf, c.H, q_out, 0, 0))) return r;
+    if ((r = L.upload(p + "self_attn.k_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out))) return r;
+    if ((r = L.upload(p + "self_attn.v_proj.weight", kv_out, c.H, w.wqkv, bf, c.H, kv_out, 0, q_out + kv_out)))
+      return r;
+    if ((r = L.upload(p + "self_attn.o_proj.weight", c.H, q_out, w.wo, bf, q_out, c.H, 0, 0))) return r;
+    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, 0))) return r;
+    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, up_off))) return r;
+    if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
+    if ((r = L.vec(p + "self_attn.q_norm.weight", c.d, &w.qn))) return r;
+    if ((r = L.vec(p + "self_attn.k_norm.weight", c.d, &w.kn))) return r;
+    if ((r = L.vec(p + "input_layernorm.weight", c.H, &w.ln1))) return r;
+    if ((r = L.vec(p + "post_attention_layernorm.weight", c.H, &w.ln1_post))) return r;
+    if ((r = L.vec(p + "pre_feedforward_layernorm.weight", c.H, &w.ln2))) return r;
+    if ((r = L.vec(p + "post_feedforward_layernorm.weight", c.H, &w.ln2_post))) return r;
+  }
+  if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
+  // Dense head: "dense_head.<j>.weight" chain, else the checkpoint's embedding_projection.
+  int in = c.H;
+  for (size_t j = 0; j < c.dense_dims.size(); ++j) {
+    const std::string name =
+        L.has("dense_head." + std::to_string(j) + ".weight") ? "dense_head." + std::to_string(j) + ".weight"
+                                                             : "embedding_projection.weight";
+    void* w = nullptr;
+    if ((r = L.matrix(name, c.dense_dims[j], in, &w, 0))) return r;
+    m->dense_chain.push_back(static_cast<float*>(w));
+    in = c.dense_dims[j];
+  }
+  m->c.embed_scale = static_cast<float>(std::sqrt(static_cast<double>(c.H)));
+  if (bf) {  // the reference multiplies by the scale cast to bf16 (crates/inl-text/src/gemma2.rs:575-587)
+    m->c.embed_scale = __bfloat162float(__float2bfloat16_rn(m->c.embed_scale));
+  }
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;        // full layers
+  if ((r = build_rope(m, c.theta_local, &m->cos1, &m->sin1))) return r;  // sliding layers
   return INL_OK;
 }
 
@@ -386,7 +618,7 @@ int create_common(const char* config_json, int device, int dtype, inl_model** ou
 int load_weights(inl_model* m, const TensorMap& t) {
   Loader L{m, t, "", {}};
   // Qwen3-VL checkpoints nest the tower (crates/inl-text/src/qwen3/mod.rs:397-404).
-  if (!t.count("embed_tokens.weight")) {
+  if (m->c.arch != inl::ARCH_MODERNBERT && !t.count("embed_tokens.weight")) {
     for (const char* p : {"model.language_model.", "model.", "language_model."})
       if (t.count(std::string(p) + "embed_tokens.weight")) {
         L.prefix = p;
@@ -396,7 +628,9 @@ int load_weights(inl_model* m, const TensorMap& t) {
   int r = INL_OK;
   switch (m->c.arch) {
     case inl::ARCH_QWEN3: r = load_qwen3(m, L); break;
-    default: r = fail(INL_ERR_CONFIG, "this model_type is not built into this library version"); break;
+    case inl::ARCH_MODERNBERT: r = load_modernbert(m, L); break;
+    case inl::ARCH_GEMMA: r = load_gemma(m, L); break;
+    default: r = fail(INL_ERR_CONFIG, "unknown architecture"); break;
   }
   return r;
 }
@@ -447,6 +681,7 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->xn.ensure(T * c.H * e), "workspace");
   INL_CUDA_TRY(m->qkv.ensure(T * std::max(qkv_cols, act_cols) * e), "workspace");
   INL_CUDA_TRY(m->attn.ensure(T * static_cast<size_t>(c.hq) * c.d * e), "workspace");
+  if (m->gated_split) INL_CUDA_TRY(m->tmp.ensure(T * 2 * static_cast<size_t>(c.I) * e), "workspace");
   INL_CUDA_TRY(m->ids.ensure(T * 4), "workspace");
   const size_t parts = static_cast<size_t>((c.H + INL_SS_COLS - 1) / INL_SS_COLS);
   INL_CUDA_TRY(m->ss_a.ensure(T * parts * 4), "workspace");
@@ -714,6 +949,19 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
   return INL_OK;
 }
 
+// act(gate(x)) * up(x) -> out [T, I]: one GEMM with the gated epilogue, or a
+// plain [T, 2I] GEMM plus act_mul when gate / up are stored split.
+int mlp_gated(inl_model* m, const void* x, int T, const void* wgu, int act, void* out) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  if (!m->gated_split)
+    return linear(m, x, c.H, wgu, T, 2 * c.I, c.H, INL_EPI_GATED_BF16, act, out, c.I, nullptr, 0, 2);
+  int r = linear(m, x, c.H, wgu, T, 2 * c.I, c.H, bf ? INL_EPI_BF16 : INL_EPI_F32, 0, m->tmp.p, 2 * c.I, nullptr, 0, 2);
+  if (r) return r;
+  m->launches++;
+  return inl::act_mul(m->tmp.p, bf, T, c.I, act, out, m->stream);
+}
+
 // Embedding + every layer; leaves the last hidden state in m->h.
 int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
   const ModelConfig& c = m->c;
@@ -776,11 +1024,138 @@ int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
               "o projection");
     INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, w.ln2, c.eps, T, c.H, m->xn.p, bf, c.H, s), "post-attention norm");
     m->launches++;
-    INL_K_TRY(linear(m, m->xn.p, c.H, w.wgu, T, 2 * c.I, c.H, INL_EPI_GATED_BF16, INL_ACT_SILU, m->qkv.p, c.I,
-                     nullptr, 0, 2),
-              "gate/up projection");
+    INL_K_TRY(mlp_gated(m, m->xn.p, T, w.wgu, INL_ACT_SILU, m->qkv.p), "gate/up projection");
     INL_K_TRY(linear(m, m->qkv.p, c.I, w.wd, T, c.H, c.I, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 3),
               "down projection");
+  }
+  return INL_OK;
+}
+
+inl::AttnArgs attn_args(inl_model* m, const Batch& b, int n_work, int qkv_cols, int q_out, int kv_out) {
+  const ModelConfig& c = m->c;
+  const size_t e = es(m);
+  inl::AttnArgs aa;
+  aa.q = m->qkv.p;
+  aa.k = static_cast<const char*>(m->qkv.p) + static_cast<size_t>(q_out) * e;
+  aa.v = static_cast<const char*>(m->qkv.p) + static_cast<size_t>(q_out + kv_out) * e;
+  aa.ldq = aa.ldk = aa.ldv = qkv_cols;
+  aa.out = m->attn.p;
+  aa.ldo = q_out;
+  aa.bf16 = m->dtype == INL_DTYPE_BF16;
+  aa.hq = c.hq;
+  aa.hkv = c.hkv;
+  aa.d = c.d;
+  aa.scale = 1.0f / std::sqrt(static_cast<float>(c.d));
+  aa.causal = 0;
+  aa.window = -1;
+  aa.cu = m->cu.as<int>();
+  aa.n = b.n;
+  aa.work = m->work.as<int2>();
+  aa.n_work = n_work;
+  aa.q_block = inl::attention_q_block(aa.bf16, c.d);
+  aa.total_rows = b.T;
+  aa.status = m->d_status;
+  return aa;
+}
+
+inl::QkRopeArgs rope_args(inl_model* m, int T, int qkv_cols, bool global) {
+  const ModelConfig& c = m->c;
+  inl::QkRopeArgs qa;
+  qa.qkv = m->qkv.p;
+  qa.bf16 = m->dtype == INL_DTYPE_BF16;
+  qa.ld = qkv_cols;
+  qa.T = T;
+  qa.hq = c.hq;
+  qa.hkv = c.hkv;
+  qa.d = c.d;
+  qa.eps = c.eps;
+  qa.pos = m->pos.as<int>();
+  qa.cos = global ? m->cos0 : m->cos1;
+  qa.sin = global ? m->sin0 : m->sin1;
+  qa.max_pos = c.max_pos;
+  qa.status = m->d_status;
+  return qa;
+}
+
+// ModernBERT tower (crates/inl-sparse/src/modernbert.rs:621-654); leaves the
+// final-normed hidden state in m->h.
+int modernbert_tower(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int T = b.T, H = c.H;
+  const int qkv_cols = 3 * H;
+  cudaStream_t s = m->stream;
+  INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, bf, c.V, H, 1.0f, m->h.p, bf, m->d_status, s),
+            "embedding");
+  INL_K_TRY(inl::layer_norm(m->h.p, bf, H, m->emb_norm, nullptr, c.norm_eps, T, H, m->h.p, bf, H, s),
+            "embedding norm");
+  m->launches += 2;
+  for (int l = 0; l < c.layers; ++l) {
+    const inl::LayerWeights& w = m->layers[l];
+    const bool global = c.layer_global[l] != 0;
+    const void* x = m->h.p;
+    if (w.ln1) {  // layer 0 has no attention norm
+      INL_K_TRY(inl::layer_norm(m->h.p, bf, H, w.ln1, nullptr, c.norm_eps, T, H, m->xn.p, bf, H, s), "attn norm");
+      m->launches++;
+      x = m->xn.p;
+    }
+    INL_K_TRY(linear(m, x, H, w.wqkv, T, qkv_cols, H, bf ? INL_EPI_BF16 : INL_EPI_F32, 0, m->qkv.p, qkv_cols, nullptr,
+                     0, 0),
+              "Wqkv");
+    inl::QkRopeArgs qa = rope_args(m, T, qkv_cols, global);
+    INL_K_TRY(inl::qk_norm_rope(qa, s), "rope");
+    inl::AttnArgs aa = attn_args(m, b, n_work, qkv_cols, H, H);
+    aa.window = global ? -1 : c.local_half_window;
+    INL_K_TRY(inl::attention(aa, s), "attention");
+    m->launches += 2;
+    INL_K_TRY(linear(m, m->attn.p, H, w.wo, T, H, H, INL_EPI_RESID_BF16, 0, m->h.p, H, m->h.p, H, 1), "Wo");
+    INL_K_TRY(inl::layer_norm(m->h.p, bf, H, w.ln2, nullptr, c.norm_eps, T, H, m->xn.p, bf, H, s), "mlp norm");
+    m->launches++;
+    INL_K_TRY(mlp_gated(m, m->xn.p, T, w.wgu, INL_ACT_GELU_ERF, m->qkv.p), "Wi");
+    INL_K_TRY(linear(m, m->qkv.p, c.I, w.wd, T, H, c.I, INL_EPI_RESID_BF16, 0, m->h.p, H, m->h.p, H, 3), "mlp Wo");
+  }
+  INL_K_TRY(inl::layer_norm(m->h.p, bf, H, m->final_norm, nullptr, c.norm_eps, T, H, m->h.p, bf, H, s),
+            "final norm");
+  m->launches++;
+  return INL_OK;
+}
+
+// EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:473-494, 622-647);
+// leaves the last hidden state (before the final norm) in m->h.
+int gemma_tower(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int T = b.T, H = c.H;
+  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv_cols = q_out + 2 * kv_out;
+  cudaStream_t s = m->stream;
+  const int plain = bf ? INL_EPI_BF16 : INL_EPI_F32;
+  INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, bf, c.V, H, c.embed_scale, m->h.p, bf,
+                              m->d_status, s),
+            "embedding");
+  m->launches++;
+  for (int l = 0; l < c.layers; ++l) {
+    const inl::LayerWeights& w = m->layers[l];
+    const bool full = c.layer_global[l] != 0;
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, H, w.ln1, c.eps, T, H, m->xn.p, bf, H, s), "input norm");
+    INL_K_TRY(linear(m, m->xn.p, H, w.wqkv, T, qkv_cols, H, plain, 0, m->qkv.p, qkv_cols, nullptr, 0, 0), "qkv");
+    inl::QkRopeArgs qa = rope_args(m, T, qkv_cols, full);
+    qa.qw = w.qn;
+    qa.kw = w.kn;
+    qa.v_norm = 1;
+    INL_K_TRY(inl::qk_norm_rope(qa, s), "q/k/v norm + rope");
+    inl::AttnArgs aa = attn_args(m, b, n_work, qkv_cols, q_out, kv_out);
+    aa.scale = c.attn_scale;
+    aa.window = full ? -1 : c.sliding_window;
+    INL_K_TRY(inl::attention(aa, s), "attention");
+    m->launches += 3;
+    INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, H, q_out, plain, 0, m->xn.p, H, nullptr, 0, 1), "o projection");
+    INL_K_TRY(inl::add_rms_norm(m->h.p, m->xn.p, bf, w.ln1_post, c.eps, T, H, s), "post-attention norm");
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, H, w.ln2, c.eps, T, H, m->xn.p, bf, H, s), "pre-feedforward norm");
+    m->launches += 2;
+    INL_K_TRY(mlp_gated(m, m->xn.p, T, w.wgu, INL_ACT_GELU_TANH, m->qkv.p), "gate/up projection");
+    INL_K_TRY(linear(m, m->qkv.p, c.I, w.wd, T, H, c.I, plain, 0, m->xn.p, H, nullptr, 0, 3), "down projection");
+    INL_K_TRY(inl::add_rms_norm(m->h.p, m->xn.p, bf, w.ln2_post, c.eps, T, H, s), "post-feedforward norm");
+    m->launches++;
   }
   return INL_OK;
 }
@@ -797,6 +1172,8 @@ int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu,
                  "ids copy");
   switch (m->c.arch) {
     case inl::ARCH_QWEN3: return m->fused ? qwen3_tower_fused(m, b, n_work) : qwen3_tower(m, b, n_work);
+    case inl::ARCH_MODERNBERT: return modernbert_tower(m, b, n_work);
+    case inl::ARCH_GEMMA: return gemma_tower(m, b, n_work);
     default: return fail(INL_ERR_CONFIG, "model_type not built");
   }
 }
@@ -914,7 +1291,8 @@ int inl_cuda_forward_hidden(inl_model* m, const uint32_t* ids, int ids_mem, cons
   const size_t bytes = static_cast<size_t>(b.T) * c.H * 4;
   INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
   const int bf = m->dtype == INL_DTYPE_BF16;
-  if (normalize_final) {
+  // (the ModernBERT tower already ends with its final LayerNorm)
+  if (normalize_final && c.arch != inl::ARCH_MODERNBERT) {
     INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->out.p, 0, c.H, m->stream),
               "final norm");
   } else {
@@ -941,9 +1319,57 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
   if (r) return r;
   if (b.n == 0) return INL_OK;
   if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  if (c.arch == inl::ARCH_MODERNBERT) return fail(INL_ERR_CONFIG, "a ModernBERT MLM model has no dense head");
+  if (c.arch == inl::ARCH_GEMMA) {
+    // final norm -> mean over each text's tokens -> dense chain -> L2 (x / sqrt(sum x^2 + 1e-12))
+    // -> Matryoshka truncation (crates/inl-text/src/gemma2.rs:645-661, native.rs:822-830)
+    const int D = c.dense_dims.empty() ? c.H : c.dense_dims.back();
+    if (out_dim < 0 || out_dim > D) return fail(INL_ERR_CONFIG, "output_dim exceeds the model's embeddings");
+    int widest = c.H;
+    for (int d : c.dense_dims) widest = std::max(widest, d);
+    INL_CUDA_TRY(m->pooled.ensure(static_cast<size_t>(b.n) * widest * 4), "pooling buffer");
+    INL_CUDA_TRY(m->head_buf.ensure(static_cast<size_t>(b.n) * widest * 4), "pooling buffer");
+    INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->xn.p, bf, c.H, m->stream),
+              "final norm");
+    INL_K_TRY(inl::segment_mean(m->xn.p, bf, c.H, m->cu.as<int>(), b.n, c.H, m->pooled.as<float>(), m->stream),
+              "mean pooling");
+    m->launches += 2;
+    float* cur = m->pooled.as<float>();
+    float* nxt = m->head_buf.as<float>();
+    int in = c.H;
+    for (size_t j = 0; j < m->dense_chain.size(); ++j) {
+      inl::GemmF32Args g;
+      g.A = cur;
+      g.lda = in;
+      g.W = m->dense_chain[j];
+      g.ldw = in;
+      g.M = b.n;
+      g.N = c.dense_dims[j];
+      g.K = in;
+      g.epi = INL_EPI_F32;
+      g.out = nxt;
+      g.ldo = c.dense_dims[j];
+      INL_K_TRY(inl::gemm_f32_tn(g, m->stream), "dense head");
+      m->launches++;
+      std::swap(cur, nxt);
+      in = c.dense_dims[j];
+    }
+    INL_K_TRY(inl::rows_l2_f32(cur, D, b.n, D, -1e-12f, cur, D, m->stream), "normalize");
+    m->launches++;
+    const int od = out_dim > 0 ? out_dim : D;
+    const size_t obytes = static_cast<size_t>(b.n) * od * 4;
+    INL_CUDA_TRY(m->out.ensure(obytes), "output buffer");
+    if (out_dim > 0) {
+      INL_K_TRY(inl::truncate_normalize(cur, b.n, D, out_dim, m->out.as<float>(), m->stream), "matryoshka");
+      m->launches++;
+    } else {
+      INL_CUDA_TRY(cudaMemcpyAsync(m->out.p, cur, obytes, cudaMemcpyDeviceToDevice, m->stream), "copy");
+    }
+    return finish(m, m->out.p, obytes, out, out_mem);
+  }
   const size_t bytes = static_cast<size_t>(b.n) * c.H * 4;
   INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
-  const int bf = m->dtype == INL_DTYPE_BF16;
   INL_K_TRY(inl::last_token_norm_l2(m->h.p, bf, c.H, m->cu.as<int>(), b.n, m->final_norm, c.eps, c.H,
                                     m->out.as<float>(), m->stream),
             "last-token pooling");
@@ -979,9 +1405,92 @@ int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int ids_mem,
   return finish(m, m->out.p, bytes, out, out_mem);
 }
 
-int inl_cuda_forward_sparse(inl_model* m, const uint32_t*, int, const int32_t*, int, float*, int) {
+int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
+                            float* out, int out_mem) {
   if (!m) return fail(INL_ERR_CONFIG, "NULL model");
-  return fail(INL_ERR_CONFIG, "this model has no SPLADE head");
+  const ModelConfig& c = m->c;
+  if (c.arch != inl::ARCH_MODERNBERT) return fail(INL_ERR_CONFIG, "this model has no SPLADE head");
+  Batch b;
+  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.n == 0) return INL_OK;
+  if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int H = c.H, V = c.V, n = b.n;
+  cudaStream_t s = m->stream;
+  // Speaking positions: every token whose id is not a prefix id
+  // (Speakers::new, crates/inl-sparse/src/modernbert.rs:703-716), packed with
+  // the index of their text.
+  std::vector<int> idx, seg;
+  idx.reserve(b.T);
+  seg.reserve(b.T);
+  std::vector<uint32_t> host_ids;
+  const uint32_t* hid = ids;
+  if (!c.prefix_ids.empty() && ids_mem == INL_MEM_DEVICE && b.T > 0) {
+    host_ids.resize(b.T);
+    INL_CUDA_TRY(cudaMemcpyAsync(host_ids.data(), m->ids.p, static_cast<size_t>(b.T) * 4, cudaMemcpyDeviceToHost, s),
+                 "ids read-back");
+    INL_CUDA_TRY(cudaStreamSynchronize(s), "ids read-back");
+    hid = host_ids.data();
+  }
+  for (int i = 0; i < n; ++i)
+    for (int t = b.cu_host[i]; t < b.cu_host[i + 1]; ++t) {
+      if (!c.prefix_ids.empty() &&
+          std::find(c.prefix_ids.begin(), c.prefix_ids.end(), static_cast<int>(hid[t])) != c.prefix_ids.end())
+        continue;
+      idx.push_back(t);
+      seg.push_back(i);
+    }
+  const int Ts = static_cast<int>(idx.size());
+  INL_CUDA_TRY(m->pooled_i.ensure(static_cast<size_t>(n) * V * 4), "pooling buffer");
+  INL_K_TRY(inl::fill_i32(m->pooled_i.as<int>(), static_cast<long long>(n) * V, inl::kOrderedNegInf, s), "fill");
+  m->launches++;
+  if (Ts > 0) {
+    INL_CUDA_TRY(m->speak_idx.ensure(static_cast<size_t>(Ts) * 4), "speaker index");
+    INL_CUDA_TRY(m->speak_seg.ensure(static_cast<size_t>(Ts) * 4), "speaker index");
+    INL_CUDA_TRY(m->head_buf.ensure(static_cast<size_t>(Ts) * H * es(m)), "head buffer");
+    INL_CUDA_TRY(cudaMemcpyAsync(m->speak_idx.p, idx.data(), static_cast<size_t>(Ts) * 4, cudaMemcpyHostToDevice, s),
+                 "speaker upload");
+    INL_CUDA_TRY(cudaMemcpyAsync(m->speak_seg.p, seg.data(), static_cast<size_t>(Ts) * 4, cudaMemcpyHostToDevice, s),
+                 "speaker upload");
+    // MLM head on the speaking rows: LN(gelu_erf(dense(h))) (project, :657-662)
+    INL_K_TRY(inl::gather_rows(m->h.p, bf, H, m->speak_idx.as<int>(), Ts, H, m->head_buf.p, s), "gather");
+    m->launches++;
+    INL_K_TRY(linear(m, m->head_buf.p, H, m->head_dense, Ts, H, H, bf ? INL_EPI_BF16 : INL_EPI_F32, 0, m->xn.p, H,
+                     nullptr, 0, 5),
+              "head dense");
+    INL_K_TRY(inl::norm_act(m->xn.p, bf, H, m->head_norm, nullptr, c.norm_eps, Ts, H, m->xn.p, bf, H, s),
+              "head norm");
+    m->launches++;
+    // Tied decoder reduced straight into per-text maxima: the [Ts, V] logits never reach memory.
+    if (bf) {
+      inl::GemmArgs g;
+      g.A = static_cast<const __nv_bfloat16*>(m->embed);  // rows = vocabulary
+      g.lda = H;
+      g.W = m->xn.as<__nv_bfloat16>();  // columns = speaking tokens
+      g.ldw = H;
+      g.M = V;
+      g.N = Ts;
+      g.K = H;
+      g.epi = INL_EPI_SEGMAX;
+      g.seg = m->speak_seg.as<int>();
+      g.pooled = m->pooled_i.as<int>();
+      g.ldp = V;
+      INL_K_TRY(gemm(m, g, 6), "decoder");
+    } else {
+      INL_K_TRY(inl::gemm_f32_segmax(m->xn.as<float>(), H, static_cast<const float*>(m->embed), H, Ts, V, H,
+                                     m->speak_seg.as<int>(), m->pooled_i.as<int>(), V, s),
+                "decoder");
+      m->launches++;
+    }
+  }
+  const size_t bytes = static_cast<size_t>(n) * m->sparse_dim * 4;
+  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  INL_K_TRY(inl::splade_finish(m->pooled_i.as<int>(), n, V, m->decoder_bias, c.logit_shift, m->open_mask, m->canon,
+                               m->sparse_dim, m->out.as<float>(), s),
+            "splade finish");
+  m->launches++;
+  return finish(m, m->out.p, bytes, out, out_mem);
 }
 
 int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
@@ -992,9 +1501,9 @@ int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
   out->hidden_size = m->c.H;
   out->num_layers = m->c.layers;
   out->vocab_size = m->c.V;
-  out->dense_dim = m->c.H;
+  out->dense_dim = (m->c.arch == inl::ARCH_GEMMA && !m->c.dense_dims.empty()) ? m->c.dense_dims.back() : m->c.H;
   out->multivector_dim = m->proj_out;
-  out->sparse_dim = 0;
+  out->sparse_dim = m->sparse_dim;
   out->max_text_tokens = m->c.max_pos;
   out->is_causal = m->c.causal ? 1 : 0;
   return INL_OK;
@@ -1006,7 +1515,7 @@ void inl_cuda_model_destroy(inl_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (void* p : m->allocs) cudaFree(p);
   for (DevBuf* d : {&m->h, &m->xn, &m->qkv, &m->attn, &m->ids, &m->cu, &m->pos, &m->work, &m->out, &m->pooled,
-                    &m->tmp, &m->ss_a, &m->ss_b})
+                    &m->tmp, &m->ss_a, &m->ss_b, &m->speak_idx, &m->speak_seg, &m->pooled_i, &m->head_buf})
     d->release();
   for (auto& r : m->prof) {
     cudaEventDestroy(r.start);

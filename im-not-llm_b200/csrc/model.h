@@ -40,6 +40,10 @@ struct ModelConfig {
   float attn_scale = 0.f;  // 0 = head_dim^-1/2
   float embed_scale = 1.f;
   std::vector<int> dense_dims;  // Gemma-style projection chain after pooling
+  std::vector<char> layer_global;  // per layer: global / full attention (1) or local / sliding (0)
+  // SPLADE pooling (ModernBERT MLM head)
+  bool decoder_bias = true;
+  std::vector<int> prefix_ids, masked_vocab_ids, canonical_ids;
 };
 
 struct TensorSrc {
@@ -132,12 +136,18 @@ struct inl_model {
   void* head_dense = nullptr;
   float* head_norm = nullptr;
   float* decoder_bias = nullptr;
-  // Gemma-style dense chain (f32 or bf16 weights) after pooling
-  std::vector<void*> dense_chain;
+  // Gemma-style dense chain (f32 weights) after pooling: dense_chain[j] is [dense_dims[j], in]
+  std::vector<float*> dense_chain;
+  // SPLADE device tables
+  float* open_mask = nullptr;  // [V] 1 / 0
+  int* canon = nullptr;        // [V] canonical term or null
+  int sparse_dim = 0;
   // workspaces
   inl::DevBuf h, xn, qkv, attn, ids, cu, pos, work, out, pooled, tmp;
   inl::DevBuf ss_a, ss_b;  // per-64-column sums of squares of h (folded RMSNorm)
+  inl::DevBuf speak_idx, speak_seg, pooled_i, head_buf;  // SPLADE head scratch
   bool fused = false;      // bf16 fused layer (folded norms, QKV epilogue)
+  bool gated_split = false;  // gate/up stored [gate; up] (intermediate not a multiple of gate_block)
   int* h_stage = nullptr;  // pinned staging for cu + work list
   size_t h_stage_bytes = 0;
   // profiling / launch accounting

@@ -9,6 +9,10 @@
 * ``LateEncoder`` — the LateEngine contract (crates/inl-late/src/lib.rs:38-55;
   encode path crates/inl-late/src/native.rs:317-374,631-683): longest-first
   planning, per-token vectors, non-finite output is an error.
+* ``SparseEncoder`` — the SparseEngine contract (crates/inl-sparse/src/lib.rs:236-252;
+  encode path crates/inl-sparse/src/native.rs:349-544): longest-first packed
+  batches, ``SparseVector`` results (positive weights only, sorted term ids),
+  non-finite output is an error.
 * ``DataParallelEmbedder`` — one model per GPU, one host thread per GPU,
   packed batches assigned longest-processing-time first; no collective.
 
@@ -226,6 +230,50 @@ class LateEncoder(_EngineBase):
             return [flat[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
 
         return self._run_batches("native late", texts, forward)
+
+
+class SparseVector:
+    """Sorted term ids with positive weights (SparseVector::from_pairs,
+    crates/inl-sparse/src/lib.rs:51-62: pairs with weight <= 0 are dropped)."""
+
+    __slots__ = ("indices", "values")
+
+    def __init__(self, indices: np.ndarray, values: np.ndarray):
+        self.indices = indices
+        self.values = values
+
+    @classmethod
+    def from_dense(cls, row: np.ndarray) -> "SparseVector":
+        idx = np.nonzero(row > 0)[0].astype(np.uint32)
+        return cls(idx, row[idx].astype(np.float32))
+
+    def dot(self, other: "SparseVector") -> float:
+        """dot_terms (crates/inl-sparse/src/lib.rs:64-90)."""
+        common, ia, ib = np.intersect1d(self.indices, other.indices, assume_unique=True, return_indices=True)
+        return float(np.dot(self.values[ia], other.values[ib])) if len(common) else 0.0
+
+    def __len__(self) -> int:
+        return len(self.indices)
+
+
+class SparseEncoder(_EngineBase):
+    """SparseEngine over a ModernBERT + SPLADE CudaModel."""
+
+    def load(self) -> EngineInfo:
+        m = self._model().model
+        return EngineInfo(self.options.id, m.info()["sparse_dim"], m.dtype, f"cuda:{m.device}", "fused",
+                          self.options.max_length)
+
+    def encode(self, tokens: Sequence[Sequence[int]]) -> list[SparseVector]:
+        texts = _truncate(tokens, self.options.max_length)
+
+        def forward(model: CudaModel, ids, cu):
+            dense = model.encode_sparse(ids, cu)
+            if not np.all(np.isfinite(dense)):  # crates/inl-sparse/src/native.rs:536-540
+                raise InlError.inference("native sparse encoder produced non-finite weights")
+            return [SparseVector.from_dense(row) for row in dense]
+
+        return self._run_batches("native sparse", texts, forward)
 
 
 class DataParallelEmbedder:

@@ -95,11 +95,23 @@ class CudaModel:
         ids, ids_mem, cu = self._inputs(ids, cu_seqlens)
         n = len(cu) - 1
         if out is None:
-            out = np.empty((n, out_dim or self.config["hidden_size"]), dtype=np.float32)
+            out = np.empty((n, out_dim or self.info()["dense_dim"]), dtype=np.float32)
         optr, omem = _ptr(out)
         iptr = ids if isinstance(ids, int) else ids.ctypes.data
         N.check(N.lib().inl_cuda_forward_dense(self.handle, iptr, ids_mem, cu.ctypes.data, n, out_dim, optr, omem),
                 "dense forward")
+        return out
+
+    def encode_sparse(self, ids, cu_seqlens, out=None) -> np.ndarray | int:
+        """SPLADE term weights, one dense row per text [n, sparse_dim] f32."""
+        ids, ids_mem, cu = self._inputs(ids, cu_seqlens)
+        n = len(cu) - 1
+        if out is None:
+            out = np.empty((n, self.info()["sparse_dim"]), dtype=np.float32)
+        optr, omem = _ptr(out)
+        iptr = ids if isinstance(ids, int) else ids.ctypes.data
+        N.check(N.lib().inl_cuda_forward_sparse(self.handle, iptr, ids_mem, cu.ctypes.data, n, optr, omem),
+                "sparse forward")
         return out
 
     def encode_multivector(self, ids, cu_seqlens, out=None) -> np.ndarray | int:

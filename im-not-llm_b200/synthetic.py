@@ -48,6 +48,56 @@ QWEN3_TINY_D64 = dict(QWEN3_TINY, hidden_size=192, num_attention_heads=6, num_ke
 
 LATE_PROJ_OUT = 128
 
+# Config 2: ModernBERT-style SPLADE encoder (KURE-Sparse-nano shapes, BASELINE vocabulary).
+# The benchmark config pins: V = 36282 tied decoder with a zero-initialised
+# decoder bias, logit shift 0, no prefix tokens, no vocabulary mask, no fold.
+MODERNBERT_SPLADE = {
+    "model_type": "modernbert",
+    "vocab_size": 36282,
+    "hidden_size": 768,
+    "intermediate_size": 1152,
+    "num_hidden_layers": 22,
+    "num_attention_heads": 12,
+    "norm_eps": 1e-5,
+    "local_attention": 128,
+    "global_attn_every_n_layers": 3,
+    "global_rope_theta": 160000.0,
+    "local_rope_theta": 10000.0,
+    "max_position_embeddings": 8192,
+    "decoder_bias": True,
+    "splade": {"logit_shift": 0.0},
+}
+MODERNBERT_TINY = dict(MODERNBERT_SPLADE, vocab_size=1000, hidden_size=256, intermediate_size=384,
+                       num_hidden_layers=4, num_attention_heads=4, local_attention=32,
+                       splade={"logit_shift": 0.05, "prefix_token_ids": [5], "masked_vocab_ids": [7, 9],
+                               "canonical_ids": [v % 900 for v in range(1000)]})
+
+# Config 4: EmbeddingGemma-style text tower (BASELINE shapes); per-layer
+# embeddings and layer scalars dropped, embedding_projection replaced by the
+# dense 768 -> 3072 -> 768 chain.
+GEMMA_STYLE = {
+    "model_type": "gemma_style",
+    "vocab_size": 262144,
+    "hidden_size": 768,
+    "intermediate_size": 1152,
+    "num_hidden_layers": 24,
+    "num_attention_heads": 3,
+    "num_key_value_heads": 1,
+    "head_dim": 256,
+    "rms_norm_eps": 1e-6,
+    "sliding_window": 512,
+    "full_attention_every_n_layers": 6,
+    "rope_theta": 1_000_000.0,
+    "rope_local_base_freq": 10_000.0,
+    "hidden_activation": "gelu_pytorch_tanh",
+    "dense_dims": [3072, 768],
+    "max_position_embeddings": 8192,
+}
+GEMMA_TINY = dict(GEMMA_STYLE, vocab_size=1000, hidden_size=256, intermediate_size=384, num_hidden_layers=4,
+                  num_attention_heads=2, num_key_value_heads=1, head_dim=128, sliding_window=40,
+                  full_attention_every_n_layers=2, dense_dims=[512, 256])
+MATRYOSHKA_DIMS = (128, 256, 512, 768)
+
 
 @dataclass
 class Spec:
@@ -80,13 +130,63 @@ def qwen3_specs(cfg: dict) -> list[Spec]:
     return specs
 
 
+def modernbert_specs(cfg: dict) -> list[Spec]:
+    """Tensor names of crates/inl-sparse/src/modernbert.rs:469-520 (decoder tied)."""
+    H, I, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    specs = [Spec("model.embeddings.tok_embeddings.weight", (V, H), "linear"),
+             Spec("model.embeddings.norm.weight", (H,), "norm")]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        if i > 0:
+            specs.append(Spec(p + "attn_norm.weight", (H,), "norm"))
+        specs += [Spec(p + "attn.Wqkv.weight", (3 * H, H), "linear"), Spec(p + "attn.Wo.weight", (H, H), "linear"),
+                  Spec(p + "mlp_norm.weight", (H,), "norm"), Spec(p + "mlp.Wi.weight", (2 * I, H), "linear"),
+                  Spec(p + "mlp.Wo.weight", (H, I), "linear")]
+    specs += [Spec("model.final_norm.weight", (H,), "norm"), Spec("head.dense.weight", (H, H), "linear"),
+              Spec("head.norm.weight", (H,), "norm"), Spec("decoder.bias", (V,), "zero")]
+    return specs
+
+
+def gemma_specs(cfg: dict) -> list[Spec]:
+    """Tensor names of crates/inl-text/src/gemma2.rs:233-494 (no PLE, no layer
+    scalar) plus the dense head chain ``dense_head.<j>.weight``."""
+    H, I, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    hq, hkv, d = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    specs = [Spec("embed_tokens.weight", (V, H), "linear")]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"layers.{i}."
+        specs += [
+            Spec(p + "self_attn.q_proj.weight", (hq * d, H), "linear"),
+            Spec(p + "self_attn.k_proj.weight", (hkv * d, H), "linear"),
+            Spec(p + "self_attn.v_proj.weight", (hkv * d, H), "linear"),
+            Spec(p + "self_attn.o_proj.weight", (H, hq * d), "linear"),
+            Spec(p + "self_attn.q_norm.weight", (d,), "norm"),
+            Spec(p + "self_attn.k_norm.weight", (d,), "norm"),
+            Spec(p + "mlp.gate_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.up_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.down_proj.weight", (H, I), "linear"),
+            Spec(p + "input_layernorm.weight", (H,), "norm"),
+            Spec(p + "post_attention_layernorm.weight", (H,), "norm"),
+            Spec(p + "pre_feedforward_layernorm.weight", (H,), "norm"),
+            Spec(p + "post_feedforward_layernorm.weight", (H,), "norm"),
+        ]
+    specs.append(Spec("norm.weight", (H,), "norm"))
+    prev = H
+    for j, out in enumerate(cfg.get("dense_dims", [])):
+        specs.append(Spec(f"dense_head.{j}.weight", (out, prev), "linear"))
+        prev = out
+    return specs
+
+
 def generate(specs: list[Spec], seed: int = 0, std: float = 0.02, norm_jitter: float = 0.0) -> dict:
     """Draw every tensor of ``specs`` in order from one PCG64 stream."""
     rng = np.random.default_rng(seed)
     out = {}
     for s in specs:
         n = int(np.prod(s.shape))
-        if s.kind == "norm":
+        if s.kind == "zero":
+            v = np.zeros(n, dtype=np.float32)
+        elif s.kind == "norm":
             if norm_jitter > 0:
                 v = 1.0 + norm_jitter * rng.standard_normal(n, dtype=np.float32)
             else:
@@ -100,6 +200,14 @@ def generate(specs: list[Spec], seed: int = 0, std: float = 0.02, norm_jitter: f
 
 def qwen3_weights(cfg: dict = QWEN3_0_6B, seed: int = 0, norm_jitter: float = 0.0) -> dict:
     return generate(qwen3_specs(cfg), seed=seed, norm_jitter=norm_jitter)
+
+
+def modernbert_weights(cfg: dict = MODERNBERT_SPLADE, seed: int = 0, norm_jitter: float = 0.0) -> dict:
+    return generate(modernbert_specs(cfg), seed=seed, norm_jitter=norm_jitter)
+
+
+def gemma_weights(cfg: dict = GEMMA_STYLE, seed: int = 0, norm_jitter: float = 0.0) -> dict:
+    return generate(gemma_specs(cfg), seed=seed, norm_jitter=norm_jitter)
 
 
 def late_projection(cfg: dict = QWEN3_0_6B, out: int = LATE_PROJ_OUT, seed: int = 0) -> np.ndarray:
@@ -145,5 +253,23 @@ def random_texts(n: int, lo: int, hi: int, vocab: int, seed: int):
     """Ragged test inputs: lengths uniform in [lo, hi], ids uniform."""
     rng = np.random.default_rng(seed)
     lengths = rng.integers(lo, hi + 1, size=n)
+    ids = rng.integers(0, vocab, size=int(lengths.sum()))
+    return packed(lengths, ids)
+
+
+def cfg2_inputs(vocab: int = MODERNBERT_SPLADE["vocab_size"]):
+    """Config 2: 32 texts, lengths uniform in [16, 256], ids uniform; default_rng(2)
+    draws the lengths then the ids."""
+    rng = np.random.default_rng(2)
+    lengths = rng.integers(16, 257, size=32)
+    ids = rng.integers(0, vocab, size=int(lengths.sum()))
+    return packed(lengths, ids)
+
+
+def cfg4_inputs(vocab: int = GEMMA_STYLE["vocab_size"], n_texts: int = 128):
+    """Config 4: lengths log-uniform in [32, 2048] (round(exp(U(ln 32, ln 2048)))),
+    ids uniform; default_rng(4) draws the lengths then the ids."""
+    rng = np.random.default_rng(4)
+    lengths = np.rint(np.exp(rng.uniform(math.log(32.0), math.log(2048.0), size=n_texts))).astype(np.int64)
     ids = rng.integers(0, vocab, size=int(lengths.sum()))
     return packed(lengths, ids)
