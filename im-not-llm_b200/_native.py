@@ -32,6 +32,7 @@ EXPORTED = (
     "inl_cuda_attention", "inl_cuda_model_set_profiling", "inl_cuda_model_profile",
     "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
     "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2", "inl_cuda_gemm_bf16_ex",
+    "inl_cuda_attention_noalloc",
 )
 
 
@@ -86,6 +87,9 @@ def _declare(lib: ctypes.CDLL) -> None:
                                       c_void_p, c_i64, c_void_p, c_i64, c_void_p]),
         "inl_cuda_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,
                                        c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int, c_void_p]),
+        "inl_cuda_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p, c_i64,
+                                               c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int,
+                                               c_void_p]),
         "inl_cuda_model_set_profiling": (c_int, [c_void_p, c_int]),
         "inl_cuda_model_profile": (c_int, [c_void_p, c_int, P(c_int), P(c_double), P(c_double)]),
         "inl_cuda_model_launch_count": (ctypes.c_longlong, [c_void_p, c_int]),

@@ -1682,6 +1682,16 @@ int inl_cuda_gemm_f32(const float* A, int64_t lda, const float* W, int64_t ldw, 
   return INL_OK;
 }
 
+}  // extern "C"
+
+namespace inl {
+// Sets the message inl_cuda_last_error returns on this thread; for entry
+// points defined in other translation units.
+int record_error(int code, const std::string& msg) { return fail(code, msg); }
+}  // namespace inl
+
+extern "C" {
+
 static int hook_status(int r, const char* what) {
   if (r == -1) return fail(INL_ERR_INVALID_INPUT, std::string(what) + ": unsupported arguments");
   if (r != 0) return fail(INL_ERR_INFERENCE, std::string(what) + " launch failed");

@@ -92,6 +92,26 @@ INL_API int inl_cuda_attention(const void* q, const void* k, const void* v, int6
                        int64_t ldo, int dtype, int hq, int hkv, int d, float scale, int causal, int window,
                        const int32_t* cu_seqlens_host, int n_texts, void* stream);
 
+/* inl_cuda_attention for callers that must not allocate device memory (a host
+ * whose pool allocator owns the GPU's memory, or code where a cudaMalloc or
+ * cudaFree would synchronise the device or be refused). No counterpart in the
+ * reference, which always allocates through candle. Same arguments, meaning
+ * and results as inl_cuda_attention; it calls no cudaMalloc, cudaFree or other
+ * allocating routine. Its state (cu_seqlens copy, work list, status word)
+ * lives in one file-scope device array of 288.5 KiB that every GPU loading the
+ * library holds until exit, so a call takes at most 8192 texts and 32768
+ * query blocks (a block is 128 query rows for bf16 head_dim 64/128, 64 for
+ * bf16 head_dim 256, 32 for f32); larger calls return INL_ERR_INVALID_INPUT. The
+ * first call on each device looks up the array's device address with that
+ * device current; make that first call before any stream capture. All calls
+ * share the array and would race if they overlapped on the GPU, so each call
+ * holds a process-wide lock until its stream has drained. A bounded device
+ * wait that runs out returns INL_ERR_TIMEOUT. */
+INL_API int inl_cuda_attention_noalloc(const void* q, const void* k, const void* v, int64_t ldq, int64_t ldk,
+                                       int64_t ldv, void* out, int64_t ldo, int dtype, int hq, int hkv, int d,
+                                       float scale, int causal, int window, const int32_t* cu_seqlens_host,
+                                       int n_texts, void* stream);
+
 /* Row gather table[ids[t]] * scale -> out [T, H]; dtypes INL_DTYPE_*. An id
  * >= vocab writes zeros and sets *status. Replaces candle's Embedding::forward
  * (index_select) at crates/inl-text/src/qwen3/mod.rs:352. */
