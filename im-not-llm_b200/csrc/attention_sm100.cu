@@ -2,20 +2,34 @@
 // texts (bf16, head_dim 64 or 128): causal, bidirectional and sliding-window
 // masks computed from positions, grouped-query heads by index.
 //
-// One CTA = one (text, 128-query tile, query head), 192 threads:
-//   warp 0      TMA: the Q tile once, then K_j / V_j tiles of 128 keys into a
-//               2-stage ring (kv_full / kv_empty);
-//   warp 1      allocates TMEM and issues tcgen05.mma: S_j = Q K_j^T into one of
-//               two TMEM score buffers (128 columns each), and O += P_j V_j into
-//               the TMEM output (D columns); S_{j+1} is issued before PV_j so
-//               the tensor core works while the softmax warps read S_j;
-//   warps 2..5  softmax: thread = query row = TMEM lane. Reads S_j with
-//               tcgen05.ld, masks, keeps a running row max m and sum l,
-//               writes P_j = exp2(s - m) as bf16 into shared memory in the
-//               K-major 128-byte-swizzle layout the MMA reads. m is only
-//               raised when the block max exceeds it by more than 2^8, and then
-//               O is rescaled in TMEM (tcgen05.ld/st), so the common block
-//               needs no O round trip. Finally O / l is written as bf16.
+// Persistent: one CTA per SM walks the tiles blockIdx.x, blockIdx.x +
+// gridDim.x, ... of the list (work item, query head), work items heaviest
+// first and the heads of one item adjacent (their K / V rows meet in L2). A
+// tile is 128 queries of one text and one head. The CTA runs two tile slots
+// side by side (its even tiles in slot 0, odd tiles in slot 1); each slot owns
+// a Q and a P buffer in shared memory and, in TMEM, a score buffer S (128
+// columns) and an output accumulator O (D columns): 2 x 256 of the 512
+// columns. 320 threads:
+//   warp 0     TMA producer: each slot's Q tile, and K / V tiles of 128 keys
+//              into one ring, in exactly the order the MMA warp consumes them
+//              (so the ring can neither deadlock nor reorder);
+//   warp 1     TMEM allocation and tcgen05.mma issue. It alternates between
+//              the slots in units "O += P(j-1) V(j-1); S = Q K(j)^T", so the
+//              tensor core works on one slot while the other slot's softmax
+//              warps compute, and one slot's tile epilogue overlaps the other
+//              slot's blocks;
+//   warps 2-5  softmax of slot 0, warps 6-9 of slot 1: thread = query row =
+//              TMEM lane. Reads S with tcgen05.ld, masks, keeps a running row
+//              max m and sum l, writes P = exp2(s - m) as bf16 into shared
+//              memory in the K-major 128-byte-swizzle layout the MMA reads. m
+//              is only raised when the block max exceeds it by more than 2^8,
+//              and then O is rescaled in TMEM. At the end of a tile, O / l is
+//              written as bf16.
+// tcgen05.commit tracks every MMA issued before it, so the arrival of S(j)
+// also means PV(j-1) is complete: P's buffer may be rewritten and O rescaled
+// without more barriers, and the first PV of a slot's next tile (which
+// overwrites O) is issued only after that slot's softmax warps, having read O
+// for the epilogue, delivered the next P.
 // Every mbarrier wait is bounded (status word + early exit, TMEM freed).
 #include "common.cuh"
 #include "kernels.h"
@@ -27,17 +41,18 @@ namespace {
 constexpr int kTQ = 128;   // queries per tile (UMMA M)
 constexpr int kTK = 128;   // keys per block (UMMA N of S, K of PV)
 constexpr int kBox = 16384;  // one TMA box: 128 rows x 128 bytes
+constexpr int kFaThreads = 320;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows 256x
 
 template <int D>
 struct FaCfg {
-  static constexpr int QB = D / 64;  // 64-column boxes per head row
-  static constexpr int Q_BYTES = QB * kBox;
-  static constexpr int KV_BYTES = QB * kBox;
-  static constexpr int P_BYTES = 2 * kBox;  // 128 keys = two 64-key boxes
-  static constexpr int SMEM = Q_BYTES + 4 * KV_BYTES + 2 * P_BYTES + 1024 + 256;
+  static constexpr int QB = D / 64;              // 64-column boxes per head row
+  static constexpr int TILE_BYTES = QB * kBox;   // one Q, K or V tile of 128 rows
+  static constexpr int P_BYTES = 2 * kBox;       // 128 keys = two 64-key boxes
+  static constexpr int NS = D == 128 ? 3 : 8;    // K / V ring slots
+  static constexpr int SMEM = 2 * TILE_BYTES + 2 * P_BYTES + NS * TILE_BYTES + 1024 + 256;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int O_COL = 2 * kTK;
+  static constexpr int SLOT_COLS = 256;          // S at +0, O at +128
 };
 
 struct FaParams {
@@ -45,10 +60,83 @@ struct FaParams {
   const int2* work;
   __nv_bfloat16* out;
   long long ldo;
-  int hq, hkv;
+  int hq, hkv, n_tiles;
   float scale_log2;
   int causal, window;
   int* status;
+};
+
+struct TileInfo {
+  int s0, L, q0, head, kvh, kb_lo, n_kv;
+};
+
+__device__ __forceinline__ bool load_tile(const FaParams& p, int t, TileInfo& ti) {
+  if (t >= p.n_tiles) return false;
+  const int item = t / p.hq;
+  ti.head = t - item * p.hq;
+  ti.kvh = ti.head / (p.hq / p.hkv);
+  const int2 wk = p.work[item];
+  ti.s0 = p.cu[wk.x];
+  ti.L = p.cu[wk.x + 1] - ti.s0;
+  ti.q0 = wk.y * kTQ;
+  int k_lo = 0, k_hi = ti.L;
+  if (p.causal) k_hi = min(ti.L, ti.q0 + kTQ);
+  if (p.window >= 0) {
+    k_lo = max(0, ti.q0 - p.window);
+    k_hi = min(k_hi, ti.q0 + kTQ + p.window);
+  }
+  ti.kb_lo = k_lo / kTK;
+  ti.n_kv = ti.q0 < ti.L ? (k_hi + kTK - 1) / kTK - ti.kb_lo : 0;
+  return true;
+}
+
+// The CTA's tile of ordinal k (k = slot, slot + 2, ...), skipping tiles
+// without key blocks; false when the slot has no more tiles.
+__device__ __forceinline__ bool next_tile(const FaParams& p, int& k, TileInfo& ti) {
+  while (load_tile(p, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x), ti)) {
+    if (ti.n_kv > 0) return true;
+    k += 2;
+  }
+  return false;
+}
+
+// The sequence of MMA units of one slot, walked identically by the producer
+// and the MMA warp: unit u issues PV of the slot's S op u-1 (if any) and S op
+// u (if any); S ops run over the slot's tiles and their key blocks in order.
+struct SlotSeq {
+  TileInfo ti;
+  int k, j;          // current tile ordinal, next key block in it
+  int tiles, ops;    // tiles whose Q was taken, S ops done
+  int pv_row, pv_kvh;
+  bool has, pv, pv_first, pv_last;
+
+  __device__ __forceinline__ void init(const FaParams& p, int slot) {
+    k = slot;
+    j = 0;
+    tiles = ops = 0;
+    pv = false;
+    has = next_tile(p, k, ti);
+  }
+  __device__ __forceinline__ bool live() const { return has || pv; }
+  __device__ __forceinline__ int row() const { return ti.s0 + (ti.kb_lo + j) * kTK; }
+  // The S op of this unit becomes the next unit's PV.
+  __device__ __forceinline__ void advance(const FaParams& p) {
+    if (!has) {
+      pv = false;
+      return;
+    }
+    pv = true;
+    pv_row = row();
+    pv_kvh = ti.kvh;
+    pv_first = j == 0;
+    pv_last = j == ti.n_kv - 1;
+    ++ops;
+    if (++j == ti.n_kv) {
+      j = 0;
+      k += 2;
+      has = next_tile(p, k, ti);
+    }
+  }
 };
 
 __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, int* status, int code, bool& ok) {
@@ -68,55 +156,77 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, int* s
   return ok;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// (d0, d1) = (a0, a1) * (b, b) + (c, c) as one packed f32x2 FMA.
+__device__ __forceinline__ void fma2_bcast(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// (s0, s1) += (a0, a1) as one packed f32x2 add.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rs;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rs, {%0, %1};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+
+// Columns c of a 128-key block outside [lo, hi) become -inf (lo, hi per row).
+template <int N>
+__device__ __forceinline__ void mask_range(uint32_t (&sv)[N], int c0, int lo, int hi) {
+#pragma unroll
+  for (int c = 0; c < N; ++c)
+    if (c0 + c < lo || c0 + c >= hi) sv[c] = __float_as_uint(-INFINITY);
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kFaThreads, 1)
     fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, FaParams p) {
   using C = FaCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C::Q_BYTES;            // 2 stages
-  uint8_t* sV = sK + 2 * C::KV_BYTES;       // 2 stages
-  uint8_t* sP = sV + 2 * C::KV_BYTES;       // 2 buffers
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 7;
-  uint64_t* p_full = bars + 9;
-  uint64_t* p_free = bars + 11;
-  uint64_t* o_done = bars + 13;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  uint8_t* sQ = smem;                          // 2 slots
+  uint8_t* sP = sQ + 2 * C::TILE_BYTES;        // 2 slots
+  uint8_t* ring = sP + 2 * C::P_BYTES;         // NS K / V tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + C::NS * C::TILE_BYTES);
+  uint64_t* q_full = bars;          // [2]
+  uint64_t* q_empty = bars + 2;     // [2]
+  uint64_t* s_full = bars + 4;      // [2]
+  uint64_t* p_full = bars + 6;      // [2]
+  uint64_t* o_full = bars + 8;      // [2]
+  uint64_t* mma_done = bars + 10;
+  uint64_t* ring_full = bars + 11;  // [NS]
+  uint64_t* ring_empty = ring_full + C::NS;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ring_empty + C::NS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int2 wk = p.work[blockIdx.x];
-  const int head = blockIdx.y;
-  const int kvh = head / (p.hq / p.hkv);
-  const int s0 = p.cu[wk.x];
-  const int L = p.cu[wk.x + 1] - s0;
-  const int q0 = wk.y * kTQ;
-  if (q0 >= L) return;  // uniform for the CTA
-  int k_lo = 0, k_hi = L;
-  if (p.causal) k_hi = min(L, q0 + kTQ);
-  if (p.window >= 0) {
-    k_lo = max(0, q0 - p.window);
-    k_hi = min(k_hi, q0 + kTQ + p.window);
-  }
-  const int kb_lo = k_lo / kTK;
-  const int n_kv = (k_hi + kTK - 1) / kTK - kb_lo;  // >= 1 because q0 < L
-
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&p_free[i], 1);
-      mbar_init(&o_done[i], 1);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 1);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -135,183 +245,243 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // Q tile: rows s0 + q0 .. +127, columns head*D .. +D.
-      mbar_expect_tx(q_full, C::Q_BYTES);
-      for (int b = 0; b < C::QB; ++b) tma_load_2d(sQ + b * kBox, &tmQ, q_full, head * D + b * 64, s0 + q0);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!wait_or_flag(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, INL_DEV_TIMEOUT_PRODUCER, ok)) break;
-        mbar_expect_tx(&kv_full[st], 2 * C::KV_BYTES);
-        const int row = s0 + (kb_lo + j) * kTK;
-        for (int b = 0; b < C::QB; ++b) {
-          tma_load_2d(sK + st * C::KV_BYTES + b * kBox, &tmK, &kv_full[st], kvh * D + b * 64, row);
-          tma_load_2d(sV + st * C::KV_BYTES + b * kBox, &tmV, &kv_full[st], kvh * D + b * 64, row);
+      SlotSeq sq0, sq1;
+      sq0.init(p, 0);
+      sq1.init(p, 1);
+      int g = 0;  // ring loads issued
+      auto ring_load = [&](const CUtensorMap* map, int row, int kvh) -> bool {
+        const int r = g % C::NS;
+        if (!wait_or_flag(&ring_empty[r], ((g / C::NS) & 1) ^ 1, p.status, INL_DEV_TIMEOUT_PRODUCER, ok))
+          return false;
+        mbar_expect_tx(&ring_full[r], C::TILE_BYTES);
+        for (int b = 0; b < C::QB; ++b)
+          tma_load_2d(ring + r * C::TILE_BYTES + b * kBox, map, &ring_full[r], kvh * D + b * 64, row);
+        ++g;
+        return true;
+      };
+      auto unit = [&](SlotSeq& q, const int s) {
+        if (!q.live() || !ok) return;
+        if (q.pv && !ring_load(&tmV, q.pv_row, q.pv_kvh)) return;
+        if (q.has) {
+          if (q.j == 0) {
+            if (q.tiles > 0 &&
+                !wait_or_flag(&q_empty[s], (q.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_PRODUCER, ok))
+              return;
+            mbar_expect_tx(&q_full[s], C::TILE_BYTES);
+            for (int b = 0; b < C::QB; ++b)
+              tma_load_2d(sQ + s * C::TILE_BYTES + b * kBox, &tmQ, &q_full[s], q.ti.head * D + b * 64,
+                          q.ti.s0 + q.ti.q0);
+            ++q.tiles;
+          }
+          if (!ring_load(&tmK, q.row(), q.ti.kvh)) return;
         }
-        ++issued;
+        q.advance(p);
+      };
+      while (ok && (sq0.live() || sq1.live())) {
+        unit(sq0, 0);
+        unit(sq1, 1);
       }
-      // drain: the Q copy and the last two K/V fills must land before exit
+      // Drain: every copy still in flight must land before the CTA exits.
       bool dok = true;
-      wait_or_flag(q_full, 0, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        if (!dok) break;
-        wait_or_flag(&kv_full[j & 1], (j >> 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
-      }
+      if (sq0.tiles > 0) wait_or_flag(&q_full[0], (sq0.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
+      if (sq1.tiles > 0) wait_or_flag(&q_full[1], (sq1.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
+      for (int i = max(0, g - C::NS); i < g; ++i)
+        wait_or_flag(&ring_full[i % C::NS], (i / C::NS) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kTQ, kTK, 0);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kTQ, D, 1);
-      const uint32_t q_addr = smem_u32(sQ);
-      wait_or_flag(q_full, 0, p.status, INL_DEV_TIMEOUT_MMA, ok);
-      for (int j = 0; j <= n_kv && ok; ++j) {
-        if (j < n_kv) {
-          const int st = j & 1, sb = j & 1;
-          if (!wait_or_flag(&kv_full[st], (j >> 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) break;
-          if (!wait_or_flag(&s_free[sb], ((j >> 1) & 1) ^ 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) break;
+      SlotSeq sq0, sq1;
+      sq0.init(p, 0);
+      sq1.init(p, 1);
+      int g = 0;  // ring tiles consumed
+      auto unit = [&](SlotSeq& q, const int s) {
+        if (!q.live() || !ok) return;
+        const uint32_t t_s = tmem + s * C::SLOT_COLS, t_o = t_s + kTK;
+        if (q.pv) {
+          if (!wait_or_flag(&p_full[s], (q.ops - 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+          const int r = g % C::NS;
+          if (!wait_or_flag(&ring_full[r], (g / C::NS) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * C::KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-            umma_bf16(tmem + sb * kTK, sw128_kmajor_desc(q_addr + off), sw128_kmajor_desc(k_addr + off), idesc_s,
-                      kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[sb]);
-        }
-        if (j >= 1) {
-          const int i = j - 1;
-          const int st = i & 1, pb = i & 1;
-          if (!wait_or_flag(&p_full[pb], (i >> 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) break;
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + pb * C::P_BYTES);
-          const uint32_t v_addr = smem_u32(sV + st * C::KV_BYTES);
+          const uint32_t p_addr = smem_u32(sP + s * C::P_BYTES);
+          const uint32_t v_addr = smem_u32(ring + r * C::TILE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < kTK / 16; ++kk) {
             const uint32_t a_off = (kk >> 2) * kBox + (kk & 3) * 32;  // P: K-major, 64 keys per box
             const uint32_t b_off = kk * 16 * 128;                      // V: 16 key rows per step
-            umma_bf16(tmem + C::O_COL, sw128_kmajor_desc(p_addr + a_off), sw128_mnmajor_desc(v_addr + b_off, kBox),
-                      idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(t_o, sw128_kmajor_desc(p_addr + a_off), sw128_mnmajor_desc(v_addr + b_off, kBox), idesc_o,
+                      (!q.pv_first || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&o_done[i & 1]);
-          umma_commit(&kv_empty[st]);
-          umma_commit(&p_free[pb]);
+          umma_commit(&ring_empty[r]);
+          ++g;
+          if (q.pv_last) umma_commit(&o_full[s]);
         }
+        if (q.has) {
+          if (q.j == 0) {
+            if (!wait_or_flag(&q_full[s], q.tiles & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+            ++q.tiles;
+          }
+          const int r = g % C::NS;
+          if (!wait_or_flag(&ring_full[r], (g / C::NS) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sQ + s * C::TILE_BYTES);
+          const uint32_t k_addr = smem_u32(ring + r * C::TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+            umma_bf16(t_s, sw128_kmajor_desc(q_addr + off), sw128_kmajor_desc(k_addr + off), idesc_s,
+                      kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[s]);
+          umma_commit(&ring_empty[r]);
+          ++g;
+          if (q.j == q.ti.n_kv - 1) umma_commit(&q_empty[s]);
+        }
+        q.advance(p);
+      };
+      while (ok && (sq0.live() || sq1.live())) {
+        unit(sq0, 0);
+        unit(sq1, 1);
       }
+      // Every MMA must be complete before TMEM is released.
+      umma_commit(mma_done);
+      bool dok = true;
+      wait_or_flag(mma_done, 0, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
     }
   } else {
-    // Softmax warps 2..5: TMEM lane quadrant warp % 4, one query row per thread.
+    // Softmax: warps 2..5 serve slot 0, warps 6..9 slot 1; TMEM lane quadrant warp % 4.
+    const int s = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int q = q0 + r;  // text-relative query
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float m = -INFINITY, l = 0.f;
-    uint8_t* prow_base = sP + r * 128;
+    const uint32_t t_s = lane_base + s * C::SLOT_COLS, t_o = t_s + kTK;
+    uint8_t* prow = sP + s * C::P_BYTES + r * 128;
     const int sw = r & 7;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!wait_warp(&s_full[sb], (j >> 1) & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
-      tc_fence_after();
-      uint32_t sv[kTK];
-#pragma unroll
-      for (int c = 0; c < kTK; c += 32) tmem_ld32(lane_base + sb * kTK + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
-      tmem_ld_wait();
-      const int key0 = (kb_lo + j) * kTK;
-      const bool full_block = key0 + kTK <= L && (!p.causal || key0 + kTK - 1 <= q0) &&
-                              (p.window < 0 || (q0 + kTQ - 1 - key0 <= p.window && key0 + kTK - 1 - q0 <= p.window));
-      // Row max with 8 independent partial maxima (a single 128-long chain of
-      // fmaxf would serialise on its latency).
-      float mp[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mp[t] = -INFINITY;
-      if (full_block) {
-#pragma unroll
-        for (int c = 0; c < kTK; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sv[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < kTK; ++c) {
-          const int key = key0 + c;
-          bool valid = key < L;
-          if (p.causal) valid = valid && key <= q;
-          if (p.window >= 0) valid = valid && abs(q - key) <= p.window;
-          if (!valid) sv[c] = __float_as_uint(-INFINITY);
-          mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sv[c]));
-        }
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      const float m_blk = mx * p.scale_log2;
-      // P_j goes into buffer j & 1: wait until PV_{j-2} released it.
-      if (!wait_warp(&p_free[sb], ((j >> 1) & 1) ^ 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
-      // Raise the running max only when the block max exceeds it by > 2^8.
-      // Rows that held a finite max and had PV blocks accumulated need O
-      // rescaled; the decision is per row, the TMEM round trip per warp.
-      const bool raise = m_blk > m + kRescaleThreshold;
-      const bool rescale_row = raise && j > 0 && m != -INFINITY;
-      const float alpha = rescale_row ? ex2_approx(m - m_blk) : 1.0f;
-      if (__any_sync(0xffffffffu, rescale_row)) {
-        const int i = j - 1;  // O holds PV_0..PV_{j-1}; wait for PV_{j-1}
-        if (!wait_warp(&o_done[i & 1], (i >> 1) & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
+    int k = s, u = 0, tiles = 0;
+    TileInfo ti;
+    while (ok && next_tile(p, k, ti)) {
+      const int q = ti.q0 + r;  // text-relative query
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < ti.n_kv; ++j, ++u) {
+        if (!wait_warp(&s_full[s], u & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(lane_base + C::O_COL + c, o);
+        const int key0 = (ti.kb_lo + j) * kTK;
+        const bool full_block = key0 + kTK <= ti.L && (!p.causal || key0 + kTK - 1 <= ti.q0) &&
+                                (p.window < 0 || (ti.q0 + kTQ - 1 - key0 <= p.window &&
+                                                  key0 + kTK - 1 - ti.q0 <= p.window));
+        // The keys row q may see in this block: columns [lo, hi).
+        int lo = 0, hi = kTK;
+        if (!full_block) {
+          hi = min(kTK, ti.L - key0);
+          if (p.causal) hi = min(hi, q - key0 + 1);
+          if (p.window >= 0) {
+            hi = min(hi, q + p.window - key0 + 1);
+            lo = max(0, q - p.window - key0);
+          }
+        }
+        // Pass 1: row max, all 128 columns read with one wait, 8 independent
+        // chains of 3-input maxima.
+        float mp[8];
+        {
+          uint32_t sv[kTK];
+#pragma unroll
+          for (int c = 0; c < kTK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
           tmem_ld_wait();
+          if (!full_block) mask_range<kTK>(sv, 0, lo, hi);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-          tmem_st32(lane_base + C::O_COL + c, o);
+          for (int t = 0; t < 8; ++t) mp[t] = fmaxf(__uint_as_float(sv[t]), __uint_as_float(sv[8 + t]));
+#pragma unroll
+          for (int c = 16; c < kTK; c += 16) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              mp[t] = fmax3(mp[t], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + 8 + t]));
+          }
         }
-        tmem_st_wait();
-      }
-      if (raise) {
-        l *= alpha;
-        m = m_blk;
-      }
-      const float m_use = m == -INFINITY ? 0.f : m;
-      float rs8[8];
+        const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+        const float m_blk = mx * p.scale_log2;
+        // Raise the running max only when the block max exceeds it by > 2^8.
+        // Rows that held a finite max need O rescaled; the decision is per
+        // row, the TMEM round trip per warp. PV(j-1) is complete (S(j) was
+        // committed after it).
+        const bool raise = m_blk > m + kRescaleThreshold;
+        const bool rescale_row = raise && j > 0 && m != -INFINITY;
+        const float alpha = rescale_row ? ex2_approx(m - m_blk) : 1.0f;
+        if (__any_sync(0xffffffffu, rescale_row)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c, o);
+            tmem_ld_wait();
 #pragma unroll
-      for (int t = 0; t < 8; ++t) rs8[t] = 0.f;
-      uint8_t* pb = prow_base + sb * C::P_BYTES;
-#pragma unroll
-      for (int c = 0; c < kTK; c += 8) {
-        uint32_t hb[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float e = ex2_approx(fmaf(__uint_as_float(sv[c + t]), p.scale_log2, -m_use));
-          rs8[t] += e;
-          // bf16 round-to-nearest-even on the integer pipe (e >= 0 and finite),
-          // keeping the conversion off the MUFU/XU pipe the exp2 needs.
-          const uint32_t b = __float_as_uint(e);
-          hb[t] = b + 0x7FFFu + ((b >> 16) & 1u);
+            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+            tmem_st32(t_o + c, o);
+          }
+          tmem_st_wait();
         }
-        uint4 w;
-        w.x = __byte_perm(hb[0], hb[1], 0x7632);
-        w.y = __byte_perm(hb[2], hb[3], 0x7632);
-        w.z = __byte_perm(hb[4], hb[5], 0x7632);
-        w.w = __byte_perm(hb[6], hb[7], 0x7632);
-        const int chunk = c >> 3;  // 16-byte chunk index 0..15 over 128 keys
-        *reinterpret_cast<uint4*>(pb + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
+        if (raise) {
+          l *= alpha;
+          m = m_blk;
+        }
+        const float neg_m = m == -INFINITY ? 0.f : -m;
+        // Pass 2: P = exp2(s * scale - m), 32 columns per TMEM read; the read
+        // of the next 32 columns is in flight while these are processed.
+        float rs[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) rs[t] = 0.f;
+        uint32_t buf[2][32];
+        tmem_ld32(t_s, buf[0]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int ch = 0; ch < kTK / 32; ++ch) {
+          uint32_t(&sv)[32] = buf[ch & 1];
+          if (ch + 1 < kTK / 32) tmem_ld32(t_s + (ch + 1) * 32, buf[(ch + 1) & 1]);
+          if (!full_block) mask_range<32>(sv, ch * 32, lo, hi);
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            float x[8];
+#pragma unroll
+            for (int t = 0; t < 8; t += 2)
+              fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
+                         neg_m);
+            uint32_t hb[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              x[t] = ex2_approx(x[t]);
+              // bf16 round-to-nearest-even on the integer pipe (x >= 0 and
+              // finite), keeping the conversion off the MUFU pipe the exp2 needs.
+              const uint32_t b = __float_as_uint(x[t]);
+              hb[t] = b + 0x7FFFu + ((b >> 16) & 1u);
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t += 2) add2(rs[t], rs[t + 1], x[t], x[t + 1]);
+            uint4 w;
+            w.x = __byte_perm(hb[0], hb[1], 0x7632);
+            w.y = __byte_perm(hb[2], hb[3], 0x7632);
+            w.z = __byte_perm(hb[4], hb[5], 0x7632);
+            w.w = __byte_perm(hb[6], hb[7], 0x7632);
+            const int chunk = (ch * 32 + c) >> 3;  // 16-byte chunk index 0..15 over 128 keys
+            *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
+          }
+          if (ch + 1 < kTK / 32) tmem_ld_wait();
+        }
+        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[s]);
       }
-      const float rowsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-      l += rowsum;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[sb]);
-      mbar_arrive(&s_free[sb]);
-    }
-    // Output: wait for the last PV, then O / l -> bf16.
-    const int last = n_kv - 1;
-    if (wait_warp(&o_done[last & 1], (last >> 1) & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) {
+      if (!ok) break;
+      // Tile epilogue: wait for the last PV, then O / l -> bf16.
+      if (!wait_warp(&o_full[s], tiles & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
-      __nv_bfloat16* orow = p.out + static_cast<long long>(s0 + q) * p.ldo + head * D;
+      __nv_bfloat16* orow = p.out + static_cast<long long>(ti.s0 + q) * p.ldo + ti.head * D;
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t o[32];
-        tmem_ld32(lane_base + C::O_COL + c, o);
+        tmem_ld32(t_o + c, o);
         tmem_ld_wait();
-        if (q < L) {
+        if (q < ti.L) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
@@ -324,6 +494,9 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+      tc_fence_before();
+      ++tiles;
+      k += 2;
     }
   }
 
@@ -343,10 +516,12 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   if (!make_tma_2d_bf16(&tk, a.k, total_rows, static_cast<long long>(a.hkv) * D, a.ldk, kTK, 64)) return -2;
   if (!make_tma_2d_bf16(&tv, a.v, total_rows, static_cast<long long>(a.hkv) * D, a.ldv, kTK, 64)) return -2;
   auto kern = fa_sm100_kernel<D>;
-  static bool attr = false;
-  if (!attr) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+  static bool attr[64] = {};  // the attribute is per device
+  if (!attr[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return -3;
-    attr = true;
+    attr[dev] = true;
   }
   FaParams p;
   p.cu = a.cu;
@@ -355,12 +530,13 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   p.ldo = a.ldo;
   p.hq = a.hq;
   p.hkv = a.hkv;
+  p.n_tiles = a.n_work * a.hq;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.causal;
   p.window = a.window;
   p.status = a.status;
-  dim3 grid(a.n_work, a.hq);
-  kern<<<grid, 192, C::SMEM, s>>>(tq, tk, tv, p);
+  const int grid = std::min(num_sms_cached(), p.n_tiles);
+  kern<<<grid, kFaThreads, C::SMEM, s>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
