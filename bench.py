@@ -381,10 +381,20 @@ def run_kernel_case(name: str, reps: int = 3):
                                                None if resid is None else resid.data_ptr(), out.stride(0), 0, None,
                                                s), name)
         flops = 2.0 * M * Nn * K
-    elif name == "attention":
+    elif name in ("attention", "attention_cfg5"):
         import numpy as np
 
-        lengths = [2048] * 4 + [512] * 8 + [256] * 16
+        if name == "attention":
+            lengths = [2048] * 4 + [512] * 8 + [256] * 16
+        else:  # ~64k tokens of config 5's lognormal lengths, in corpus order (seeded)
+            import im_not_llm_b200 as inl
+
+            all_lengths, _ = inl.synthetic.cfg5_corpus(n_texts=1024)
+            lengths = []
+            for L in all_lengths:
+                if sum(lengths) + int(L) > 65536:
+                    break
+                lengths.append(int(L))
         cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
         T = int(cu[-1])
         qkv = torch.randn(T, 4096, device="cuda").to(torch.bfloat16)
@@ -411,7 +421,8 @@ def run_kernel_case(name: str, reps: int = 3):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention", "gemm_qkv_fused", "gemm_gateup_fused"],
+    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention", "attention_cfg5", "gemm_qkv_fused",
+                                                              "gemm_gateup_fused"],
                     default=None,
                     help="time one kernel on a small case instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)

@@ -185,6 +185,13 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
       : "f"(a0), "f"(a1));
 }
 
+// bf16x2 {lo, hi} with round-to-nearest-even, one instruction.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 // Columns c of a 128-key block outside [lo, hi) become -inf (lo, hi per row).
 template <int N>
 __device__ __forceinline__ void mask_range(uint32_t (&sv)[N], int c0, int lo, int hi) {
@@ -380,25 +387,24 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             lo = max(0, q - p.window - key0);
           }
         }
-        // Pass 1: row max, all 128 columns read with one wait, 8 independent
+        // The block's 128 scores are read from TMEM once, with one wait
+        // (tcgen05.wait::ld waits for every read in flight, so chunked reads
+        // would each expose the full TMEM latency). Row max: 8 independent
         // chains of 3-input maxima.
-        float mp[8];
-        {
-          uint32_t sv[kTK];
+        uint32_t sv[kTK];
 #pragma unroll
-          for (int c = 0; c < kTK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
-          tmem_ld_wait();
-          if (!full_block) mask_range<kTK>(sv, 0, lo, hi);
+        for (int c = 0; c < kTK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+        tmem_ld_wait();
+        if (!full_block) mask_range<kTK>(sv, 0, lo, hi);
+        float mp[4];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) mp[t] = fmaxf(__uint_as_float(sv[t]), __uint_as_float(sv[8 + t]));
+        for (int t = 0; t < 4; ++t) mp[t] = fmaxf(__uint_as_float(sv[t]), __uint_as_float(sv[4 + t]));
 #pragma unroll
-          for (int c = 16; c < kTK; c += 16) {
+        for (int c = 8; c < kTK; c += 8) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-              mp[t] = fmax3(mp[t], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + 8 + t]));
-          }
+          for (int t = 0; t < 4; ++t) mp[t] = fmax3(mp[t], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + 4 + t]));
         }
-        const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+        const float mx = fmax3(mp[0], mp[1], fmaxf(mp[2], mp[3]));
         const float m_blk = mx * p.scale_log2;
         // Raise the running max only when the block max exceeds it by > 2^8.
         // Rows that held a finite max need O rescaled; the decision is per
@@ -409,13 +415,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const float alpha = rescale_row ? ex2_approx(m - m_blk) : 1.0f;
         if (__any_sync(0xffffffffu, rescale_row)) {
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(t_o + c, o);
+          for (int c = 0; c < D; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(t_o + c, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-            tmem_st32(t_o + c, o);
+            for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+            tmem_st16(t_o + c, o);
           }
           tmem_st_wait();
         }
@@ -424,48 +430,32 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           m = m_blk;
         }
         const float neg_m = m == -INFINITY ? 0.f : -m;
-        // Pass 2: P = exp2(s * scale - m), 32 columns per TMEM read; the read
-        // of the next 32 columns is in flight while these are processed.
-        float rs[8];
+        // P = exp2(s * scale - m) from the registers read above.
+        float rs[4];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) rs[t] = 0.f;
-        uint32_t buf[2][32];
-        tmem_ld32(t_s, buf[0]);
-        tmem_ld_wait();
+        for (int t = 0; t < 4; ++t) rs[t] = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < kTK / 32; ++ch) {
-          uint32_t(&sv)[32] = buf[ch & 1];
-          if (ch + 1 < kTK / 32) tmem_ld32(t_s + (ch + 1) * 32, buf[(ch + 1) & 1]);
-          if (!full_block) mask_range<32>(sv, ch * 32, lo, hi);
+        for (int c = 0; c < kTK; c += 8) {
+          float x[8];
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float x[8];
+          for (int t = 0; t < 8; t += 2)
+            fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
+                       neg_m);
 #pragma unroll
-            for (int t = 0; t < 8; t += 2)
-              fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
-                         neg_m);
-            uint32_t hb[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              x[t] = ex2_approx(x[t]);
-              // bf16 round-to-nearest-even on the integer pipe (x >= 0 and
-              // finite), keeping the conversion off the MUFU pipe the exp2 needs.
-              const uint32_t b = __float_as_uint(x[t]);
-              hb[t] = b + 0x7FFFu + ((b >> 16) & 1u);
-            }
-#pragma unroll
-            for (int t = 0; t < 8; t += 2) add2(rs[t], rs[t + 1], x[t], x[t + 1]);
-            uint4 w;
-            w.x = __byte_perm(hb[0], hb[1], 0x7632);
-            w.y = __byte_perm(hb[2], hb[3], 0x7632);
-            w.z = __byte_perm(hb[4], hb[5], 0x7632);
-            w.w = __byte_perm(hb[6], hb[7], 0x7632);
-            const int chunk = (ch * 32 + c) >> 3;  // 16-byte chunk index 0..15 over 128 keys
-            *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
-          }
-          if (ch + 1 < kTK / 32) tmem_ld_wait();
+          for (int t = 0; t < 8; ++t) x[t] = ex2_approx(x[t]);
+          add2(rs[0], rs[1], x[0], x[1]);
+          add2(rs[2], rs[3], x[2], x[3]);
+          add2(rs[0], rs[1], x[4], x[5]);
+          add2(rs[2], rs[3], x[6], x[7]);
+          uint4 w;
+          w.x = cvt_bf16x2(x[0], x[1]);
+          w.y = cvt_bf16x2(x[2], x[3]);
+          w.z = cvt_bf16x2(x[4], x[5]);
+          w.w = cvt_bf16x2(x[6], x[7]);
+          const int chunk = c >> 3;  // 16-byte chunk index 0..15 over 128 keys
+          *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
         }
-        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&p_full[s]);
@@ -476,20 +466,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __nv_bfloat16* orow = p.out + static_cast<long long>(ti.s0 + q) * p.ldo + ti.head * D;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(t_o + c, o);
+      {
+        uint32_t o[D];  // one TMEM read of the whole output row, one wait
+#pragma unroll
+        for (int c = 0; c < D; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
         tmem_ld_wait();
         if (q < ti.L) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
+          for (int t = 0; t < D / 8; ++t) {
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[8 * t + 0]) * inv, __uint_as_float(o[8 * t + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[8 * t + 2]) * inv, __uint_as_float(o[8 * t + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[8 * t + 4]) * inv, __uint_as_float(o[8 * t + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[8 * t + 6]) * inv, __uint_as_float(o[8 * t + 7]) * inv);
+            w.x = cvt_bf16x2(__uint_as_float(o[8 * t + 0]) * inv, __uint_as_float(o[8 * t + 1]) * inv);
+            w.y = cvt_bf16x2(__uint_as_float(o[8 * t + 2]) * inv, __uint_as_float(o[8 * t + 3]) * inv);
+            w.z = cvt_bf16x2(__uint_as_float(o[8 * t + 4]) * inv, __uint_as_float(o[8 * t + 5]) * inv);
+            w.w = cvt_bf16x2(__uint_as_float(o[8 * t + 6]) * inv, __uint_as_float(o[8 * t + 7]) * inv);
             dst[t] = w;
           }
         }
