@@ -344,6 +344,7 @@ def run_kernel_case(name: str, reps: int = 3):
     from im_not_llm_b200 import _native as N
 
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")  # device wait status of the GEMM cases
     if name in ("gemm_qkv_fused", "gemm_gateup_fused"):
         M, K = 32768, 1024
         fused_qkv = name == "gemm_qkv_fused"
@@ -353,16 +354,17 @@ def run_kernel_case(name: str, reps: int = 3):
         out = torch.empty(M, Nn if fused_qkv else Nn // 2, device="cuda", dtype=torch.bfloat16)
         ss = torch.rand(M, K // 64, device="cuda") + 1.0
         pos = (torch.arange(M, device="cuda", dtype=torch.int32) % 2048)  # packed texts: consecutive positions
-        cs = torch.rand(64, 2048, device="cuda")  # frequency-major [d/2, max_pos]
+        cs = torch.rand(32, 2048, 4, device="cuda")  # RoPE pairs [d/4, max_pos, (cos, cos, sin, sin)]
         qn = torch.ones(128, device="cuda")
         a = N.GemmEx()
         a.A, a.lda, a.W, a.ldw, a.M, a.N, a.K = A.data_ptr(), K, W.data_ptr(), K, M, Nn, K
         a.epi, a.act, a.gate_block = (4 if fused_qkv else 2), 0, 128
         a.out, a.ldo = out.data_ptr(), out.stride(0)
         a.ss_in, a.ss_in_parts, a.ss_dim, a.ss_eps = ss.data_ptr(), K // 64, K, 1e-6
+        a.status = status.data_ptr()
         if fused_qkv:
             a.qn = a.kn = qn.data_ptr()
-            a.pos, a.cos, a.sin = pos.data_ptr(), cs.data_ptr(), cs.data_ptr()
+            a.pos, a.cos = pos.data_ptr(), cs.data_ptr()
             a.hq, a.hkv, a.d, a.max_pos, a.qk_eps = 16, 8, 128, 2048, 1e-6
 
         def launch():
@@ -378,8 +380,8 @@ def run_kernel_case(name: str, reps: int = 3):
         def launch():
             N.check(N.lib().inl_cuda_gemm_bf16(A.data_ptr(), K, W.data_ptr(), K, M, Nn, K, epi, 0, 128,
                                                out.data_ptr(), out.stride(0),
-                                               None if resid is None else resid.data_ptr(), out.stride(0), 0, None,
-                                               s), name)
+                                               None if resid is None else resid.data_ptr(), out.stride(0), 0,
+                                               status.data_ptr(), s), name)
         flops = 2.0 * M * Nn * K
     elif name in ("attention", "attention_cfg5"):
         import numpy as np
@@ -416,7 +418,10 @@ def run_kernel_case(name: str, reps: int = 3):
     en.record()
     torch.cuda.synchronize()
     ms = st.elapsed_time(en) / reps
-    print(json.dumps({"case": name, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+    code = int(status.item())
+    print(json.dumps({"case": name, "ms": ms, "tflops": flops / ms / 1e9, "device_status": code}), flush=True)
+    if code:
+        raise SystemExit(f"{name}: a device wait ran past its limit (status {code})")
 
 
 def main():

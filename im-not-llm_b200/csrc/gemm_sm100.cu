@@ -122,13 +122,14 @@ __device__ __forceinline__ float ss_bf16_32(const float (&v)[32]) {
 
 // One q or k head of width D in TMEM columns [c0, c0 + D) of this thread's row:
 // RMSNorm with weight w, then half-split RoPE at position p, stored at dst.
-// cosT / sinT are [D/2, max_pos] (frequency-major), so the 32 threads of a
-// warp (consecutive tokens, mostly consecutive positions) read one line per
-// frequency instead of 32.
+// rp is the RoPE table packed by frequency pairs, [D/4, max_pos] float4 =
+// (cos f, cos f+1, sin f, sin f+1) for f = 2i: one 16-byte load serves two
+// frequencies, and the 32 threads of a warp (consecutive tokens, mostly
+// consecutive positions) read consecutive float4s. w is read as float4.
 template <int D>
 __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const float* __restrict__ w, float eps,
-                                        const float* __restrict__ cosT, const float* __restrict__ sinT, int p,
-                                        int max_pos, bool row_ok, __nv_bfloat16* dst) {
+                                        const float4* __restrict__ rp, int p, int max_pos, bool row_ok,
+                                        __nv_bfloat16* dst) {
   uint32_t r[32], u[32];
   float ss = 0.f;
 #pragma unroll 1
@@ -151,13 +152,20 @@ __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const 
     if (!row_ok) continue;
     float lo[32], hi[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float x1 = __uint_as_float(r[j]) * inv * w[c + j];
-      const float x2 = __uint_as_float(u[j]) * inv * w[HALF + c + j];
-      const long long ti = static_cast<long long>(c + j) * max_pos + p;
-      const float cs = cosT[ti], sn = sinT[ti];
-      lo[j] = x1 * cs - x2 * sn;
-      hi[j] = x2 * cs + x1 * sn;
+    for (int j = 0; j < 32; j += 4) {
+      const float4 wl = __ldg(reinterpret_cast<const float4*>(w + c + j));
+      const float4 wh = __ldg(reinterpret_cast<const float4*>(w + HALF + c + j));
+      const float4 t0 = __ldg(rp + static_cast<long long>((c + j) >> 1) * max_pos + p);
+      const float4 t1 = __ldg(rp + static_cast<long long>(((c + j) >> 1) + 1) * max_pos + p);
+      const float a[4] = {wl.x, wl.y, wl.z, wl.w}, b[4] = {wh.x, wh.y, wh.z, wh.w};
+      const float cs[4] = {t0.x, t0.y, t1.x, t1.y}, sn[4] = {t0.z, t0.w, t1.z, t1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x1 = __uint_as_float(r[j + i]) * inv * a[i];
+        const float x2 = __uint_as_float(u[j + i]) * inv * b[i];
+        lo[j + i] = x1 * cs[i] - x2 * sn[i];
+        hi[j + i] = x2 * cs[i] + x1 * sn[i];
+      }
     }
     store_row32_bf16(dst + c, lo, 32);
     store_row32_bf16(dst + HALF + c, hi, 32);
@@ -253,9 +261,11 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       if (head < e.hq + e.hkv) {
         const float* w = head < e.hq ? e.qn : e.kn;
         if (hd == 128)
-          qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, e.cos, e.sin, p, e.max_pos, row_ok, orow + col);
+          qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, reinterpret_cast<const float4*>(e.cos), p, e.max_pos,
+                       row_ok, orow + col);
         else
-          qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, e.cos, e.sin, p, e.max_pos, row_ok, orow + col);
+          qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, reinterpret_cast<const float4*>(e.cos), p, e.max_pos,
+                      row_ok, orow + col);
       } else {
 #pragma unroll 1
         for (int c = 0; c < hd; c += 32) {
@@ -550,7 +560,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     // Each epilogue warp owns 128 columns = whole heads of width 64 or 128.
     bn = 256;
     if ((g.d != 64 && g.d != 128) || (g.N % 256) != 0 || g.N != (g.hq + 2 * g.hkv) * g.d || !g.pos || !g.cos ||
-        !g.sin || g.max_pos <= 0)
+        g.max_pos <= 0 || !g.qn || !g.kn || (reinterpret_cast<uintptr_t>(g.cos) & 15) ||
+        (reinterpret_cast<uintptr_t>(g.qn) & 15) || (reinterpret_cast<uintptr_t>(g.kn) & 15))
       return -1;
   }
   if (g.force_bn == 128 || g.force_bn == 256) {

@@ -354,8 +354,7 @@ struct Loader {
   }
 };
 
-int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, float** cosT_out = nullptr,
-               float** sinT_out = nullptr) {
+int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, float** pairs_out = nullptr) {
   const int half = m->c.d / 2;
   const int P = m->c.max_pos;
   std::vector<float> c(static_cast<size_t>(P) * half), s(static_cast<size_t>(P) * half);
@@ -379,24 +378,23 @@ int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, flo
   INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "rope upload");
   *cos_out = static_cast<float*>(dc);
   *sin_out = static_cast<float*>(ds);
-  if (cosT_out && sinT_out) {
-    // frequency-major copies [half, P] for the GEMM epilogue
-    std::vector<float> ct(c.size()), st(s.size());
-    for (int p = 0; p < P; ++p)
-      for (int i = 0; i < half; ++i) {
-        ct[static_cast<size_t>(i) * P + p] = c[static_cast<size_t>(p) * half + i];
-        st[static_cast<size_t>(i) * P + p] = s[static_cast<size_t>(p) * half + i];
+  if (pairs_out) {
+    // For the GEMM epilogue: [half / 2, P] float4 = (cos f, cos f+1, sin f, sin f+1), f = 2i.
+    std::vector<float> pk(static_cast<size_t>(half) * P * 2);
+    for (int i = 0; i < half / 2; ++i)
+      for (int p = 0; p < P; ++p) {
+        float* o = pk.data() + (static_cast<size_t>(i) * P + p) * 4;
+        o[0] = c[static_cast<size_t>(p) * half + 2 * i];
+        o[1] = c[static_cast<size_t>(p) * half + 2 * i + 1];
+        o[2] = s[static_cast<size_t>(p) * half + 2 * i];
+        o[3] = s[static_cast<size_t>(p) * half + 2 * i + 1];
       }
-    void *dct = nullptr, *dst = nullptr;
-    INL_CUDA_TRY(cudaMalloc(&dct, bytes), "rope table");
-    m->allocs.push_back(dct);
-    INL_CUDA_TRY(cudaMalloc(&dst, bytes), "rope table");
-    m->allocs.push_back(dst);
-    INL_CUDA_TRY(cudaMemcpyAsync(dct, ct.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
-    INL_CUDA_TRY(cudaMemcpyAsync(dst, st.data(), bytes, cudaMemcpyHostToDevice, m->stream), "rope upload");
+    void* dp = nullptr;
+    INL_CUDA_TRY(cudaMalloc(&dp, pk.size() * 4), "rope table");
+    m->allocs.push_back(dp);
+    INL_CUDA_TRY(cudaMemcpyAsync(dp, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice, m->stream), "rope upload");
     INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "rope upload");
-    *cosT_out = static_cast<float*>(dct);
-    *sinT_out = static_cast<float*>(dst);
+    *pairs_out = static_cast<float*>(dp);
   }
   return INL_OK;
 }
@@ -445,7 +443,7 @@ int load_qwen3(inl_model* m, Loader& L) {
     if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
   }
   if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
-  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0, &m->cos0T, &m->sin0T))) return r;
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0, &m->rope_pairs))) return r;
   return INL_OK;
 }
 
@@ -866,8 +864,8 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
     g.qn = w.qn;
     g.kn = w.kn;
     g.pos = m->pos.as<int>();
-    g.cos = m->cos0T;
-    g.sin = m->sin0T;
+    g.cos = m->rope_pairs;
+    g.sin = nullptr;
     g.hq = c.hq;
     g.hkv = c.hkv;
     g.d = c.d;

@@ -126,8 +126,7 @@ struct inl_model {
   float* sin0 = nullptr;
   float* cos1 = nullptr;
   float* sin1 = nullptr;
-  float* cos0T = nullptr;  // frequency-major [d/2, max_pos] copies for the QKV epilogue
-  float* sin0T = nullptr;
+  float* rope_pairs = nullptr;  // QKV epilogue table [d/4, max_pos] x (cos f, cos f+1, sin f, sin f+1)
   // late Dense head
   void* proj = nullptr;
   float* proj_bias = nullptr;

@@ -43,9 +43,11 @@ INL_API int inl_cuda_gemm_bf16(const void* A, int64_t lda, const void* W, int64_
  *  ss_in/ss_in_parts/ss_dim/ss_eps: folded RMSNorm of the A rows; the
  *    accumulator is scaled by rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps);
  *  ss_out: [M, ceil(N / 64)] sums of squares of the stored bf16 rows (RESID);
- *  qn, kn, pos, cos, sin, hq, hkv, d, max_pos, qk_eps: the QKV epilogue
- *    (per-head RMSNorm of q/k heads, half-split RoPE at pos[row]); cos / sin
- *    are frequency-major tables [d/2, max_pos]. */
+ *  qn, kn, pos, cos, hq, hkv, d, max_pos, qk_eps: the QKV epilogue (per-head
+ *    RMSNorm of q/k heads, half-split RoPE at pos[row]); cos is the RoPE table
+ *    packed by frequency pairs, [d/4, max_pos, 4] f32 holding (cos f, cos f+1,
+ *    sin f, sin f+1) for f = 2i, 16-byte aligned; sin is unused (NULL); qn / kn
+ *    16-byte aligned. */
 typedef struct inl_gemm_ex {
   const void* A;
   int64_t lda;

@@ -275,11 +275,12 @@ def test_gemm_qkv_epilogue(gpu, d, hq, hkv):
     inv = 1.0 / (1e6 ** (torch.arange(half, dtype=torch.float64) * 2 / d))
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
     cos, sin = ang.cos().float().cuda(), ang.sin().float().cuda()
-    cosT, sinT = cos.t().contiguous(), sin.t().contiguous()  # frequency-major for the epilogue
+    # packed by frequency pairs for the epilogue: [d/4, max_pos, (cos f, cos f+1, sin f, sin f+1)]
+    pairs = torch.stack([cos[:, 0::2], cos[:, 1::2], sin[:, 0::2], sin[:, 1::2]], -1).transpose(0, 1).contiguous()
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     _ex(torch, A=x, lda=K, W=W, M=M, N=N, K=K, epi=4, out=out, ldo=N, ss_in=ss, ss_in_parts=K // 64, ss_dim=K,
-        ss_eps=1e-6, qn=qn, kn=kn, pos=pos, cos=cosT, sin=sinT, hq=hq, hkv=hkv, d=d, max_pos=max_pos, qk_eps=1e-6,
+        ss_eps=1e-6, qn=qn, kn=kn, pos=pos, cos=pairs, hq=hq, hkv=hkv, d=d, max_pos=max_pos, qk_eps=1e-6,
         status=st)
     assert st.item() == 0
     r = 1.0 / (x.double().pow(2).mean(-1, keepdim=True) + 1e-6).sqrt()
