@@ -303,7 +303,11 @@ def run_ours(args, world, rank, local):
                        "parallelism": f"dp{world} independent replicas"},
             "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05, all projections)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} bf16 sustained", "traffic": None,
+                         "peak_source": f"{peak_kind} bf16 sustained",
+                         "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per gemm_bf16_tn launch, mean "
+                                         "over one bench step's 112 launches (ncu, profiles/launches_cfg5_bench.md); "
+                                         "algorithmic bytes per launch ~6.1e8",
                          "gemm_launches": prof["launches"], "gemm_ms": prof["ms"],
                          "gemm_share_of_step": prof["ms"] / ms if ms > 0 else None,
                          "by_projection": {k: {"ms_per_step": v["ms"] / args.steps,
@@ -324,6 +328,10 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
     model.close()
 
+
+# Mean DRAM bytes (read + write) per gemm_bf16_tn launch over one config-5 bench
+# step (64.6k tokens), measured with ncu: 256.2 MB read + 202.2 MB written.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 458.4e6
 
 KERNEL_CASES = {
     # name: (M tokens, N, K, epilogue) — the four projections of one Qwen3-0.6B layer
