@@ -2,22 +2,24 @@
 //
 //   Y[M, N] = X[M, K] . W[N, K]^T        (X = packed token rows, W = nn.Linear weight)
 //
-// One CTA per SM, 192 threads, warp-specialised:
+// One CTA per SM, 320 threads, warp-specialised:
 //   warp 0      TMA producer: X and W tiles -> shared memory (128-byte swizzle),
 //               STAGES-deep ring guarded by full/empty mbarriers;
 //   warp 1      allocates TMEM and issues tcgen05.mma (one elected thread),
 //               M=128 x N=BN x K=16 per instruction, accumulators in TMEM,
 //               two accumulator buffers so the epilogue of tile i overlaps the
 //               main loop of tile i+1;
-//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers, fused epilogue
-//               (plain store, residual add, gated activation, f32 store,
-//               per-row scale), 16-byte global stores. Warp w reads TMEM lane
-//               quadrant w % 4, i.e. tile rows 32*(w%4) .. 32*(w%4)+31, one
-//               row per thread.
+//   warps 2..9  epilogue: tcgen05.ld TMEM -> registers, fused epilogue
+//               (plain store, residual add, gated activation, q/k norm + RoPE,
+//               f32 store, per-row scale). Warp w reads TMEM lane quadrant
+//               w % 4 (tile rows 32*(w%4) .. +31, one row per thread) and half
+//               (w - 2) / 4 of the tile's columns. bf16 results leave 32 x 32 at a
+//               time through a shared-memory staging area and a TMA tensor store.
 // Tiles are walked in row-major tile order by a static stride-gridDim
 // schedule, so the CTAs resident at one time share the same few X row blocks
 // and read W (a few MB) out of L2.
 #include <cstdio>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -38,7 +40,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int OUT_STAGE_BYTES = kEpiWarps * 2 * 32 * 64;  // per epilogue warp: 2 chunks of 32 x 32 bf16
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct EpiArgs {
@@ -65,31 +68,51 @@ struct EpiArgs {
   long long ldp;
 };
 
+// Output path of one epilogue warp: 32 rows x 32 bf16 columns at a time go
+// through a double-buffered 2 KB staging area in shared memory (64-byte rows,
+// 64-byte swizzle: the 16-byte piece j of row r sits at piece j ^ ((r >> 1) & 3),
+// which keeps each 8-lane group of a warp's stores on distinct banks) and leave
+// with one TMA tensor store, instead of 32 scattered 16-byte stores per
+// instruction. Rows and columns past the output's extent are clipped by the
+// tensor map. Every lane of the warp calls it together.
+struct OutStage {
+  const CUtensorMap* map;
+  uint8_t* buf;  // this warp's 2 x 2048 bytes
+  int issued;    // chunks stored so far
+};
+constexpr int kStageChunkBytes = 32 * 64;
+
+__device__ __forceinline__ void stage_store32(OutStage& st, const float (&v)[32], int col, int row0, int lane) {
+  uint8_t* b = st.buf + (st.issued & 1) * kStageChunkBytes;
+  if (st.issued >= 2) {
+    if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+    __syncwarp();
+  }
+  uint8_t* rowp = b + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(st.map, b, col, row0);
+    bulk_commit_group();
+  }
+  ++st.issued;
+}
+
 template <int ACT>
 __device__ __forceinline__ float gate_act(float x) {
   if constexpr (ACT == INL_ACT_SILU) return silu_f(x);
   else if constexpr (ACT == INL_ACT_GELU_ERF) return gelu_erf_f(x);
   else return gelu_tanh_f(x);
-}
-
-// Store 32 consecutive bf16 values of one row (64 bytes) with column guard.
-__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float (&v)[32], int ncols_left) {
-  if (ncols_left >= 32) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-      d4[j] = w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < ncols_left) dst[j] = __float2bfloat16_rn(v[j]);
-  }
 }
 
 __device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* src, float (&v)[32], int ncols_left) {
@@ -121,15 +144,16 @@ __device__ __forceinline__ float ss_bf16_32(const float (&v)[32]) {
 }
 
 // One q or k head of width D in TMEM columns [c0, c0 + D) of this thread's row:
-// RMSNorm with weight w, then half-split RoPE at position p, stored at dst.
+// RMSNorm with weight w, then half-split RoPE at position p, stored through st
+// at output columns col0 .. col0 + D of rows row0 .. row0 + 31.
 // rp is the RoPE table packed by frequency pairs, [D/4, max_pos] float4 =
 // (cos f, cos f+1, sin f, sin f+1) for f = 2i: one 16-byte load serves two
 // frequencies, and the 32 threads of a warp (consecutive tokens, mostly
 // consecutive positions) read consecutive float4s. w is read as float4.
 template <int D>
 __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const float* __restrict__ w, float eps,
-                                        const float4* __restrict__ rp, int p, int max_pos, bool row_ok,
-                                        __nv_bfloat16* dst) {
+                                        const float4* __restrict__ rp, int p, int max_pos, OutStage& st, int col0,
+                                        int row0, int lane) {
   uint32_t r[32], u[32];
   float ss = 0.f;
 #pragma unroll 1
@@ -149,8 +173,7 @@ __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const 
     tmem_ld32(t_row + c0 + c, r);
     tmem_ld32(t_row + c0 + HALF + c, u);
     tmem_ld_wait();
-    if (!row_ok) continue;
-    float lo[32], hi[32];
+    float lo[32], hi[32];  // rows past M are computed too (p = 0) and clipped by the store
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       const float4 wl = __ldg(reinterpret_cast<const float4*>(w + c + j));
@@ -167,17 +190,19 @@ __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const 
         hi[j + i] = x2 * cs[i] + x1 * sn[i];
       }
     }
-    store_row32_bf16(dst + c, lo, 32);
-    store_row32_bf16(dst + HALF + c, hi, 32);
+    stage_store32(st, lo, col0 + c, row0, lane);
+    stage_store32(st, hi, col0 + HALF + c, row0, lane);
   }
 }
 
 // Epilogue of one tile for one warp: TMEM lanes = tile rows (one per thread),
 // columns [half * BN/2, (half + 1) * BN/2) of the tile.
 template <int BN, int EPI, int ACT>
-__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, int half, const EpiArgs& e) {
+__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, int half, const EpiArgs& e,
+                                              OutStage& st, int lane) {
   constexpr int HW = BN / 2;
   const bool row_ok = row < e.M;
+  const int row0 = row - lane;  // first row of this warp's 32
   float rs = 1.0f;
   if (e.ss_in != nullptr && row_ok) {
     const float* sp = e.ss_in + static_cast<long long>(row) * e.ss_in_parts;
@@ -209,10 +234,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = gate_act<ACT>(__uint_as_float(r[j]) * rs) * (__uint_as_float(u[j]) * rs);
-      if (row_ok) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo + o0 + c;
-        store_row32_bf16(dst, v, out_n - (o0 + c));
-      }
+      if (o0 + c < out_n) stage_store32(st, v, o0 + c, row0, lane);  // uniform; rows past M are clipped
     }
   } else if constexpr (EPI == INL_EPI_SEGMAX) {
     // Rows are vocabulary entries, columns are packed tokens of segment seg[col]:
@@ -252,7 +274,6 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       }
     }
     const int hd = e.d;
-    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo;
 #pragma unroll 1
     for (int hc = 0; hc < HW; hc += hd) {
       const int col = c_begin + hc;
@@ -262,10 +283,10 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
         const float* w = head < e.hq ? e.qn : e.kn;
         if (hd == 128)
           qk_head<128>(t_row, half * HW + hc, rs, w, e.qk_eps, reinterpret_cast<const float4*>(e.cos), p, e.max_pos,
-                       row_ok, orow + col);
+                       st, col, row0, lane);
         else
           qk_head<64>(t_row, half * HW + hc, rs, w, e.qk_eps, reinterpret_cast<const float4*>(e.cos), p, e.max_pos,
-                      row_ok, orow + col);
+                      st, col, row0, lane);
       } else {
 #pragma unroll 1
         for (int c = 0; c < hd; c += 32) {
@@ -273,7 +294,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
-          if (row_ok) store_row32_bf16(orow + col + c, v, 32);
+          stage_store32(st, v, col + c, row0, lane);
         }
       }
     }
@@ -284,10 +305,11 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       tmem_ld_wait();
       const int col = n0 + half * HW + c;
       const int left = e.N - col;
-      if (!row_ok || left <= 0) continue;  // loads above stay warp-uniform
+      if (left <= 0) continue;  // warp-uniform
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
       if constexpr (EPI == INL_EPI_F32) {
+        if (!row_ok) continue;
         float* dst = reinterpret_cast<float*>(e.out) + static_cast<long long>(row) * e.ldo + col;
         if (left >= 32) {
 #pragma unroll
@@ -298,6 +320,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
         }
       } else {
         if constexpr (EPI == INL_EPI_RESID_BF16) {
+          if (row_ok) {
           float rr[32];
           load_row32_bf16(e.resid + static_cast<long long>(row) * e.ldr + col, rr, left);
 #pragma unroll
@@ -309,9 +332,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
             if ((c & 32) == 0) *so = s;
             else *so += s;
           }
+          }
         }
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out) + static_cast<long long>(row) * e.ldo + col;
-        store_row32_bf16(dst, v, left);
+        stage_store32(st, v, col, row0, lane);  // rows past M / columns past N are clipped
       }
     }
   }
@@ -319,14 +342,15 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
 
 template <int BN, int EPI, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                        int N, int K, EpiArgs e, int* status) {
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiArgs e, int* status) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint8_t* sOut = sB + C::STAGES * C::B_BYTES;  // output staging of the epilogue warps
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::OUT_STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -436,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue warps 2..9: lane quadrant warp % 4, column half (warp - 2) / 4.
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
+    OutStage st{&tmO, sOut + (warp - 2) * 2 * kStageChunkBytes, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -444,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = mb * kBM + quad * 32 + lane;
-      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e);
+      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e, st, lane);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
@@ -452,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_group<0>();  // output stores finished before the CTA's shared memory goes away
   }
 
   tc_fence_before();
@@ -496,31 +522,37 @@ int num_sms() {
 }
 
 template <int BN, int EPI, int ACT>
-cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& e,
+cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, int M, int N, int K,
+                        const EpiArgs& e,
                         int* status, int max_ctas, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_tn_kernel<BN, EPI, ACT>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
+  int dev = 0;
+  cudaError_t derr = cudaGetDevice(&dev);
+  if (derr != cudaSuccess) return derr;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  static bool attr_set[64] = {};  // per instantiation and device
+  if (!attr_set[dev]) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (err != cudaSuccess) return err;
-    attr_set = true;
+    attr_set[dev] = true;
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, M, N, K, e, status);
+  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, to, M, N, K, e, status);
   return cudaGetLastError();
 }
 
 template <int BN, int EPI>
-cudaError_t dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+cudaError_t dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, int M, int N,
+                         int K,
                          const EpiArgs& e, int* status, int max_ctas, cudaStream_t s) {
   switch (act) {
-    case INL_ACT_SILU: return launch_gemm<BN, EPI, INL_ACT_SILU>(ta, tb, M, N, K, e, status, max_ctas, s);
-    case INL_ACT_GELU_ERF: return launch_gemm<BN, EPI, INL_ACT_GELU_ERF>(ta, tb, M, N, K, e, status, max_ctas, s);
-    default: return launch_gemm<BN, EPI, INL_ACT_GELU_TANH>(ta, tb, M, N, K, e, status, max_ctas, s);
+    case INL_ACT_SILU: return launch_gemm<BN, EPI, INL_ACT_SILU>(ta, tb, to, M, N, K, e, status, max_ctas, s);
+    case INL_ACT_GELU_ERF: return launch_gemm<BN, EPI, INL_ACT_GELU_ERF>(ta, tb, to, M, N, K, e, status, max_ctas, s);
+    default: return launch_gemm<BN, EPI, INL_ACT_GELU_TANH>(ta, tb, to, M, N, K, e, status, max_ctas, s);
   }
 }
 
@@ -528,6 +560,24 @@ cudaError_t dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, 
 
 // Row-major [rows, cols] bf16 with row stride `ld` elements; box [box_rows, box_cols]
 // (box_cols * 2 = 128 bytes for the 128-byte swizzle), out-of-range reads fill zeros.
+bool make_tma_2d_bf16_swizzled(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                               int box_rows, int box_cols, int swizzle_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tma_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
                       int box_rows, int box_cols) {
   EncodeTiledFn fn = encode_fn();
@@ -573,29 +623,36 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
     bn = 256;
   }
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, bn)) return -2;
+  // bf16 outputs leave through the epilogue warps' staging: boxes of 32 rows x 32
+  // columns, 64-byte swizzle; the gated epilogue writes N / 2 columns.
+  std::memset(&to, 0, sizeof(to));
+  if (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16 || g.epi == INL_EPI_QKV) {
+    const int out_cols = g.epi == INL_EPI_GATED_BF16 ? g.N / 2 : g.N;
+    if (!make_tma_2d_bf16_swizzled(&to, g.out, g.M, out_cols, g.ldo, 32, 32, 64)) return -2;
+  }
   EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.ss_in, g.ss_in_parts, g.ss_dim, g.ss_eps, g.ss_out,
             (g.N + INL_SS_COLS - 1) / INL_SS_COLS, g.qn, g.kn, g.pos, g.cos, g.sin, g.hq, g.hkv, g.d, g.max_pos,
             g.qk_eps, g.status, g.M, g.N, g.seg, g.pooled, g.ldp};
   cudaError_t err;
   if (bn == 256) {
     switch (g.epi) {
-      case INL_EPI_BF16: err = launch_gemm<256, INL_EPI_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_QKV: err = launch_gemm<256, INL_EPI_QKV, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_SEGMAX: err = launch_gemm<256, INL_EPI_SEGMAX, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_BF16: err = launch_gemm<256, INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_QKV: err = launch_gemm<256, INL_EPI_QKV, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_SEGMAX: err = launch_gemm<256, INL_EPI_SEGMAX, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: return -1;
     }
   } else {
     switch (g.epi) {
-      case INL_EPI_BF16: err = launch_gemm<128, INL_EPI_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_RESID_BF16: err = launch_gemm<128, INL_EPI_RESID_BF16, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_F32: err = launch_gemm<128, INL_EPI_F32, 0>(ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_GATED_BF16: err = dispatch_act<128, INL_EPI_GATED_BF16>(g.act, ta, tb, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_BF16: err = launch_gemm<128, INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_BF16: err = launch_gemm<128, INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_F32: err = launch_gemm<128, INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_BF16: err = dispatch_act<128, INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: return -1;
     }
   }

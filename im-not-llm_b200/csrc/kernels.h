@@ -47,7 +47,8 @@ struct GemmArgs {
   float ss_eps = 0.f;
   // residual epilogue: partial sums of squares of the output rows [M, ceil(N / INL_SS_COLS)]
   float* ss_out = nullptr;
-  // QKV epilogue; cos / sin are FREQUENCY-MAJOR tables [d/2, max_pos]
+  // QKV epilogue; cos is the RoPE table packed by frequency pairs
+  // [d/4, max_pos] x float4 (cos f, cos f+1, sin f, sin f+1); sin is unused
   const float* qn = nullptr;
   const float* kn = nullptr;
   const int* pos = nullptr;
