@@ -488,6 +488,192 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM
+// The same GEMM on CTA pairs (clusters of 2) with tcgen05 cta_group::2: a pair
+// computes a 256 x 256 tile. Each CTA loads its 128 rows of X and its 128 rows of
+// W (its half of the tile's N) per K step, 32 KB instead of the 48 KB a CTA
+// loads for a 128 x 256 tile alone, and the leading CTA issues one M = 256
+// MMA stream that reads both CTAs' shared memory and writes each CTA's 128
+// accumulator rows into its own TMEM. Every CTA then runs the usual epilogue
+// on its own rows. Handshake:
+//   full[s]   (leading CTA only) armed by the leader's producer for both CTAs'
+//             bytes; both producers' TMA loads complete on it;
+//   empty[s]  (each CTA) one commit from the leader's MMA thread each;
+//   tfull[a]  (each CTA) one commit from the leader's MMA thread each;
+//   tempty[a] (leading CTA) one arrival per epilogue warp of both CTAs.
+// No load uses multicast.
+struct PairCfg {
+  static constexpr int BN = 256;
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = kBM * kBK * 2;         // 128 rows of X
+  static constexpr int B_BYTES = 128 * kBK * 2;         // 128 rows of W (half the tile's N)
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int OUT_STAGE_BYTES = kEpiWarps * 2 * 32 * 64;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_STAGE_BYTES + 1024 + 256;
+};
+
+template <int EPI, int ACT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiArgs e, int* status) {
+  using C = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint8_t* sOut = sB + C::STAGES * C::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::OUT_STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leading CTA of the pair
+  const uint32_t peer = rank ^ 1u;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int m_tiles = (M + 2 * kBM - 1) / (2 * kBM);
+  const int n_tiles = (N + C::BN - 1) / C::BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+        const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int b_row = nb * C::BN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status, INL_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, bar, kb * kBK, a_row);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, bar, kb * kBK, b_row);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every stage this CTA filled must have been consumed (its empty
+      // barrier released by the leader's commit) before the CTA can go away,
+      // since the leader's MMAs read this CTA's shared memory.
+      const long long first = issued > C::STAGES ? issued - C::STAGES : 0;
+      for (long long f = first; f < issued; ++f) {
+        const int s = static_cast<int>(f % C::STAGES);
+        const uint32_t ph = static_cast<uint32_t>((f / C::STAGES) & 1);
+        if (!mbar_wait(&empty[s], ph, status, INL_DEV_TIMEOUT_DRAIN)) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(2 * kBM, C::BN);
+      const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
+      const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status, INL_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, INL_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_bf16_pair(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                           (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(empty_peer0 + static_cast<uint32_t>(stage * sizeof(uint64_t)));
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        umma_commit_pair(tfull_peer0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..9 of both CTAs, on this CTA's 128 rows of the tile.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    OutStage st{&tmO, sOut + (warp - 2) * 2 * kStageChunkBytes, 0};
+    const uint32_t tempty_lead0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+      const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * C::BN);
+      const int row = mb * 2 * kBM + static_cast<int>(rank) * kBM + quad * 32 + lane;
+      epilogue_tile<C::BN, EPI, ACT>(t_row, row, nb * C::BN, half, e, st, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_lead0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its partner may still touch its shared memory / TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -543,6 +729,39 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   if (tiles < grid) grid = tiles;
   kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, to, M, N, K, e, status);
   return cudaGetLastError();
+}
+
+template <int EPI, int ACT>
+cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, int M, int N, int K,
+                             const EpiArgs& e, int* status, int max_ctas, cudaStream_t stream) {
+  using C = PairCfg;
+  auto kern = gemm_bf16_pair_kernel<EPI, ACT>;
+  int dev = 0;
+  cudaError_t derr = cudaGetDevice(&dev);
+  if (derr != cudaSuccess) return derr;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  static bool attr_set[64] = {};  // per instantiation and device
+  if (!attr_set[dev]) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + C::BN - 1) / C::BN);
+  int pairs = num_sms() / 2;
+  if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+  if (tiles < pairs) pairs = tiles;
+  kern<<<2 * pairs, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, to, M, N, K, e, status);
+  return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t dispatch_act_pair(int act, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, int M,
+                              int N, int K, const EpiArgs& e, int* status, int max_ctas, cudaStream_t s) {
+  switch (act) {
+    case INL_ACT_SILU: return launch_gemm_pair<EPI, INL_ACT_SILU>(ta, tb, to, M, N, K, e, status, max_ctas, s);
+    case INL_ACT_GELU_ERF: return launch_gemm_pair<EPI, INL_ACT_GELU_ERF>(ta, tb, to, M, N, K, e, status, max_ctas, s);
+    default: return launch_gemm_pair<EPI, INL_ACT_GELU_TANH>(ta, tb, to, M, N, K, e, status, max_ctas, s);
+  }
 }
 
 template <int BN, int EPI>
@@ -623,9 +842,14 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
     bn = 256;
   }
+  // CTA pairs (cta_group::2) take 256-wide tiles of the bf16 epilogues; each CTA
+  // of a pair loads 128 rows of W.
+  const bool pair = g.cta_pair && bn == 256 &&
+                    (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16 ||
+                     g.epi == INL_EPI_QKV);
   CUtensorMap ta, tb, to;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
-  if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, bn)) return -2;
+  if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, pair ? 128 : bn)) return -2;
   // bf16 outputs leave through the epilogue warps' staging: boxes of 32 rows x 32
   // columns, 64-byte swizzle; the gated epilogue writes N / 2 columns.
   std::memset(&to, 0, sizeof(to));
@@ -637,7 +861,14 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
             (g.N + INL_SS_COLS - 1) / INL_SS_COLS, g.qn, g.kn, g.pos, g.cos, g.sin, g.hq, g.hkv, g.d, g.max_pos,
             g.qk_eps, g.status, g.M, g.N, g.seg, g.pooled, g.ldp};
   cudaError_t err;
-  if (bn == 256) {
+  if (pair) {
+    switch (g.epi) {
+      case INL_EPI_BF16: err = launch_gemm_pair<INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_BF16: err = launch_gemm_pair<INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_BF16: err = dispatch_act_pair<INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      default: err = launch_gemm_pair<INL_EPI_QKV, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+    }
+  } else if (bn == 256) {
     switch (g.epi) {
       case INL_EPI_BF16: err = launch_gemm<256, INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;

@@ -63,6 +63,7 @@ struct GemmArgs {
   int* status = nullptr;
   int max_ctas = 0;   // 0 = one CTA per SM
   int force_bn = 0;   // 0 = automatic tile width
+  int cta_pair = 1;   // 1 = 256 x 256 tiles on CTA pairs (cta_group::2) where the epilogue allows, 0 = one CTA per tile
 };
 
 // tcgen05 bf16 GEMM; returns 0 on success, <0 on bad arguments / launch error.
