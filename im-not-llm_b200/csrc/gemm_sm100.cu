@@ -420,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      const uint64_t a_desc0 = sw128_kmajor_desc(smem_u32(sA)), b_desc0 = sw128_kmajor_desc(smem_u32(sB));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -435,11 +436,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+          // Descriptors differ from the ring's base descriptors only in the
+          // start-address field (address >> 4, 14 bits; shared memory < 256 KB).
+          const uint64_t a_desc = a_desc0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
+          const uint64_t b_desc = b_desc0 + static_cast<uint64_t>((stage * C::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+            umma_bf16(d_tmem, a_desc + static_cast<uint64_t>(kk * 2), b_desc + static_cast<uint64_t>(kk * 2), idesc,
                       (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -600,6 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(2 * kBM, C::BN);
+      const uint64_t a_desc0 = sw128_kmajor_desc(smem_u32(sA)), b_desc0 = sw128_kmajor_desc(smem_u32(sB));
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
       const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
       int stage = 0;
@@ -617,11 +621,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+          // Descriptors differ from the ring's base descriptors only in the
+          // start-address field (address >> 4, 14 bits; shared memory < 256 KB).
+          const uint64_t a_desc = a_desc0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
+          const uint64_t b_desc = b_desc0 + static_cast<uint64_t>((stage * C::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_bf16_pair(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+            umma_bf16_pair(d_tmem, a_desc + static_cast<uint64_t>(kk * 2), b_desc + static_cast<uint64_t>(kk * 2), idesc,
                            (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit_pair(smem_u32(&empty[stage]));
@@ -842,11 +848,11 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
     bn = 256;
   }
-  // CTA pairs (cta_group::2) take 256-wide tiles of the bf16 epilogues; each CTA
-  // of a pair loads 128 rows of W.
+  // CTA pairs (cta_group::2) take 256-wide tiles of the plain, residual and gated
+  // bf16 epilogues; each CTA of a pair loads 128 rows of W. The QKV epilogue
+  // (q/k norm + RoPE) measured faster on single CTAs, so it stays there.
   const bool pair = g.cta_pair && bn == 256 &&
-                    (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16 ||
-                     g.epi == INL_EPI_QKV);
+                    (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16);
   CUtensorMap ta, tb, to;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, pair ? 128 : bn)) return -2;
@@ -865,8 +871,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     switch (g.epi) {
       case INL_EPI_BF16: err = launch_gemm_pair<INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm_pair<INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      case INL_EPI_GATED_BF16: err = dispatch_act_pair<INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
-      default: err = launch_gemm_pair<INL_EPI_QKV, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      default: err = dispatch_act_pair<INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
     }
   } else if (bn == 256) {
     switch (g.epi) {
