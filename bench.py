@@ -301,11 +301,11 @@ def run_ours(args, world, rank, local):
                        "tokens_per_step_per_gpu": tokens / args.steps,
                        "l2": "no flush: working set per step > L2 (1.2 GB bf16 weights, >=128 MB activations)",
                        "parallelism": f"dp{world} independent replicas"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tn (tcgen05, all projections)",
+            "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMMs of all projections (gemm_bf16_tn: qkv; gemm_bf16_pair: o, gate/up, down)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} bf16 sustained",
                          "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
-                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per gemm_bf16_tn launch, mean "
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch, mean "
                                          "over one bench step's 112 launches (ncu, profiles/launches_cfg5_bench.md); "
                                          "algorithmic bytes per launch ~6.1e8",
                          "gemm_launches": prof["launches"], "gemm_ms": prof["ms"],
@@ -329,9 +329,10 @@ def run_ours(args, world, rank, local):
     model.close()
 
 
-# Mean DRAM bytes (read + write) per gemm_bf16_tn launch over one config-5 bench
-# step (64.6k tokens), measured with ncu: 256.2 MB read + 202.2 MB written.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 458.4e6
+# Mean DRAM bytes (read + write) per GEMM launch (gemm_bf16_tn_kernel for QKV,
+# gemm_bf16_pair_kernel for o, gate/up and down) over one config-5 bench step
+# (64.6k tokens), measured with ncu: 464.6 MB.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 464.6e6
 
 KERNEL_CASES = {
     # name: (M tokens, N, K, epilogue) — the four projections of one Qwen3-0.6B layer
