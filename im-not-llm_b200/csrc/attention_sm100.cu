@@ -3,21 +3,23 @@
 // masks computed from positions, grouped-query heads by index.
 //
 // Persistent: one CTA per SM walks the tiles blockIdx.x, blockIdx.x +
-// gridDim.x, ... of the list (work item, query head), work items heaviest
-// first and the heads of one item adjacent (their K / V rows meet in L2). A
-// tile is 128 queries of one text and one head. The CTA runs two tile slots
-// side by side (its even tiles in slot 0, odd tiles in slot 1); each slot owns
-// a Q and a P buffer in shared memory and, in TMEM, a score buffer S (128
-// columns) and an output accumulator O (D columns): 2 x 256 of the 512
-// columns. 320 threads:
+// gridDim.x, ... of the list (work item, query heads), work items heaviest
+// first and the heads of one item adjacent (their K / V rows meet in L2). The
+// CTA runs two slots side by side; each slot owns a Q and a P buffer in
+// shared memory and, in TMEM, a score buffer S (128 columns) and an output
+// accumulator O (D columns): 2 x 256 of the 512 columns. When the GQA group
+// size is even, a tile is 128 queries of one text and two query heads of one
+// K / V head, one per slot, and each K / V tile is loaded once for both.
+// Otherwise a tile is 128 queries and one head, the CTA's even tiles run in
+// slot 0 and its odd tiles in slot 1. 320 threads:
 //   warp 0     TMA producer: each slot's Q tile, and K / V tiles of 128 keys
 //              into one ring, in exactly the order the MMA warp consumes them
 //              (so the ring can neither deadlock nor reorder);
 //   warp 1     TMEM allocation and tcgen05.mma issue. It alternates between
-//              the slots in units "O += P(j-1) V(j-1); S = Q K(j)^T", so the
-//              tensor core works on one slot while the other slot's softmax
-//              warps compute, and one slot's tile epilogue overlaps the other
-//              slot's blocks;
+//              the slots in units "S = Q K(j)^T; O += P(j-1) V(j-1)". S(j) only
+//              needs the softmax warps to have read S(j-1) out of TMEM, so it
+//              runs while they still compute P(j-1), and the next block's
+//              scores are ready when they finish;
 //   warps 2-5  softmax of slot 0, warps 6-9 of slot 1: thread = query row =
 //              TMEM lane. Reads S with tcgen05.ld, masks, keeps a running row
 //              max m and sum l, writes P = exp2(s - m) as bf16 into shared
@@ -25,11 +27,12 @@
 //              is only raised when the block max exceeds it by more than 2^8,
 //              and then O is rescaled in TMEM. At the end of a tile, O / l is
 //              written as bf16.
-// tcgen05.commit tracks every MMA issued before it, so the arrival of S(j)
-// also means PV(j-1) is complete: P's buffer may be rewritten and O rescaled
-// without more barriers, and the first PV of a slot's next tile (which
-// overwrites O) is issued only after that slot's softmax warps, having read O
-// for the epilogue, delivered the next P.
+// Per slot, barriers order the shared buffers: s_free (the scores were read,
+// S may be overwritten), pv_done (PV(j-1) is complete: P's buffer may be
+// rewritten and O rescaled; the softmax warps compute exp2 into registers
+// before they wait on it), p_full, o_full. The first PV of a slot's next tile
+// (which overwrites O) is issued only after that slot's softmax warps, having
+// read O for the epilogue, delivered the next P.
 // Every mbarrier wait is bounded (status word + early exit, TMEM freed).
 #include "common.cuh"
 #include "kernels.h"
@@ -50,7 +53,7 @@ struct FaCfg {
   static constexpr int TILE_BYTES = QB * kBox;   // one Q, K or V tile of 128 rows
   static constexpr int P_BYTES = 2 * kBox;       // 128 keys = two 64-key boxes
   static constexpr int NS = D == 128 ? 3 : 8;    // K / V ring slots
-  static constexpr int SMEM = 2 * TILE_BYTES + 2 * P_BYTES + NS * TILE_BYTES + 1024 + 256;
+  static constexpr int SMEM = 2 * TILE_BYTES + 2 * P_BYTES + NS * TILE_BYTES + 1024 + 512;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SLOT_COLS = 256;          // S at +0, O at +128
 };
@@ -61,6 +64,8 @@ struct FaParams {
   __nv_bfloat16* out;
   long long ldo;
   int hq, hkv, n_tiles;
+  int hpt;    // query heads per tile: 2 = the two heads of a GQA pair share every K / V load
+  int tstep;  // tile ordinal step of one sequence: 2 = slots take alternate tiles, 1 = paired slots
   float scale_log2;
   int causal, window;
   int* status;
@@ -72,8 +77,9 @@ struct TileInfo {
 
 __device__ __forceinline__ bool load_tile(const FaParams& p, int t, TileInfo& ti) {
   if (t >= p.n_tiles) return false;
-  const int item = t / p.hq;
-  ti.head = t - item * p.hq;
+  const int per_item = p.hq / p.hpt;
+  const int item = t / per_item;
+  ti.head = (t - item * per_item) * p.hpt;
   ti.kvh = ti.head / (p.hq / p.hkv);
   const int2 wk = p.work[item];
   ti.s0 = p.cu[wk.x];
@@ -90,19 +96,20 @@ __device__ __forceinline__ bool load_tile(const FaParams& p, int t, TileInfo& ti
   return true;
 }
 
-// The CTA's tile of ordinal k (k = slot, slot + 2, ...), skipping tiles
-// without key blocks; false when the slot has no more tiles.
+// The CTA's tile of ordinal k (k = first, first + tstep, ...), skipping tiles
+// without key blocks; false when the sequence has no more tiles.
 __device__ __forceinline__ bool next_tile(const FaParams& p, int& k, TileInfo& ti) {
   while (load_tile(p, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x), ti)) {
     if (ti.n_kv > 0) return true;
-    k += 2;
+    k += p.tstep;
   }
   return false;
 }
 
-// The sequence of MMA units of one slot, walked identically by the producer
-// and the MMA warp: unit u issues PV of the slot's S op u-1 (if any) and S op
-// u (if any); S ops run over the slot's tiles and their key blocks in order.
+// The sequence of MMA units of one slot (or of both slots, paired), walked
+// identically by the producer and the MMA warp: unit u issues S op u (if any)
+// and PV of S op u-1 (if any); S ops run over the tiles and their key blocks
+// in order.
 struct SlotSeq {
   TileInfo ti;
   int k, j;          // current tile ordinal, next key block in it
@@ -110,8 +117,8 @@ struct SlotSeq {
   int pv_row, pv_kvh;
   bool has, pv, pv_first, pv_last;
 
-  __device__ __forceinline__ void init(const FaParams& p, int slot) {
-    k = slot;
+  __device__ __forceinline__ void init(const FaParams& p, int first) {
+    k = first;
     j = 0;
     tiles = ops = 0;
     pv = false;
@@ -133,7 +140,7 @@ struct SlotSeq {
     ++ops;
     if (++j == ti.n_kv) {
       j = 0;
-      k += 2;
+      k += p.tstep;
       has = next_tile(p, k, ti);
     }
   }
@@ -185,6 +192,41 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
       : "f"(a0), "f"(a1));
 }
 
+// 2^a, 2^b for a, b <= 8 on the FMA pipe, for the share of the softmax
+// exponentials taken off the special-function unit. Range reduction x = j + f
+// with j = rint(x) (the 1.5 * 2^23 rounding constant: t = x + c holds j in its
+// low mantissa bits) and f in [-1/2, 1/2]; 2^f by a cubic, then j is added to
+// the exponent field: bits(t) << 23 == j << 23 modulo 2^32. The cubic is this
+// file's own minimax fit of 2^f on [-1/2, 1/2] (Lawson's iteratively
+// reweighted least squares on relative error): max relative error 7.5e-5,
+// well under the 2^-9 rounding step of the bf16 P it feeds. Inputs are
+// clamped at -126, so a masked score (-inf) gives ~1e-38 instead of 0.
+__device__ __forceinline__ void exp2_poly2(float& a, float& b) {
+  const float xa = fmaxf(a, -126.0f), xb = fmaxf(b, -126.0f);
+  uint32_t ta, tb, pa, pb;
+  asm("{\n\t.reg .b64 x, t, j, f, p, k;\n\t"
+      "mov.b64 x, {%4, %5};\n\t"
+      "mov.b64 k, 0x4B4000004B400000;\n\t"  // 1.5 * 2^23
+      "add.rn.f32x2 t, x, k;\n\t"
+      "mov.b64 k, 0xCB400000CB400000;\n\t"  // -1.5 * 2^23
+      "add.rn.f32x2 j, t, k;\n\t"
+      "mov.b64 k, 0xBF800000BF800000;\n\t"  // -1
+      "fma.rn.f32x2 f, j, k, x;\n\t"
+      "mov.b64 k, 0x3D61FBAF3D61FBAF;\n\t"  // c3 = 0.0551716648
+      "mov.b64 p, 0x3E786F103E786F10;\n\t"  // c2 = 0.2426111698
+      "fma.rn.f32x2 p, f, k, p;\n\t"
+      "mov.b64 k, 0x3F31798D3F31798D;\n\t"  // c1 = 0.6932609677
+      "fma.rn.f32x2 p, p, f, k;\n\t"
+      "mov.b64 k, 0x3F7FFB493F7FFB49;\n\t"  // c0 = 0.9999280572
+      "fma.rn.f32x2 p, p, f, k;\n\t"
+      "mov.b64 {%0, %1}, t;\n\t"
+      "mov.b64 {%2, %3}, p;\n\t}"
+      : "=r"(ta), "=r"(tb), "=r"(pa), "=r"(pb)
+      : "f"(xa), "f"(xb));
+  a = __uint_as_float((ta << 23) + pa);
+  b = __uint_as_float((tb << 23) + pb);
+}
+
 // bf16x2 {lo, hi} with round-to-nearest-even, one instruction.
 __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   uint32_t d;
@@ -200,7 +242,12 @@ __device__ __forceinline__ void mask_range(uint32_t (&sv)[N], int c0, int lo, in
     if (c0 + c < lo || c0 + c >= hi) sv[c] = __float_as_uint(-INFINITY);
 }
 
-template <int D>
+// PAIR: the two slots take the two query heads of one GQA pair for the same
+// 128 queries (one tile), so every K / V tile is loaded once for both; the
+// producer and the MMA warp walk one sequence and issue each unit's S and PV
+// for both slots. Otherwise the slots take alternate tiles, each with its own
+// sequence and K / V loads.
+template <int D, bool PAIR>
 __global__ void __launch_bounds__(kFaThreads, 1)
     fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, FaParams p) {
@@ -216,8 +263,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint64_t* s_full = bars + 4;      // [2]
   uint64_t* p_full = bars + 6;      // [2]
   uint64_t* o_full = bars + 8;      // [2]
-  uint64_t* mma_done = bars + 10;
-  uint64_t* ring_full = bars + 11;  // [NS]
+  uint64_t* s_free = bars + 10;     // [2]
+  uint64_t* pv_done = bars + 12;    // [2]
+  uint64_t* mma_done = bars + 14;
+  uint64_t* ring_full = bars + 15;  // [NS]
   uint64_t* ring_empty = ring_full + C::NS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ring_empty + C::NS);
 
@@ -229,6 +278,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
     mbar_init(mma_done, 1);
     for (int i = 0; i < C::NS; ++i) {
@@ -252,6 +303,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      constexpr int NH = PAIR ? 2 : 1;  // slots served by one unit
       SlotSeq sq0, sq1;
       sq0.init(p, 0);
       sq1.init(p, 1);
@@ -268,30 +320,36 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       };
       auto unit = [&](SlotSeq& q, const int s) {
         if (!q.live() || !ok) return;
-        if (q.pv && !ring_load(&tmV, q.pv_row, q.pv_kvh)) return;
         if (q.has) {
           if (q.j == 0) {
             if (q.tiles > 0 &&
                 !wait_or_flag(&q_empty[s], (q.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_PRODUCER, ok))
               return;
-            mbar_expect_tx(&q_full[s], C::TILE_BYTES);
-            for (int b = 0; b < C::QB; ++b)
-              tma_load_2d(sQ + s * C::TILE_BYTES + b * kBox, &tmQ, &q_full[s], q.ti.head * D + b * 64,
-                          q.ti.s0 + q.ti.q0);
+            mbar_expect_tx(&q_full[s], NH * C::TILE_BYTES);
+            for (int h = 0; h < NH; ++h)
+              for (int b = 0; b < C::QB; ++b)
+                tma_load_2d(sQ + (s + h) * C::TILE_BYTES + b * kBox, &tmQ, &q_full[s], (q.ti.head + h) * D + b * 64,
+                            q.ti.s0 + q.ti.q0);
             ++q.tiles;
           }
           if (!ring_load(&tmK, q.row(), q.ti.kvh)) return;
         }
+        if (q.pv && !ring_load(&tmV, q.pv_row, q.pv_kvh)) return;
         q.advance(p);
       };
-      while (ok && (sq0.live() || sq1.live())) {
-        unit(sq0, 0);
-        unit(sq1, 1);
+      if constexpr (PAIR) {
+        while (ok && sq0.live()) unit(sq0, 0);
+      } else {
+        while (ok && (sq0.live() || sq1.live())) {
+          unit(sq0, 0);
+          unit(sq1, 1);
+        }
       }
       // Drain: every copy still in flight must land before the CTA exits.
       bool dok = true;
       if (sq0.tiles > 0) wait_or_flag(&q_full[0], (sq0.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
-      if (sq1.tiles > 0) wait_or_flag(&q_full[1], (sq1.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
+      if (!PAIR && sq1.tiles > 0)
+        wait_or_flag(&q_full[1], (sq1.tiles - 1) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
       for (int i = max(0, g - C::NS); i < g; ++i)
         wait_or_flag(&ring_full[i % C::NS], (i / C::NS) & 1, p.status, INL_DEV_TIMEOUT_DRAIN, dok);
     }
@@ -299,31 +357,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kTQ, kTK, 0);
       constexpr uint32_t idesc_o = umma_idesc_bf16(kTQ, D, 1);
+      constexpr int NH = PAIR ? 2 : 1;  // slots served by one unit
       SlotSeq sq0, sq1;
       sq0.init(p, 0);
       sq1.init(p, 1);
       int g = 0;  // ring tiles consumed
       auto unit = [&](SlotSeq& q, const int s) {
         if (!q.live() || !ok) return;
-        const uint32_t t_s = tmem + s * C::SLOT_COLS, t_o = t_s + kTK;
-        if (q.pv) {
-          if (!wait_or_flag(&p_full[s], (q.ops - 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
-          const int r = g % C::NS;
-          if (!wait_or_flag(&ring_full[r], (g / C::NS) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + s * C::P_BYTES);
-          const uint32_t v_addr = smem_u32(ring + r * C::TILE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < kTK / 16; ++kk) {
-            const uint32_t a_off = (kk >> 2) * kBox + (kk & 3) * 32;  // P: K-major, 64 keys per box
-            const uint32_t b_off = kk * 16 * 128;                      // V: 16 key rows per step
-            umma_bf16(t_o, sw128_kmajor_desc(p_addr + a_off), sw128_mnmajor_desc(v_addr + b_off, kBox), idesc_o,
-                      (!q.pv_first || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&ring_empty[r]);
-          ++g;
-          if (q.pv_last) umma_commit(&o_full[s]);
-        }
         if (q.has) {
           if (q.j == 0) {
             if (!wait_or_flag(&q_full[s], q.tiles & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
@@ -331,25 +371,58 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           const int r = g % C::NS;
           if (!wait_or_flag(&ring_full[r], (g / C::NS) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(sQ + s * C::TILE_BYTES);
           const uint32_t k_addr = smem_u32(ring + r * C::TILE_BYTES);
+          for (int h = 0; h < NH; ++h) {
+            const int sh = s + h;
+            // S is rewritten once the softmax warps have read the previous scores.
+            if (q.ops > 0 && !wait_or_flag(&s_free[sh], (q.ops - 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+            tc_fence_after();
+            const uint32_t t_s = tmem + sh * C::SLOT_COLS;
+            const uint32_t q_addr = smem_u32(sQ + sh * C::TILE_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-            umma_bf16(t_s, sw128_kmajor_desc(q_addr + off), sw128_kmajor_desc(k_addr + off), idesc_s,
-                      kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+              umma_bf16(t_s, sw128_kmajor_desc(q_addr + off), sw128_kmajor_desc(k_addr + off), idesc_s,
+                        kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[sh]);
           }
-          umma_commit(&s_full[s]);
           umma_commit(&ring_empty[r]);
           ++g;
           if (q.j == q.ti.n_kv - 1) umma_commit(&q_empty[s]);
         }
+        if (q.pv) {
+          const int r = g % C::NS;
+          if (!wait_or_flag(&ring_full[r], (g / C::NS) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+          const uint32_t v_addr = smem_u32(ring + r * C::TILE_BYTES);
+          for (int h = 0; h < NH; ++h) {
+            const int sh = s + h;
+            if (!wait_or_flag(&p_full[sh], (q.ops - 1) & 1, p.status, INL_DEV_TIMEOUT_MMA, ok)) return;
+            tc_fence_after();
+            const uint32_t t_o = tmem + sh * C::SLOT_COLS + kTK;
+            const uint32_t p_addr = smem_u32(sP + sh * C::P_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < kTK / 16; ++kk) {
+              const uint32_t a_off = (kk >> 2) * kBox + (kk & 3) * 32;  // P: K-major, 64 keys per box
+              const uint32_t b_off = kk * 16 * 128;                      // V: 16 key rows per step
+              umma_bf16(t_o, sw128_kmajor_desc(p_addr + a_off), sw128_mnmajor_desc(v_addr + b_off, kBox),
+                        idesc_o, (!q.pv_first || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&pv_done[sh]);
+            if (q.pv_last) umma_commit(&o_full[sh]);
+          }
+          umma_commit(&ring_empty[r]);
+          ++g;
+        }
         q.advance(p);
       };
-      while (ok && (sq0.live() || sq1.live())) {
-        unit(sq0, 0);
-        unit(sq1, 1);
+      if constexpr (PAIR) {
+        while (ok && sq0.live()) unit(sq0, 0);
+      } else {
+        while (ok && (sq0.live() || sq1.live())) {
+          unit(sq0, 0);
+          unit(sq1, 1);
+        }
       }
       // Every MMA must be complete before TMEM is released.
       umma_commit(mma_done);
@@ -365,9 +438,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const uint32_t t_s = lane_base + s * C::SLOT_COLS, t_o = t_s + kTK;
     uint8_t* prow = sP + s * C::P_BYTES + r * 128;
     const int sw = r & 7;
-    int k = s, u = 0, tiles = 0;
+    int k = PAIR ? 0 : s, u = 0, tiles = 0;
     TileInfo ti;
     while (ok && next_tile(p, k, ti)) {
+      if constexpr (PAIR) ti.head += s;
       const int q = ti.q0 + r;  // text-relative query
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < ti.n_kv; ++j, ++u) {
@@ -395,6 +469,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
         for (int c = 0; c < kTK; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
         tmem_ld_wait();
+        // The scores are in registers: the next S may overwrite the buffer.
+        tc_fence_before();
+        mbar_arrive(&s_free[s]);
         if (!full_block) mask_range<kTK>(sv, 0, lo, hi);
         float mp[4];
 #pragma unroll
@@ -408,11 +485,45 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const float m_blk = mx * p.scale_log2;
         // Raise the running max only when the block max exceeds it by > 2^8.
         // Rows that held a finite max need O rescaled; the decision is per
-        // row, the TMEM round trip per warp. PV(j-1) is complete (S(j) was
-        // committed after it).
+        // row, the TMEM round trip per warp.
         const bool raise = m_blk > m + kRescaleThreshold;
         const bool rescale_row = raise && j > 0 && m != -INFINITY;
         const float alpha = rescale_row ? ex2_approx(m - m_blk) : 1.0f;
+        if (raise) {
+          l *= alpha;
+          m = m_blk;
+        }
+        const float neg_m = m == -INFINITY ? 0.f : -m;
+        // P = exp2(s * scale - m) into packed bf16 registers while PV(j-1)
+        // may still be reading P's buffer.
+        float rs[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) rs[t] = 0.f;
+        uint32_t pk[kTK / 2];
+#pragma unroll
+        for (int c = 0; c < kTK; c += 8) {
+          float x[8];
+#pragma unroll
+          for (int t = 0; t < 8; t += 2)
+            fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
+                       neg_m);
+          // Half of the exponentials on the special-function unit, half on the FMA pipe.
+#pragma unroll
+          for (int t = 0; t < 4; ++t) x[t] = ex2_approx(x[t]);
+          exp2_poly2(x[4], x[5]);
+          exp2_poly2(x[6], x[7]);
+          add2(rs[0], rs[1], x[0], x[1]);
+          add2(rs[2], rs[3], x[2], x[3]);
+          add2(rs[0], rs[1], x[4], x[5]);
+          add2(rs[2], rs[3], x[6], x[7]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) pk[c / 2 + t] = cvt_bf16x2(x[2 * t], x[2 * t + 1]);
+        }
+        // PV(u-1) must be complete before O is rescaled and P is rewritten.
+        if (u > 0) {
+          if (!wait_warp(&pv_done[s], (u - 1) & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
+          tc_fence_after();
+        }
         if (__any_sync(0xffffffffu, rescale_row)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 16) {
@@ -425,68 +536,58 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           tmem_st_wait();
         }
-        if (raise) {
-          l *= alpha;
-          m = m_blk;
-        }
-        const float neg_m = m == -INFINITY ? 0.f : -m;
-        // P = exp2(s * scale - m) from the registers read above.
-        float rs[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) rs[t] = 0.f;
-#pragma unroll
-        for (int c = 0; c < kTK; c += 8) {
-          float x[8];
-#pragma unroll
-          for (int t = 0; t < 8; t += 2)
-            fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
-                       neg_m);
-#pragma unroll
-          for (int t = 0; t < 8; ++t) x[t] = ex2_approx(x[t]);
-          add2(rs[0], rs[1], x[0], x[1]);
-          add2(rs[2], rs[3], x[2], x[3]);
-          add2(rs[0], rs[1], x[4], x[5]);
-          add2(rs[2], rs[3], x[6], x[7]);
-          uint4 w;
-          w.x = cvt_bf16x2(x[0], x[1]);
-          w.y = cvt_bf16x2(x[2], x[3]);
-          w.z = cvt_bf16x2(x[4], x[5]);
-          w.w = cvt_bf16x2(x[6], x[7]);
-          const int chunk = c >> 3;  // 16-byte chunk index 0..15 over 128 keys
-          *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) = w;
-        }
+        for (int chunk = 0; chunk < kTK / 8; ++chunk)  // 16-byte chunks 0..15 over 128 keys
+          *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) =
+              make_uint4(pk[4 * chunk], pk[4 * chunk + 1], pk[4 * chunk + 2], pk[4 * chunk + 3]);
         l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&p_full[s]);
       }
       if (!ok) break;
-      // Tile epilogue: wait for the last PV, then O / l -> bf16.
+      // Tile epilogue: wait for the last PV, then O / l -> bf16. The rows go
+      // through the slot's P buffer (free: the last PV has read it) in the
+      // swizzled layout of P, and each warp writes its 32 rows back with
+      // whole-row stores (256 / D rows per instruction), skipping rows past
+      // the end of the text.
       if (!wait_warp(&o_full[s], tiles & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
-      __nv_bfloat16* orow = p.out + static_cast<long long>(ti.s0 + q) * p.ldo + ti.head * D;
       {
         uint32_t o[D];  // one TMEM read of the whole output row, one wait
 #pragma unroll
         for (int c = 0; c < D; c += 32) tmem_ld32(t_o + c, *reinterpret_cast<uint32_t(*)[32]>(&o[c]));
         tmem_ld_wait();
-        if (q < ti.L) {
-          uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
-          for (int t = 0; t < D / 8; ++t) {
-            uint4 w;
-            w.x = cvt_bf16x2(__uint_as_float(o[8 * t + 0]) * inv, __uint_as_float(o[8 * t + 1]) * inv);
-            w.y = cvt_bf16x2(__uint_as_float(o[8 * t + 2]) * inv, __uint_as_float(o[8 * t + 3]) * inv);
-            w.z = cvt_bf16x2(__uint_as_float(o[8 * t + 4]) * inv, __uint_as_float(o[8 * t + 5]) * inv);
-            w.w = cvt_bf16x2(__uint_as_float(o[8 * t + 6]) * inv, __uint_as_float(o[8 * t + 7]) * inv);
-            dst[t] = w;
-          }
+        for (int t = 0; t < D / 8; ++t) {
+          uint4 w;
+          w.x = cvt_bf16x2(__uint_as_float(o[8 * t + 0]) * inv, __uint_as_float(o[8 * t + 1]) * inv);
+          w.y = cvt_bf16x2(__uint_as_float(o[8 * t + 2]) * inv, __uint_as_float(o[8 * t + 3]) * inv);
+          w.z = cvt_bf16x2(__uint_as_float(o[8 * t + 4]) * inv, __uint_as_float(o[8 * t + 5]) * inv);
+          w.w = cvt_bf16x2(__uint_as_float(o[8 * t + 6]) * inv, __uint_as_float(o[8 * t + 7]) * inv);
+          *reinterpret_cast<uint4*>(prow + (t >> 3) * kBox + (((t & 7) ^ sw) << 4)) = w;
         }
       }
+      __syncwarp();
+      {
+        constexpr int CPR = D / 8;       // 16-byte chunks per output row
+        constexpr int RPI = 32 / CPR;    // rows per store instruction
+        const int c = lane % CPR;
+        const uint8_t* stage = sP + s * C::P_BYTES + (c >> 3) * kBox;
+        __nv_bfloat16* out_head = p.out + ti.head * D + c * 8;
+#pragma unroll 4
+        for (int i = 0; i < 32 / RPI; ++i) {
+          const int rr = quad * 32 + i * RPI + lane / CPR;  // tile row
+          const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 128 + (((c & 7) ^ (rr & 7)) << 4));
+          if (ti.q0 + rr < ti.L)
+            *reinterpret_cast<uint4*>(out_head + static_cast<long long>(ti.s0 + ti.q0 + rr) * p.ldo) = w;
+        }
+      }
+      __syncwarp();  // the next P store rewrites these rows
       tc_fence_before();
       ++tiles;
-      k += 2;
+      k += p.tstep;
     }
   }
 
@@ -505,13 +606,15 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   if (!make_tma_2d_bf16(&tq, a.q, total_rows, static_cast<long long>(a.hq) * D, a.ldq, kTQ, 64)) return -2;
   if (!make_tma_2d_bf16(&tk, a.k, total_rows, static_cast<long long>(a.hkv) * D, a.ldk, kTK, 64)) return -2;
   if (!make_tma_2d_bf16(&tv, a.v, total_rows, static_cast<long long>(a.hkv) * D, a.ldv, kTK, 64)) return -2;
-  auto kern = fa_sm100_kernel<D>;
+  // Pair the query heads of a GQA group when the group size is even.
+  const bool pair = (a.hq / a.hkv) % 2 == 0;
+  auto kern = pair ? fa_sm100_kernel<D, true> : fa_sm100_kernel<D, false>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
-  static bool attr[64] = {};  // the attribute is per device
-  if (!attr[dev]) {
+  static bool attr[2][64] = {};  // the attribute is per kernel and device
+  if (!attr[pair][dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return -3;
-    attr[dev] = true;
+    attr[pair][dev] = true;
   }
   FaParams p;
   p.cu = a.cu;
@@ -520,7 +623,9 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   p.ldo = a.ldo;
   p.hq = a.hq;
   p.hkv = a.hkv;
-  p.n_tiles = a.n_work * a.hq;
+  p.hpt = pair ? 2 : 1;
+  p.tstep = pair ? 1 : 2;
+  p.n_tiles = a.n_work * (a.hq / p.hpt);
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.causal;
   p.window = a.window;

@@ -669,9 +669,22 @@ int check_inputs(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* 
 
 size_t es(const inl_model* m) { return m->dtype == INL_DTYPE_BF16 ? 2 : 4; }
 
+// Token- and text-sized buffers are allocated in granules of 16384 tokens and
+// 1024 texts. Batches planned under one token budget then share one allocation,
+// and a batch slightly larger than the first one does not reallocate (cudaFree
+// synchronises the device) in the middle of a stream of batches.
+constexpr size_t kTokenGranule = 16384;
+constexpr size_t kTextGranule = 1024;
+size_t token_cap(int T) {
+  return (static_cast<size_t>(std::max(T, 1)) + kTokenGranule - 1) / kTokenGranule * kTokenGranule;
+}
+size_t text_cap(int n) {
+  return (static_cast<size_t>(std::max(n, 1)) + kTextGranule - 1) / kTextGranule * kTextGranule;
+}
+
 int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   const ModelConfig& c = m->c;
-  const size_t T = static_cast<size_t>(std::max(b.T, 1));
+  const size_t T = token_cap(b.T);
   const size_t e = es(m);
   const size_t qkv_cols = static_cast<size_t>(c.hq + 2 * c.hkv) * c.d;
   const size_t act_cols = static_cast<size_t>(c.I);
@@ -685,7 +698,7 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->ss_a.ensure(T * parts * 4), "workspace");
   INL_CUDA_TRY(m->ss_b.ensure(T * parts * 4), "workspace");
   INL_CUDA_TRY(m->pos.ensure(T * 4), "workspace");
-  INL_CUDA_TRY(m->cu.ensure(static_cast<size_t>(b.n + 1) * 4), "workspace");
+  INL_CUDA_TRY(m->cu.ensure((text_cap(b.n) + 1) * 4), "workspace");
   INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
   const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work) * 8 + 64;
   if (stage > m->h_stage_bytes) {
@@ -702,20 +715,23 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   return INL_OK;
 }
 
-// Attention work items (text, query block), heaviest first so the long causal
-// tails start early and the short ones fill the gaps.
-int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch& b, int* n_work_out) {
-  const int qb = inl::attention_q_block(m->dtype == INL_DTYPE_BF16, m->c.d);
+// Attention work items (text, query block of qb rows), heaviest first (key
+// blocks a causal query block attends to, or the text's block count) so the
+// long tails start early and the short items fill the gaps.
+std::vector<std::pair<int, int2>> attention_work(const int* cu_host, int n, int qb, bool causal) {
   std::vector<std::pair<int, int2>> items;
-  for (int i = 0; i < b.n; ++i) {
-    const int L = b.cu_host[i + 1] - b.cu_host[i];
+  for (int i = 0; i < n; ++i) {
+    const int L = cu_host[i + 1] - cu_host[i];
     const int nb = (L + qb - 1) / qb;
-    for (int q = 0; q < nb; ++q) {
-      int cost = m->c.causal ? (q + 1) : nb;
-      items.push_back({cost, make_int2(i, q)});
-    }
+    for (int q = 0; q < nb; ++q) items.push_back({causal ? (q + 1) : nb, make_int2(i, q)});
   }
   std::stable_sort(items.begin(), items.end(), [](const auto& a, const auto& c) { return a.first > c.first; });
+  return items;
+}
+
+int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch& b, int* n_work_out) {
+  const int qb = inl::attention_q_block(m->dtype == INL_DTYPE_BF16, m->c.d);
+  const std::vector<std::pair<int, int2>> items = attention_work(b.cu_host, b.n, qb, m->c.causal != 0);
   const int n_work = static_cast<int>(items.size());
   int r = ensure_workspace(m, b, n_work);
   if (r) return r;
@@ -1287,7 +1303,7 @@ int inl_cuda_forward_hidden(inl_model* m, const uint32_t* ids, int ids_mem, cons
   if (b.T == 0) return INL_OK;
   const ModelConfig& c = m->c;
   const size_t bytes = static_cast<size_t>(b.T) * c.H * 4;
-  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  INL_CUDA_TRY(m->out.ensure(token_cap(b.T) * c.H * 4), "output buffer");
   const int bf = m->dtype == INL_DTYPE_BF16;
   // (the ModernBERT tower already ends with its final LayerNorm)
   if (normalize_final && c.arch != inl::ARCH_MODERNBERT) {
@@ -1326,8 +1342,8 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
     if (out_dim < 0 || out_dim > D) return fail(INL_ERR_CONFIG, "output_dim exceeds the model's embeddings");
     int widest = c.H;
     for (int d : c.dense_dims) widest = std::max(widest, d);
-    INL_CUDA_TRY(m->pooled.ensure(static_cast<size_t>(b.n) * widest * 4), "pooling buffer");
-    INL_CUDA_TRY(m->head_buf.ensure(static_cast<size_t>(b.n) * widest * 4), "pooling buffer");
+    INL_CUDA_TRY(m->pooled.ensure(text_cap(b.n) * widest * 4), "pooling buffer");
+    INL_CUDA_TRY(m->head_buf.ensure(text_cap(b.n) * widest * 4), "pooling buffer");
     INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->xn.p, bf, c.H, m->stream),
               "final norm");
     INL_K_TRY(inl::segment_mean(m->xn.p, bf, c.H, m->cu.as<int>(), b.n, c.H, m->pooled.as<float>(), m->stream),
@@ -1357,7 +1373,7 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
     m->launches++;
     const int od = out_dim > 0 ? out_dim : D;
     const size_t obytes = static_cast<size_t>(b.n) * od * 4;
-    INL_CUDA_TRY(m->out.ensure(obytes), "output buffer");
+    INL_CUDA_TRY(m->out.ensure(text_cap(b.n) * od * 4), "output buffer");
     if (out_dim > 0) {
       INL_K_TRY(inl::truncate_normalize(cur, b.n, D, out_dim, m->out.as<float>(), m->stream), "matryoshka");
       m->launches++;
@@ -1367,7 +1383,7 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
     return finish(m, m->out.p, obytes, out, out_mem);
   }
   const size_t bytes = static_cast<size_t>(b.n) * c.H * 4;
-  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  INL_CUDA_TRY(m->out.ensure(text_cap(b.n) * c.H * 4), "output buffer");
   INL_K_TRY(inl::last_token_norm_l2(m->h.p, bf, c.H, m->cu.as<int>(), b.n, m->final_norm, c.eps, c.H,
                                     m->out.as<float>(), m->stream),
             "last-token pooling");
@@ -1387,7 +1403,7 @@ int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int ids_mem,
   if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
   const int bf = m->dtype == INL_DTYPE_BF16;
   const size_t bytes = static_cast<size_t>(b.T) * m->proj_out * 4;
-  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  INL_CUDA_TRY(m->out.ensure(token_cap(b.T) * m->proj_out * 4), "output buffer");
   // final norm on every token -> Dense projection (f32 out) -> F.normalize.
   INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->xn.p, bf, c.H, m->stream),
             "final norm");
@@ -1440,13 +1456,13 @@ int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, cons
       seg.push_back(i);
     }
   const int Ts = static_cast<int>(idx.size());
-  INL_CUDA_TRY(m->pooled_i.ensure(static_cast<size_t>(n) * V * 4), "pooling buffer");
+  INL_CUDA_TRY(m->pooled_i.ensure(text_cap(n) * V * 4), "pooling buffer");
   INL_K_TRY(inl::fill_i32(m->pooled_i.as<int>(), static_cast<long long>(n) * V, inl::kOrderedNegInf, s), "fill");
   m->launches++;
   if (Ts > 0) {
-    INL_CUDA_TRY(m->speak_idx.ensure(static_cast<size_t>(Ts) * 4), "speaker index");
-    INL_CUDA_TRY(m->speak_seg.ensure(static_cast<size_t>(Ts) * 4), "speaker index");
-    INL_CUDA_TRY(m->head_buf.ensure(static_cast<size_t>(Ts) * H * es(m)), "head buffer");
+    INL_CUDA_TRY(m->speak_idx.ensure(token_cap(Ts) * 4), "speaker index");
+    INL_CUDA_TRY(m->speak_seg.ensure(token_cap(Ts) * 4), "speaker index");
+    INL_CUDA_TRY(m->head_buf.ensure(token_cap(Ts) * H * es(m)), "head buffer");
     INL_CUDA_TRY(cudaMemcpyAsync(m->speak_idx.p, idx.data(), static_cast<size_t>(Ts) * 4, cudaMemcpyHostToDevice, s),
                  "speaker upload");
     INL_CUDA_TRY(cudaMemcpyAsync(m->speak_seg.p, seg.data(), static_cast<size_t>(Ts) * 4, cudaMemcpyHostToDevice, s),
@@ -1483,7 +1499,7 @@ int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, cons
     }
   }
   const size_t bytes = static_cast<size_t>(n) * m->sparse_dim * 4;
-  INL_CUDA_TRY(m->out.ensure(bytes), "output buffer");
+  INL_CUDA_TRY(m->out.ensure(text_cap(n) * m->sparse_dim * 4), "output buffer");
   INL_K_TRY(inl::splade_finish(m->pooled_i.as<int>(), n, V, m->decoder_bias, c.logit_shift, m->open_mask, m->canon,
                                m->sparse_dim, m->out.as<float>(), s),
             "splade finish");
@@ -1752,12 +1768,11 @@ int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq,
   if (n_texts <= 0) return INL_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int qb = inl::attention_q_block(dtype == INL_DTYPE_BF16, d);
+  for (int i = 0; i < n_texts; ++i)
+    if (cu_seqlens_host[i + 1] < cu_seqlens_host[i])
+      return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
   std::vector<int2> work;
-  for (int i = 0; i < n_texts; ++i) {
-    const int L = cu_seqlens_host[i + 1] - cu_seqlens_host[i];
-    if (L < 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
-    for (int b = 0; b * qb < L; ++b) work.push_back(make_int2(i, b));
-  }
+  for (const auto& it : attention_work(cu_seqlens_host, n_texts, qb, causal != 0)) work.push_back(it.second);
   // Hook scratch (device cu + work list), cached across calls so a timing
   // loop measures the kernel, not allocations; calls are serialised.
   static std::mutex hook_mu;

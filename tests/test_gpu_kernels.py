@@ -169,7 +169,7 @@ def _attn_ref(torch, q, k, v, cu, hq, hkv, d, scale, causal, window):
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 @pytest.mark.parametrize("d,hq,hkv,causal,window", [
     (128, 16, 8, 1, -1), (128, 4, 4, 0, -1), (64, 12, 12, 0, 64), (256, 3, 1, 0, 512), (64, 4, 2, 1, -1),
-    (256, 3, 1, 0, -1), (128, 2, 1, 0, 40),
+    (256, 3, 1, 0, -1), (128, 2, 1, 0, 40), (128, 8, 2, 1, -1), (64, 6, 2, 0, -1),
 ])
 def test_attention_varlen(gpu, dtype, d, hq, hkv, causal, window):
     import torch
