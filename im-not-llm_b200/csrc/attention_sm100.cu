@@ -250,7 +250,8 @@ __device__ __forceinline__ void mask_range(uint32_t (&sv)[N], int c0, int lo, in
 template <int D, bool PAIR>
 __global__ void __launch_bounds__(kFaThreads, 1)
     fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, FaParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    FaParams p) {
   using C = FaCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -290,6 +291,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -536,6 +538,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           tmem_st_wait();
         }
+        // The previous tile's output store must have read these rows.
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
 #pragma unroll
         for (int chunk = 0; chunk < kTK / 8; ++chunk)  // 16-byte chunks 0..15 over 128 keys
           *reinterpret_cast<uint4*>(prow + (chunk >> 3) * kBox + (((chunk & 7) ^ sw) << 4)) =
@@ -548,9 +553,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       if (!ok) break;
       // Tile epilogue: wait for the last PV, then O / l -> bf16. The rows go
       // through the slot's P buffer (free: the last PV has read it) in the
-      // swizzled layout of P, and each warp writes its 32 rows back with
-      // whole-row stores (256 / D rows per instruction), skipping rows past
-      // the end of the text.
+      // 128-byte-swizzled layout of P. A warp whose 32 rows all lie inside the
+      // text hands them to one TMA tensor store (32 x 64 boxes); a warp that
+      // crosses the end of the text writes its rows back with whole-row
+      // stores (256 / D rows per instruction) and skips the rows past it.
       if (!wait_warp(&o_full[s], tiles & 1, p.status, INL_DEV_TIMEOUT_EPILOGUE, ok)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
@@ -569,26 +575,37 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           *reinterpret_cast<uint4*>(prow + (t >> 3) * kBox + (((t & 7) ^ sw) << 4)) = w;
         }
       }
-      __syncwarp();
-      {
+      const uint8_t* stage = sP + s * C::P_BYTES + quad * 32 * 128;  // this warp's 32 rows
+      if (ti.q0 + quad * 32 + 32 <= ti.L) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int b = 0; b < D / 64; ++b)
+            tma_store_2d(&tmO, stage + b * kBox, ti.head * D + b * 64, ti.s0 + ti.q0 + quad * 32);
+          bulk_commit_group();
+        }
+      } else {
+        __syncwarp();
         constexpr int CPR = D / 8;       // 16-byte chunks per output row
         constexpr int RPI = 32 / CPR;    // rows per store instruction
         const int c = lane % CPR;
-        const uint8_t* stage = sP + s * C::P_BYTES + (c >> 3) * kBox;
         __nv_bfloat16* out_head = p.out + ti.head * D + c * 8;
 #pragma unroll 4
         for (int i = 0; i < 32 / RPI; ++i) {
-          const int rr = quad * 32 + i * RPI + lane / CPR;  // tile row
-          const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 128 + (((c & 7) ^ (rr & 7)) << 4));
-          if (ti.q0 + rr < ti.L)
-            *reinterpret_cast<uint4*>(out_head + static_cast<long long>(ti.s0 + ti.q0 + rr) * p.ldo) = w;
+          const int rw = i * RPI + lane / CPR;  // row within the warp's 32
+          const uint4 w = *reinterpret_cast<const uint4*>(stage + (c >> 3) * kBox + rw * 128 +
+                                                          (((c & 7) ^ (rw & 7)) << 4));
+          if (ti.q0 + quad * 32 + rw < ti.L)
+            *reinterpret_cast<uint4*>(out_head + static_cast<long long>(ti.s0 + ti.q0 + quad * 32 + rw) * p.ldo) =
+                w;
         }
+        __syncwarp();  // the next P store rewrites these rows
       }
-      __syncwarp();  // the next P store rewrites these rows
       tc_fence_before();
       ++tiles;
       k += p.tstep;
     }
+    if (lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -606,6 +623,8 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   if (!make_tma_2d_bf16(&tq, a.q, total_rows, static_cast<long long>(a.hq) * D, a.ldq, kTQ, 64)) return -2;
   if (!make_tma_2d_bf16(&tk, a.k, total_rows, static_cast<long long>(a.hkv) * D, a.ldk, kTK, 64)) return -2;
   if (!make_tma_2d_bf16(&tv, a.v, total_rows, static_cast<long long>(a.hkv) * D, a.ldv, kTK, 64)) return -2;
+  CUtensorMap to;  // output rows, 32-row boxes (one warp's rows)
+  if (!make_tma_2d_bf16(&to, a.out, total_rows, static_cast<long long>(a.hq) * D, a.ldo, 32, 64)) return -2;
   // Pair the query heads of a GQA group when the group size is even.
   const bool pair = (a.hq / a.hkv) % 2 == 0;
   auto kern = pair ? fa_sm100_kernel<D, true> : fa_sm100_kernel<D, false>;
@@ -631,7 +650,7 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   p.window = a.window;
   p.status = a.status;
   const int grid = std::min(num_sms_cached(), p.n_tiles);
-  kern<<<grid, kFaThreads, C::SMEM, s>>>(tq, tk, tv, p);
+  kern<<<grid, kFaThreads, C::SMEM, s>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
