@@ -254,6 +254,7 @@ def run_ours(args, world, rank, local):
     launches = model.launch_count()
     prof = model.profile(-1)
     kinds = {name: model.profile(k) for k, name in enumerate(("qkv", "o", "gate_up", "down"))}
+    attn_prof = model.profile(100)  # attention launches
     model.set_profiling(False)
 
     # ---------------- end-to-end leg (e2e): pinned host ids -> host embeddings
@@ -310,6 +311,8 @@ def run_ours(args, world, rank, local):
                                          "algorithmic bytes per launch ~6.1e8",
                          "gemm_launches": prof["launches"], "gemm_ms": prof["ms"],
                          "gemm_share_of_step": prof["ms"] / ms if ms > 0 else None,
+                         "attention_ms_per_step": attn_prof["ms"] / args.steps,
+                         "attention_share_of_step": attn_prof["ms"] / ms if ms > 0 else None,
                          "by_projection": {k: {"ms_per_step": v["ms"] / args.steps,
                                                "tflops": v["flops"] / (v["ms"] / 1000.0) / 1e12 if v["ms"] else 0.0}
                                            for k, v in kinds.items()}},

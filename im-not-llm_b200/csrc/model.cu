@@ -824,6 +824,26 @@ int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int
   return r;
 }
 
+// Profiling kind of attention launches (GEMM kinds are 0..99).
+constexpr int kProfAttention = 100;
+
+// Attention launch, bracketed by profiling events when profiling is on.
+int run_attention(inl_model* m, const inl::AttnArgs& a, cudaStream_t s) {
+  ProfileRec rec{};
+  if (m->profiling) {
+    rec.start = take_event(m);
+    rec.stop = take_event(m);
+    rec.kind = kProfAttention;
+    cudaEventRecord(rec.start, s);
+  }
+  const int r = inl::attention(a, s);
+  if (m->profiling) {
+    cudaEventRecord(rec.stop, s);
+    m->prof.push_back(rec);
+  }
+  return r;
+}
+
 // bf16 tcgen05 GEMM with every epilogue field (folded norm, QKV, residual sums).
 int gemm(inl_model* m, inl::GemmArgs g, int kind) {
   ProfileRec rec{};
@@ -910,7 +930,7 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
     aa.q_block = inl::attention_q_block(1, c.d);
     aa.total_rows = T;
     aa.status = m->d_status;
-    INL_K_TRY(inl::attention(aa, s), "attention");
+    INL_K_TRY(run_attention(m, aa, s), "attention");
     m->launches++;
 
     inl::GemmArgs o;
@@ -1032,7 +1052,7 @@ int qwen3_tower(inl_model* m, const Batch& b, int n_work) {
     aa.q_block = inl::attention_q_block(bf, c.d);
     aa.total_rows = T;
     aa.status = m->d_status;
-    INL_K_TRY(inl::attention(aa, s), "attention");
+    INL_K_TRY(run_attention(m, aa, s), "attention");
     m->launches++;
     INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, c.H, q_out, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 1),
               "o projection");
@@ -1120,7 +1140,7 @@ int modernbert_tower(inl_model* m, const Batch& b, int n_work) {
     INL_K_TRY(inl::qk_norm_rope(qa, s), "rope");
     inl::AttnArgs aa = attn_args(m, b, n_work, qkv_cols, H, H);
     aa.window = global ? -1 : c.local_half_window;
-    INL_K_TRY(inl::attention(aa, s), "attention");
+    INL_K_TRY(run_attention(m, aa, s), "attention");
     m->launches += 2;
     INL_K_TRY(linear(m, m->attn.p, H, w.wo, T, H, H, INL_EPI_RESID_BF16, 0, m->h.p, H, m->h.p, H, 1), "Wo");
     INL_K_TRY(inl::layer_norm(m->h.p, bf, H, w.ln2, nullptr, c.norm_eps, T, H, m->xn.p, bf, H, s), "mlp norm");
@@ -1160,7 +1180,7 @@ int gemma_tower(inl_model* m, const Batch& b, int n_work) {
     inl::AttnArgs aa = attn_args(m, b, n_work, qkv_cols, q_out, kv_out);
     aa.scale = c.attn_scale;
     aa.window = full ? -1 : c.sliding_window;
-    INL_K_TRY(inl::attention(aa, s), "attention");
+    INL_K_TRY(run_attention(m, aa, s), "attention");
     m->launches += 3;
     INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, H, q_out, plain, 0, m->xn.p, H, nullptr, 0, 1), "o projection");
     INL_K_TRY(inl::add_rms_norm(m->h.p, m->xn.p, bf, w.ln1_post, c.eps, T, H, s), "post-attention norm");
@@ -1585,7 +1605,7 @@ int inl_cuda_model_profile(inl_model* m, int kind, int* launches, double* total_
   int n = 0;
   double ms = 0, fl = 0;
   for (const auto& r : m->prof) {
-    if (kind >= 0 && r.kind != kind) continue;
+    if (kind >= 0 ? r.kind != kind : r.kind >= kProfAttention) continue;
     float t = 0;
     cudaEventElapsedTime(&t, r.start, r.stop);
     ms += t;

@@ -145,10 +145,11 @@ INL_API int inl_cuda_token_positions(const int32_t* cu, int n, int T, int32_t* p
 INL_API int inl_cuda_last_token_norm_l2(const void* h, int h_dtype, int64_t ldh, const int32_t* cu, int n,
                                         const float* w, float eps, int H, float* out, void* stream);
 
-/* Measurement hooks: with profiling on, every GEMM launch of the model is
- * bracketed by CUDA events on the model's stream. kind: 0 qkv, 1 o, 2 gate/up,
- * 3 down, 4 Dense head, -1 all. The reference has no counterpart (its
- * profiling was external, nsys). */
+/* Measurement hooks: with profiling on, every GEMM and attention launch of
+ * the model is bracketed by CUDA events on the model's stream. kind: 0 qkv,
+ * 1 o, 2 gate/up, 3 down, 4 Dense head, -1 all GEMMs; 100 attention (flops
+ * reported as 0). The reference has no counterpart (its profiling was
+ * external, nsys). */
 INL_API int inl_cuda_model_set_profiling(inl_model* m, int enable);
 INL_API int inl_cuda_model_profile(inl_model* m, int kind, int* launches, double* total_ms, double* flops);
 
