@@ -334,8 +334,8 @@ def run_ours(args, world, rank, local):
 
 # Mean DRAM bytes (read + write) per GEMM launch (gemm_bf16_tn_kernel for QKV,
 # gemm_bf16_pair_kernel for o, gate/up and down) over one config-5 bench step
-# (64.6k tokens), measured with ncu: 464.6 MB.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 464.6e6
+# (64.6k tokens), measured with ncu: 465.4 MB.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 465.4e6
 
 KERNEL_CASES = {
     # name: (M tokens, N, K, epilogue) — the four projections of one Qwen3-0.6B layer
