@@ -186,7 +186,7 @@ def run_reference(args, world, rank):
                          "sample": f"{args.steps} samples of ~{CPU_SAMPLE_TOKENS} tokens of the cfg5 corpus, numpy f32 restatement of crates/inl-text/src/qwen3/mod.rs with BLAS on {cores} threads"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args, world, rank, local):
@@ -328,7 +328,7 @@ def run_ours(args, world, rank, local):
             line["cpu_baseline"] = {"value": r, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                                     "sample": f"{k} texts / {n} tokens of the cfg5 corpus through the numpy f32 "
                                               f"restatement (oracle/qwen3.py), BLAS on {os.cpu_count()} threads, {dt:.1f}s"}
-        print(json.dumps(line), flush=True)
+        emit(line)
     model.close()
 
 
@@ -436,7 +436,18 @@ def run_kernel_case(name: str, reps: int = 3):
         raise SystemExit(f"{name}: a device wait ran past its limit (status {code})")
 
 
+# The benchmark's stdout carries exactly one JSON line. main() keeps the real
+# stdout here and points file descriptor 1 at stderr, so whatever a library
+# prints there (NCCL's version banner under torchrun, for one) goes to stderr.
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    print(json.dumps(line), file=_JSON_OUT or sys.stdout, flush=True)
+
+
 def main():
+    global _JSON_OUT
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention", "attention_cfg5", "gemm_qkv_fused",
                                                               "gemm_gateup_fused"],
@@ -451,6 +462,9 @@ def main():
     if args.case:
         run_kernel_case(args.case)
         return
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))
     if args.impl == "reference":
