@@ -15,18 +15,22 @@
 //   warp 0     TMA producer: each slot's Q tile, and K / V tiles of 128 keys
 //              into one ring, in exactly the order the MMA warp consumes them
 //              (so the ring can neither deadlock nor reorder);
-//   warp 1     TMEM allocation and tcgen05.mma issue. It alternates between
-//              the slots in units "S = Q K(j)^T; O += P(j-1) V(j-1)". S(j) only
-//              needs the softmax warps to have read S(j-1) out of TMEM, so it
-//              runs while they still compute P(j-1), and the next block's
-//              scores are ready when they finish;
+//   warp 1     TMEM allocation and tcgen05.mma issue, in units
+//              "S = Q K(j)^T; O += P(j-1) V(j-1)": one unit serves both slots
+//              of a GQA pair, or the units alternate between the slots. S(j)
+//              only needs the softmax warps to have read S(j-1) out of TMEM,
+//              so it runs while they still compute P(j-1), and the next
+//              block's scores are ready when they finish;
 //   warps 2-5  softmax of slot 0, warps 6-9 of slot 1: thread = query row =
 //              TMEM lane. Reads S with tcgen05.ld, masks, keeps a running row
 //              max m and sum l, writes P = exp2(s - m) as bf16 into shared
 //              memory in the K-major 128-byte-swizzle layout the MMA reads. m
 //              is only raised when the block max exceeds it by more than 2^8,
-//              and then O is rescaled in TMEM. At the end of a tile, O / l is
-//              written as bf16.
+//              and then O is rescaled in TMEM. A quarter of the exp2 run as a
+//              cubic on the FMA pipe, the rest on the special-function unit.
+//              At the end of a tile, O / l goes as bf16 through the slot's P
+//              buffer to one TMA tensor store per warp (whole-row stores for a
+//              warp that crosses the end of the text).
 // Per slot, barriers order the shared buffers: s_free (the scores were read,
 // S may be overwritten), pv_done (PV(j-1) is complete: P's buffer may be
 // rewritten and O rescaled; the softmax warps compute exp2 into registers
