@@ -6,10 +6,11 @@ from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  
 from .model import CudaModel  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder,  # noqa: F401
                      SparseEncoder, SparseVector, TextEmbedder, TextOptions)
-from . import planner, synthetic  # noqa: F401
+from .text import TextTokenizer  # noqa: F401
+from . import planner, synthetic, text  # noqa: F401
 
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "InferenceError",
-    "InlError", "InvalidInputError", "LateEncoder", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions", "TimeoutError_",
-    "planner", "synthetic",
+    "InlError", "InvalidInputError", "LateEncoder", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
+    "TextTokenizer", "TimeoutError_", "planner", "synthetic", "text",
 ]

@@ -16,8 +16,10 @@
 * ``DataParallelEmbedder`` — one model per GPU, one host thread per GPU,
   packed batches assigned longest-processing-time first; no collective.
 
-Inputs are token-id lists: tokenization is the caller's (the reference's
-tokenizer front end is not part of this library).
+Inputs are strings or token-id lists. Strings go through the model's
+tokenizer.json (``text.TextTokenizer``, the reference's settings: special
+tokens, truncation by the tokenizer) with the query / passage prefixes of the
+reference's options. Token-id lists are truncated to ``max_length``.
 """
 from __future__ import annotations
 
@@ -31,12 +33,15 @@ import numpy as np
 from .errors import InlError
 from .model import CudaModel
 from .planner import assign_lpt, batch_cost, longest_first, pack, plan_packed
+from .text import TextTokenizer
 
 DEFAULT_MAX_LENGTH = 2048          # crates/inl-text/src/native.rs:23
 DEFAULT_BATCH_SIZE = 64            # crates/inl-text/src/native.rs:26
 DEFAULT_TIMEOUT_SECONDS = 60       # crates/inl-text/src/native.rs:32
 DEFAULT_PACKED_TOKENS = 65536      # packed real tokens per forward on one B200
 MATRYOSHKA_DIMS = (128, 256, 512, 768)  # crates/inl-text/src/native.rs:82-88
+SPARSE_QUERY_PREFIX = "[Q] "       # crates/inl-sparse/src/native.rs:44
+SPARSE_PASSAGE_PREFIX = "[D] "     # crates/inl-sparse/src/native.rs:45
 
 
 class BatchDeadline:
@@ -107,6 +112,16 @@ class TextOptions:
     timeout_seconds: float = DEFAULT_TIMEOUT_SECONDS
     per_batch_timeout_seconds: float | None = None
     output_dim: int | None = None
+    query_prefix: str | None = None    # prepended to string queries (embed_query / encode_query)
+    passage_prefix: str | None = None  # prepended to string inputs of embed / encode
+
+    @classmethod
+    def sparse(cls, **kw) -> "TextOptions":
+        """The sparse encoder's defaults: the "[Q] " / "[D] " markers
+        (SparseOptions::default, crates/inl-sparse/src/native.rs:80-95)."""
+        kw.setdefault("query_prefix", SPARSE_QUERY_PREFIX)
+        kw.setdefault("passage_prefix", SPARSE_PASSAGE_PREFIX)
+        return cls(**kw)
 
     def batch_timeout(self) -> float:
         """crates/inl-text/src/native.rs:739-752."""
@@ -127,9 +142,11 @@ class _Loaded:
 
 
 class _EngineBase:
-    def __init__(self, loader: Callable[[], CudaModel], options: TextOptions):
+    def __init__(self, loader: Callable[[], CudaModel], options: TextOptions,
+                 tokenizer: TextTokenizer | None = None):
         self._loader = loader
         self.options = options
+        self.tokenizer = tokenizer
         self.deadline = BatchDeadline()
         self._load_lock = threading.Lock()
         self._loaded: _Loaded | None = None
@@ -152,8 +169,31 @@ class _EngineBase:
             self._loaded = None
             return True
 
-    def token_counts(self, tokens: Sequence[Sequence[int]]) -> list[int]:
-        return [len(t) for t in tokens]
+    def _is_text(self, inputs: list) -> bool:
+        kinds = {isinstance(x, str) for x in inputs}
+        if len(kinds) > 1:
+            raise InlError.invalid_input("inputs mix strings and token-id lists")
+        if kinds == {True} and self.tokenizer is None:
+            raise InlError.config("string inputs need a tokenizer (tokenizer=TextTokenizer.from_file(...))")
+        return kinds == {True}
+
+    def _prepare(self, inputs: Sequence, prefix: str | None) -> list[np.ndarray]:
+        """Strings: prefix prepended, then tokenized (the tokenizer truncates
+        to max_length). Token-id lists: truncated to max_length."""
+        items = list(inputs)
+        if self._is_text(items):
+            if prefix:
+                items = [prefix + t for t in items]
+            return self.tokenizer.encode(items, self.options.max_length)
+        return _truncate(items, self.options.max_length)
+
+    def token_counts(self, inputs: Sequence) -> list[int]:
+        """Tokens per input before truncation, as given (no prefix;
+        crates/inl-text/src/native.rs:502-520)."""
+        items = list(inputs)
+        if self._is_text(items):
+            return self.tokenizer.counts(items)
+        return [len(t) for t in items]
 
     def _run_batches(self, what: str, texts: list[np.ndarray], forward) -> list:
         if not texts:
@@ -200,8 +240,18 @@ class TextEmbedder(_EngineBase):
             raise InlError.config(f"output_dim {dim} exceeds the model's embeddings")
         return dim
 
-    def embed(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
-        texts = _truncate(tokens, self.options.max_length)
+    def embed(self, inputs: Sequence) -> list[np.ndarray]:
+        """Passages (strings get the passage prefix) or token-id lists."""
+        return self._embed(self._prepare(inputs, self.options.passage_prefix))
+
+    def embed_query(self, text: str) -> np.ndarray:
+        """One search query with the query prefix (crates/inl-text/src/native.rs:534-546)."""
+        out = self._embed(self._prepare([text], self.options.query_prefix))
+        if not out:
+            raise InlError.inference("empty response")
+        return out[0]
+
+    def _embed(self, texts: list[np.ndarray]) -> list[np.ndarray]:
         if not texts:
             return []
         out_dim = self._output_dim(self._model().model)
@@ -220,8 +270,9 @@ class LateEncoder(_EngineBase):
         return EngineInfo(self.options.id, m.info()["multivector_dim"], m.dtype, f"cuda:{m.device}", "fused",
                           self.options.max_length)
 
-    def encode(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
-        texts = _truncate(tokens, self.options.max_length)
+    def encode(self, inputs: Sequence) -> list[np.ndarray]:
+        """Strings (passage prefix, if set) or token-id lists."""
+        texts = self._prepare(inputs, self.options.passage_prefix)
 
         def forward(model: CudaModel, ids, cu):
             flat = model.encode_multivector(ids, cu)
@@ -264,9 +315,18 @@ class SparseEncoder(_EngineBase):
         return EngineInfo(self.options.id, m.info()["sparse_dim"], m.dtype, f"cuda:{m.device}", "fused",
                           self.options.max_length)
 
-    def encode(self, tokens: Sequence[Sequence[int]]) -> list[SparseVector]:
-        texts = _truncate(tokens, self.options.max_length)
+    def encode(self, inputs: Sequence) -> list[SparseVector]:
+        """Documents (strings get the passage marker) or token-id lists."""
+        return self._encode(self._prepare(inputs, self.options.passage_prefix))
 
+    def encode_query(self, text: str) -> SparseVector:
+        """One query with the query marker (crates/inl-sparse/src/native.rs:310-317)."""
+        out = self._encode(self._prepare([text], self.options.query_prefix))
+        if not out:
+            raise InlError.inference("empty response")
+        return out[0]
+
+    def _encode(self, texts: list[np.ndarray]) -> list[SparseVector]:
         def forward(model: CudaModel, ids, cu):
             dense = model.encode_sparse(ids, cu)
             if not np.all(np.isfinite(dense)):  # crates/inl-sparse/src/native.rs:536-540

@@ -1,0 +1,119 @@
+"""Text front end (im-not-llm_b200/text.py and the facades' string inputs).
+
+The tokenizer path is pinned against the reference's tiny_embeddinggemma2
+fixture: its golden.json records the token count of every text at
+max_length 64 and 9 (crates/inl-text/src/gemma2.rs:941-967), and
+tests/test_oracle_gemma.py restates the fixture's tokenizer.json by hand.
+The library must give the same ids, keep the template's special tokens when
+it truncates, and count tokens before truncation."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import im_not_llm_b200 as inl
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_embeddinggemma2"
+
+
+def _tok():
+    return inl.TextTokenizer.from_file(GOLDEN / "tokenizer.json")
+
+
+def _restated(text, max_length, vocab):
+    words = [vocab.get(w, vocab["<unk>"]) for w in text.lower().split()]
+    return [vocab["<bos>"]] + words[: max(0, max_length - 2)] + [vocab["<eos>"]]
+
+
+def test_library_ids_match_restatement_and_golden_lengths():
+    golden = json.loads((GOLDEN / "golden.json").read_text())
+    vocab = json.loads((GOLDEN / "tokenizer.json").read_text())["model"]["vocab"]
+    tok = _tok()
+    for case in golden["cases"]:
+        ids = tok.encode(golden["texts"], case["max_length"])
+        assert [len(x) for x in ids] == case["lengths"]
+        for text, got in zip(golden["texts"], ids):
+            assert got.dtype == np.uint32
+            assert got.tolist() == _restated(text, case["max_length"], vocab)
+
+
+def test_truncation_keeps_special_tokens_and_counts_are_untruncated():
+    vocab = json.loads((GOLDEN / "tokenizer.json").read_text())["model"]["vocab"]
+    tok = _tok()
+    text = " ".join(["the"] * 40)
+    (ids,) = tok.encode([text], 9)
+    assert len(ids) == 9 and ids[0] == vocab["<bos>"] and ids[-1] == vocab["<eos>"]
+    assert tok.counts([text]) == [42]
+    # one truncating copy per max_length, independent of each other
+    assert len(tok.encode([text], 5)[0]) == 5 and len(tok.encode([text], 64)[0]) == 42
+
+
+def test_unparsable_tokenizer_is_an_inference_error(tmp_path):
+    bad = tmp_path / "tokenizer.json"
+    bad.write_text("{ not json")
+    with pytest.raises(inl.InferenceError):
+        inl.TextTokenizer.from_file(bad)
+    with pytest.raises(inl.ConfigError):
+        _tok().encode(["x"], 0)
+
+
+class RecordingModel:
+    """Stands in for CudaModel: records the id segments it receives."""
+
+    def __init__(self):
+        self.dtype, self.device, self.seen = "bf16", 0, []
+
+    def info(self):
+        return {"dense_dim": 2, "arch": 0, "multivector_dim": 2, "sparse_dim": 4}
+
+    def _segments(self, ids, cu):
+        segs = [ids[cu[i]:cu[i + 1]].tolist() for i in range(len(cu) - 1)]
+        self.seen.extend(segs)
+        return segs
+
+    def embed(self, ids, cu, out_dim=0):
+        return np.array([[len(s), s[0]] for s in self._segments(ids, cu)], dtype=np.float32)
+
+    def encode_sparse(self, ids, cu):
+        out = np.zeros((len(cu) - 1, 4), dtype=np.float32)
+        for i, s in enumerate(self._segments(ids, cu)):
+            out[i, len(s) % 4] = 1.0
+        return out
+
+    def close(self):
+        pass
+
+
+def test_embedder_applies_passage_and_query_prefixes():
+    tok = _tok()
+    model = RecordingModel()
+    opts = inl.TextOptions(max_length=64, passage_prefix="title: none | text: ", query_prefix="query: ")
+    e = inl.TextEmbedder(lambda: model, opts, tokenizer=tok)
+    out = e.embed(["A quick test", "b"])
+    want = tok.encode(["title: none | text: A quick test", "title: none | text: b"], 64)
+    assert model.seen == [w.tolist() for w in want]
+    assert [v[0] for v in out] == [len(w) for w in want]
+    model.seen.clear()
+    e.embed_query("what is it")
+    assert model.seen == [tok.encode(["query: what is it"], 64)[0].tolist()]
+    # token_counts: as given, no prefix, before truncation
+    assert e.token_counts(["A quick test"]) == tok.counts(["A quick test"])
+    # token ids still work and skip the tokenizer
+    model.seen.clear()
+    e.embed([np.array([5, 6, 7], dtype=np.uint32)])
+    assert model.seen == [[5, 6, 7]]
+
+
+def test_sparse_encoder_markers_and_input_errors():
+    tok = _tok()
+    model = RecordingModel()
+    s = inl.SparseEncoder(lambda: model, inl.TextOptions.sparse(max_length=9), tokenizer=tok)
+    s.encode(["some document text"])
+    s.encode_query("a query")
+    assert model.seen == [tok.encode(["[D] some document text"], 9)[0].tolist(),
+                          tok.encode(["[Q] a query"], 9)[0].tolist()]
+    with pytest.raises(inl.InvalidInputError):
+        s.encode(["text", [1, 2, 3]])
+    with pytest.raises(inl.ConfigError):
+        inl.TextEmbedder(lambda: model, inl.TextOptions()).embed(["no tokenizer"])
