@@ -20,7 +20,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 FIXTURES = {
     "tiny_splade": ("crates/inl-sparse/tests/fixtures/tiny_splade",
-                    ["config.json", "model.safetensors", "golden.json", "1_ShiftedTopKSpladePooling/config.json"]),
+                    ["config.json", "model.safetensors", "golden.json", "1_ShiftedTopKSpladePooling/config.json",
+                     "tokenizer.json"]),
     "tiny_embeddinggemma2": ("crates/inl-text/tests/fixtures/tiny_embeddinggemma2",
                              ["config.json", "model.safetensors", "golden.json", "tokenizer.json"]),
 }

@@ -1,9 +1,13 @@
 """Text front end (im-not-llm_b200/text.py and the facades' string inputs).
 
-The tokenizer path is pinned against the reference's tiny_embeddinggemma2
-fixture: its golden.json records the token count of every text at
-max_length 64 and 9 (crates/inl-text/src/gemma2.rs:941-967), and
-tests/test_oracle_gemma.py restates the fixture's tokenizer.json by hand.
+The tokenizer path is pinned against two of the reference's own fixtures.
+
+* tiny_embeddinggemma2: its golden.json records the token count of every
+  text at max_length 64 and 9 (crates/inl-text/src/gemma2.rs:941-967), and
+  tests/test_oracle_gemma.py restates the fixture's tokenizer.json by hand.
+* tiny_splade: its golden.json records the ids the reference fed its model
+  for documents and queries at max_length 64 and 12.
+
 The library must give the same ids, keep the template's special tokens when
 it truncates, and count tokens before truncation."""
 import json
@@ -117,3 +121,21 @@ def test_sparse_encoder_markers_and_input_errors():
         s.encode(["text", [1, 2, 3]])
     with pytest.raises(inl.ConfigError):
         inl.TextEmbedder(lambda: model, inl.TextOptions()).embed(["no tokenizer"])
+
+
+SPLADE = Path(__file__).resolve().parent / "golden" / "tiny_splade"
+
+
+def test_sparse_markers_and_truncation_reproduce_the_references_recorded_ids():
+    """tiny_splade's golden.json records, per case, the ids the reference fed
+    its model: the "[D] " / "[Q] " marker prepended (SparseEncoder::encode /
+    encode_query), special tokens added, the tokenizer truncating at
+    max_length 64 and 12 with [SEP] kept (crates/inl-sparse/src/modernbert.rs:1014-1057)."""
+    golden = json.loads((SPLADE / "golden.json").read_text())
+    tok = inl.TextTokenizer.from_file(SPLADE / "tokenizer.json")
+    opts = inl.TextOptions.sparse()
+    for case in golden["cases"]:
+        prefix = opts.passage_prefix if case["kind"] == "document" else opts.query_prefix
+        got = tok.encode([prefix + t for t in case["texts"]], case["max_length"])
+        for rows in (case["batched"], case["alone"]):
+            assert [g.tolist() for g in got] == [r["ids"] for r in rows], case["kind"]
