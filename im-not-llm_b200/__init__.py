@@ -4,13 +4,13 @@ host layer that mirrors the reference's engine API."""
 from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  # noqa: F401
                      TimeoutError_)
 from .model import CudaModel  # noqa: F401
-from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder,  # noqa: F401
+from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder, LateTask,  # noqa: F401
                      SparseEncoder, SparseVector, TextEmbedder, TextOptions)
 from .text import TextTokenizer  # noqa: F401
 from . import planner, synthetic, text  # noqa: F401
 
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "InferenceError",
-    "InlError", "InvalidInputError", "LateEncoder", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
+    "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
     "TextTokenizer", "TimeoutError_", "planner", "synthetic", "text",
 ]

@@ -23,9 +23,11 @@ reference's options. Token-id lists are truncated to ``max_length``.
 """
 from __future__ import annotations
 
+import json
 import threading
 import time
 from dataclasses import dataclass, field
+from pathlib import Path
 from typing import Callable, Sequence
 
 import numpy as np
@@ -262,25 +264,104 @@ class TextEmbedder(_EngineBase):
         return self._run_batches("native embedding", texts, forward)
 
 
+@dataclass(frozen=True)
+class LateTask:
+    """TaskSetup (crates/inl-late/src/native.rs:122-128): the prompt put in
+    front of string inputs, the context in tokens (prompt included), and the
+    token ids whose vectors are dropped from the output."""
+    prompt: str = ""
+    length: int = DEFAULT_MAX_LENGTH
+    skip: frozenset = frozenset()
+
+    @staticmethod
+    def from_model_dir(model_dir: str | Path, tokenizer: TextTokenizer,
+                       max_length: int | None = None) -> dict[str, "LateTask"]:
+        """Query and document setups of a Sentence-Transformers late model
+        directory, as crates/inl-late/src/native.rs:455-620 reads them:
+        prompts from config_sentence_transformers.json; query_length /
+        document_length from sentence_bert_config.json (else max_seq_length,
+        else the model's max_position_embeddings), capped by ``max_length``
+        and the positions; the MultiVectorMask module's skiplist (a word
+        counts only when it is one vocabulary token; tasks default to
+        ["document"]; keep_only_token_ids is not supported)."""
+        d = Path(model_dir)
+
+        def read(name, default):
+            f = d / name
+            return json.loads(f.read_text()) if f.exists() else default
+
+        cfg = read("config.json", {})
+        positions = cfg.get("max_position_embeddings") or cfg.get("text_config", {}).get("max_position_embeddings")
+        st = read("sentence_bert_config.json", {})
+        prompts = read("config_sentence_transformers.json", {}).get("prompts") or {}
+        mask = {"skiplist_words": [], "skiplist_tasks": []}
+        for module in read("modules.json", []):
+            if module.get("type", "").rsplit(".", 1)[-1] == "MultiVectorMask":
+                mask = read(str(Path(module.get("path", "")) / "config.json"), {})
+        if mask.get("keep_only_token_ids") is not None:
+            raise InlError.inference("native late model keep_only_token_ids is not supported")
+        ids = (tokenizer.token_to_id(w) for w in mask.get("skiplist_words", []))
+        skip = frozenset(i for i in ids if i is not None)
+        skip_tasks = mask.get("skiplist_tasks", ["document"])
+        fallback = st.get("max_seq_length") or positions or DEFAULT_MAX_LENGTH
+
+        def cap(length):
+            v = length if length is not None else fallback
+            if max_length is not None:
+                v = min(v, max_length)
+            return min(v, positions) if positions else v
+
+        return {name: LateTask(prompts.get(name) or "", cap(st.get(f"{name}_length")),
+                               skip if name in skip_tasks else frozenset())
+                for name in ("query", "document")}
+
+
 class LateEncoder(_EngineBase):
-    """LateEngine over a CudaModel with a Dense head attached."""
+    """LateEngine over a CudaModel with a Dense head attached:
+    ``encode(inputs, task)`` with task "query" or "document"
+    (crates/inl-late/src/native.rs:292-374, 631-683). String inputs get the
+    task's prompt and are cut at the task's length after tokenizing (the
+    tokenizer does not truncate); token-id lists are cut at the task's
+    length. The vectors of the task's skiplist tokens are dropped, and a
+    non-finite kept value is an error."""
+
+    TASKS = ("query", "document")
+
+    def __init__(self, loader: Callable[[], CudaModel], options: TextOptions,
+                 tokenizer: TextTokenizer | None = None, tasks: dict[str, LateTask] | None = None):
+        super().__init__(loader, options, tokenizer)
+        default = LateTask(length=options.max_length)
+        self.tasks = {name: (tasks or {}).get(name, default) for name in self.TASKS}
 
     def load(self) -> EngineInfo:
         m = self._model().model
         return EngineInfo(self.options.id, m.info()["multivector_dim"], m.dtype, f"cuda:{m.device}", "fused",
-                          self.options.max_length)
+                          self.tasks["document"].length)
 
-    def encode(self, inputs: Sequence) -> list[np.ndarray]:
-        """Strings (passage prefix, if set) or token-id lists."""
-        texts = self._prepare(inputs, self.options.passage_prefix)
+    def encode(self, inputs: Sequence, task: str = "document") -> list[np.ndarray]:
+        setup = self.tasks.get(task)
+        if setup is None:
+            raise InlError.invalid_input(f"unknown late task {task!r}: use 'query' or 'document'")
+        items = list(inputs)
+        if self._is_text(items):
+            rows = [ids[:setup.length] for ids in self.tokenizer.encode_untruncated([setup.prompt + t for t in items])]
+        else:
+            rows = _truncate(items, setup.length)
+        skip = np.fromiter(sorted(setup.skip), dtype=np.uint32) if setup.skip else None
 
         def forward(model: CudaModel, ids, cu):
             flat = model.encode_multivector(ids, cu)
-            if not np.all(np.isfinite(flat)):  # crates/inl-late/src/native.rs:675-679
-                raise InlError.inference("native late encoder produced non-finite values")
-            return [flat[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
+            out = []
+            for i in range(len(cu) - 1):
+                m = flat[cu[i]:cu[i + 1]]
+                if skip is not None:
+                    m = m[~np.isin(ids[cu[i]:cu[i + 1]], skip)]
+                if not np.all(np.isfinite(m)):  # crates/inl-late/src/native.rs:675-679
+                    raise InlError.inference("native late encoder produced non-finite values")
+                out.append(m)
+            return out
 
-        return self._run_batches("native late", texts, forward)
+        return self._run_batches("native late", rows, forward)
 
 
 class SparseVector:

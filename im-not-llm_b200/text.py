@@ -77,10 +77,19 @@ class TextTokenizer:
             raise InlError.inference(f"native tokenizer encode failed: {e}") from e
         return [np.asarray(e.ids, dtype=np.uint32) for e in encs]
 
-    def counts(self, texts: Sequence[str]) -> list[int]:
-        """Tokens per text as the model would see them before truncation."""
+    def encode_untruncated(self, texts: Sequence[str]) -> list[np.ndarray]:
+        """Ids per text with special tokens and no truncation (the late
+        encoder cuts them itself, crates/inl-late/src/native.rs:292-305)."""
         try:
             encs = self._plain.encode_batch(list(texts), add_special_tokens=True)
         except Exception as e:
             raise InlError.inference(f"native tokenizer encode failed: {e}") from e
-        return [len(e.ids) for e in encs]
+        return [np.asarray(e.ids, dtype=np.uint32) for e in encs]
+
+    def counts(self, texts: Sequence[str]) -> list[int]:
+        """Tokens per text as the model would see them before truncation."""
+        return [len(x) for x in self.encode_untruncated(texts)]
+
+    def token_to_id(self, token: str) -> int | None:
+        """The id of ``token`` if it is one vocabulary entry, else None."""
+        return self._plain.token_to_id(token)

@@ -12,6 +12,13 @@ checkpoint plus the golden outputs the reference's tests assert against.
   * tiny_embeddinggemma2   crates/inl-text/tests/fixtures/tiny_embeddinggemma2/
                            (EmbeddingGemma 2 text tower; asserted by
                            crates/inl-text/src/gemma2.rs:941-967, |d| < 2e-5)
+  * tiny_qwen3_5_late      crates/inl-late/tests/fixtures/tiny_qwen3_5_late/
+                           (the late model's task setup only: prompts, lengths,
+                           MultiVectorMask skiplist, tokenizer and golden.json,
+                           whose per-task token counts and kept-vector counts
+                           pin the host's task handling; not the weights, as
+                           the Qwen3.5 tower is not built here). Directory
+                           layout kept, as the loader follows modules.json.
 """
 import shutil
 import sys
@@ -24,7 +31,11 @@ FIXTURES = {
                      "tokenizer.json"]),
     "tiny_embeddinggemma2": ("crates/inl-text/tests/fixtures/tiny_embeddinggemma2",
                              ["config.json", "model.safetensors", "golden.json", "tokenizer.json"]),
+    "tiny_qwen3_5_late": ("crates/inl-late/tests/fixtures/tiny_qwen3_5_late",
+                          ["config.json", "config_sentence_transformers.json", "sentence_bert_config.json",
+                           "modules.json", "2_MultiVectorMask/config.json", "tokenizer.json", "golden.json"]),
 }
+KEEP_DIRS = {"tiny_qwen3_5_late"}
 
 
 def main(ref_root: str) -> None:
@@ -32,7 +43,7 @@ def main(ref_root: str) -> None:
     for name, (rel, files) in FIXTURES.items():
         for f in files:
             src = ref / rel / f
-            dst = HERE / name / f.replace("/", "__")
+            dst = HERE / name / (f if name in KEEP_DIRS else f.replace("/", "__"))
             dst.parent.mkdir(parents=True, exist_ok=True)
             shutil.copyfile(src, dst)
             print(f"{src} -> {dst.relative_to(HERE)}")
