@@ -246,6 +246,19 @@ class TextEmbedder(_EngineBase):
         """Passages (strings get the passage prefix) or token-id lists."""
         return self._embed(self._prepare(inputs, self.options.passage_prefix))
 
+    def count_truncated(self, texts: Sequence[str]) -> int:
+        """How many of ``texts`` (passage prefix applied) reach ``max_length``
+        tokens and are therefore truncated (crates/inl-text/src/native.rs:372-404).
+        Texts shorter than ``max_length`` UTF-8 bytes are skipped untokenized,
+        as there: byte-level BPE gives at most one token per byte."""
+        prefix = self.options.passage_prefix or ""
+        cands = [prefix + t for t in texts if len((prefix + t).encode()) >= self.options.max_length]
+        if not cands:
+            return 0
+        if self.tokenizer is None:
+            raise InlError.config("count_truncated needs a tokenizer")
+        return sum(n >= self.options.max_length for n in self.tokenizer.counts(cands))
+
     def embed_query(self, text: str) -> np.ndarray:
         """One search query with the query prefix (crates/inl-text/src/native.rs:534-546)."""
         out = self._embed(self._prepare([text], self.options.query_prefix))
@@ -399,6 +412,20 @@ class SparseEncoder(_EngineBase):
     def encode(self, inputs: Sequence) -> list[SparseVector]:
         """Documents (strings get the passage marker) or token-id lists."""
         return self._encode(self._prepare(inputs, self.options.passage_prefix))
+
+    def count_truncated(self, texts: Sequence[str]) -> int:
+        """How many of ``texts`` reach the context limit once the passage
+        marker and special tokens are counted (crates/inl-sparse/src/native.rs:319-348):
+        texts shorter than ``max_length`` UTF-8 bytes are skipped, the rest are
+        tokenized with truncation and counted when they come back at the limit."""
+        cands = [(self.options.passage_prefix or "") + t for t in texts
+                 if len(t.encode()) >= self.options.max_length]
+        if not cands:
+            return 0
+        if self.tokenizer is None:
+            raise InlError.config("count_truncated needs a tokenizer")
+        return sum(len(ids) >= self.options.max_length
+                   for ids in self.tokenizer.encode(cands, self.options.max_length))
 
     def encode_query(self, text: str) -> SparseVector:
         """One query with the query marker (crates/inl-sparse/src/native.rs:310-317)."""

@@ -139,3 +139,21 @@ def test_sparse_markers_and_truncation_reproduce_the_references_recorded_ids():
         got = tok.encode([prefix + t for t in case["texts"]], case["max_length"])
         for rows in (case["batched"], case["alone"]):
             assert [g.tolist() for g in got] == [r["ids"] for r in rows], case["kind"]
+
+
+def test_count_truncated_dense_and_sparse():
+    tok = _tok()
+    model = RecordingModel()
+    texts = ["a b c d e f g h i j k", "short", "x " * 3, "w1 w2 w3 w4 w5 w6 w7"]
+    counts = tok.counts(texts)  # <bos> ... <eos>: 13, 3, 5, 9
+    e = inl.TextEmbedder(lambda: model, inl.TextOptions(max_length=9), tokenizer=tok)
+    assert e.count_truncated(texts) == sum(n >= 9 for n in counts) == 2
+    # the passage prefix counts, and texts under max_length bytes are not tokenized
+    e2 = inl.TextEmbedder(lambda: model, inl.TextOptions(max_length=9, passage_prefix="p q r s "), tokenizer=tok)
+    assert e2.count_truncated(texts) == sum(n >= 9 for n in tok.counts(["p q r s " + t for t in texts]))
+    s = inl.SparseEncoder(lambda: model, inl.TextOptions.sparse(max_length=9), tokenizer=tok)
+    # sparse: the byte gate looks at the text without its marker
+    want = sum(len(t.encode()) >= 9 and len(ids) >= 9
+               for t, ids in zip(texts, tok.encode(["[D] " + t for t in texts], 9)))
+    assert s.count_truncated(texts) == want == 2  # "short" and "x x x " are under 9 bytes
+    assert model.seen == []  # nothing reached the model
