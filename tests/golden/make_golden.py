@@ -13,12 +13,12 @@ checkpoint plus the golden outputs the reference's tests assert against.
                            (EmbeddingGemma 2 text tower; asserted by
                            crates/inl-text/src/gemma2.rs:941-967, |d| < 2e-5)
   * tiny_qwen3_5_late      crates/inl-late/tests/fixtures/tiny_qwen3_5_late/
-                           (the late model's task setup only: prompts, lengths,
-                           MultiVectorMask skiplist, tokenizer and golden.json,
-                           whose per-task token counts and kept-vector counts
-                           pin the host's task handling; not the weights, as
-                           the Qwen3.5 tower is not built here). Directory
-                           layout kept, as the loader follows modules.json.
+                           (Qwen3.5 tower with Gated DeltaNet and gated full
+                           attention, 1_Dense, the document skiplist;
+                           asserted by crates/inl-late/tests/tiny_golden.rs,
+                           max |d| < 1e-4: pins oracle/qwen3_5.py and the
+                           host's task handling). Directory layout kept, as
+                           the loader follows modules.json.
 """
 import shutil
 import sys
@@ -33,7 +33,8 @@ FIXTURES = {
                              ["config.json", "model.safetensors", "golden.json", "tokenizer.json"]),
     "tiny_qwen3_5_late": ("crates/inl-late/tests/fixtures/tiny_qwen3_5_late",
                           ["config.json", "config_sentence_transformers.json", "sentence_bert_config.json",
-                           "modules.json", "2_MultiVectorMask/config.json", "tokenizer.json", "golden.json"]),
+                           "modules.json", "2_MultiVectorMask/config.json", "tokenizer.json", "golden.json",
+                           "model.safetensors", "1_Dense/config.json", "1_Dense/model.safetensors"]),
 }
 KEEP_DIRS = {"tiny_qwen3_5_late"}
 
