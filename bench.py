@@ -143,6 +143,36 @@ def cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=CPU_SAMPLE_TO
     return total / dt, total, len(picked), dt
 
 
+def rank_share(batches: list, rank: int, world: int, steps: int, warmup: int) -> list:
+    """The batches one rank runs, warm-up first: every ``world``-th batch of
+    the corpus. The timed steps are the rank's whole share when ``steps``
+    covers it, else ``steps`` batches spaced evenly over it (the share runs
+    longest to shortest, so a prefix would over-weight the attention-heavy
+    2k-token texts); the warm-up batches come from the same spread."""
+    mine = batches[rank::world]
+    if steps >= len(mine):
+        timed = [mine[i % len(mine)] for i in range(steps)]
+    else:
+        timed = [mine[int(i)] for i in np.linspace(0, len(mine) - 1, steps)]
+    return [timed[i % len(timed)] for i in range(warmup)] + timed
+
+
+def reduce_timing(ms: float, e2e_ms: float, tokens: float, world: int, device: str) -> tuple[float, float, float]:
+    """Across ranks: the max of the device-timed and the end-to-end times,
+    the sum of the tokens (every rank takes the same collective steps)."""
+    if world == 1:
+        return ms, e2e_ms, float(tokens)
+    import torch
+    import torch.distributed as dist
+
+    stats = torch.tensor([ms, e2e_ms, float(tokens)], dtype=torch.float64, device=device)
+    mx = stats.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    tot = stats.clone()
+    dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    return mx[0].item(), mx[1].item(), tot[2].item()
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -199,17 +229,8 @@ def run_ours(args, world, rank, local):
     weights = inl.synthetic.qwen3_weights(cfg, seed=0)
     model = inl.CudaModel(cfg, weights, device=local, dtype="bf16")
     texts, batches, lengths = corpus_batches()
-    mine = batches[rank::world]
     need = args.warmup + args.steps
-    # Timed steps: the rank's whole share when K covers it, else K batches
-    # spaced evenly over it (the share runs longest to shortest, so a prefix
-    # would over-weight the attention-heavy 2k-token texts). Warm-up batches
-    # come from the same spread.
-    if args.steps >= len(mine):
-        timed = [mine[i % len(mine)] for i in range(args.steps)]
-    else:
-        timed = [mine[int(i)] for i in np.linspace(0, len(mine) - 1, args.steps)]
-    sel = [timed[i % len(timed)] for i in range(args.warmup)] + timed
+    sel = rank_share(batches, rank, world, args.steps, args.warmup)
     packed = [inl.planner.pack(texts, b) for b in sel]
     # inputs resident in HBM for the device-timed leg
     dev_ids = [torch.from_numpy(p[0].view(np.int32)).cuda() for p in packed]
@@ -277,17 +298,7 @@ def run_ours(args, world, rank, local):
     e2e_s = time.perf_counter() - t0
     barrier()
 
-    stats = torch.tensor([ms, e2e_s * 1000.0, float(tokens)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        import torch.distributed as dist
-
-        mx = stats.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = stats.clone()
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, e2e_max, tokens_all = mx[0].item(), mx[1].item(), tot[2].item()
-    else:
-        ms_max, e2e_max, tokens_all = ms, e2e_s * 1000.0, float(tokens)
+    ms_max, e2e_max, tokens_all = reduce_timing(ms, e2e_s * 1000.0, tokens, world, "cuda")
 
     if rank == 0:
         peak, peak_kind = _peaks()
