@@ -32,7 +32,7 @@ EXPORTED = (
     "inl_cuda_attention", "inl_cuda_model_set_profiling", "inl_cuda_model_profile",
     "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
     "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2", "inl_cuda_gemm_bf16_ex",
-    "inl_cuda_attention_noalloc",
+    "inl_cuda_attention_noalloc", "inl_cuda_causal_conv_silu", "inl_cuda_gated_delta_rule",
 )
 
 
@@ -104,6 +104,11 @@ def _declare(lib: ctypes.CDLL) -> None:
         "inl_cuda_token_positions": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
         "inl_cuda_last_token_norm_l2": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_int, c_void_p, c_float, c_int,
                                                 c_void_p, c_void_p]),
+        "inl_cuda_causal_conv_silu": (c_int, [c_void_p, c_i64, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                              c_i64, c_void_p]),
+        "inl_cuda_gated_delta_rule": (c_int, [c_void_p, c_i64, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                                              c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_int, c_void_p,
+                                              c_int, c_void_p, c_i64, c_void_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

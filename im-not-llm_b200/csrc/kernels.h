@@ -209,4 +209,30 @@ int attention_tc(const AttnArgs& a, long long total_rows, cudaStream_t s);
 // Number of query rows per work item the attention kernels expect.
 int attention_q_block(int bf16, int d);
 
+// ---------------------------------------------------------------- Gated DeltaNet (Qwen3.5 linear attention)
+// out[t, c] = silu(sum_j w[c, j] x[t - K + 1 + j, c]) over each text's tokens (pos[t] = position in its text).
+int causal_conv_silu(const float* x, long long ldx, int T, int C, const float* w, int K, const int* pos, float* out,
+                     long long ldo, cudaStream_t s);
+
+struct DeltaArgs {
+  const float* mixed = nullptr;  // [T, ld_mixed]: q (nk dk) | k (nk dk) | v (nv dv), after the convolution
+  long long ld_mixed = 0;
+  const float* b_in = nullptr;   // [T, ld_ab] step-size logits (beta = sigmoid) at column vh
+  const float* a_in = nullptr;   // [T, ld_ab] decay inputs (g = softplus(a + dt_bias) * -exp(A_log)) at column vh
+  long long ld_ab = 0;
+  const float* z = nullptr;      // [T, ld_z] output gate, nv dv columns
+  long long ld_z = 0;
+  const float* dt_bias = nullptr;  // [nv]
+  const float* a_log = nullptr;    // [nv]
+  const float* norm_w = nullptr;   // [dv] gated RMSNorm weight
+  float eps = 1e-6f;
+  int nk = 0, nv = 0, dk = 0, dv = 0;
+  const int* cu = nullptr;  // device [n+1]
+  int n = 0;
+  float* out = nullptr;     // [T, ldo] nv dv columns
+  long long ldo = 0;
+};
+// Recurrent gated delta rule with the gated RMSNorm fused; -1 on unsupported shapes.
+int gated_delta_rule(const DeltaArgs& a, cudaStream_t s);
+
 }  // namespace inl

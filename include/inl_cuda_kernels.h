@@ -145,6 +145,30 @@ INL_API int inl_cuda_token_positions(const int32_t* cu, int n, int T, int32_t* p
 INL_API int inl_cuda_last_token_norm_l2(const void* h, int h_dtype, int64_t ldh, const int32_t* cu, int n,
                                         const float* w, float eps, int H, float* out, void* stream);
 
+/* Gated DeltaNet (Qwen3.5 "linear_attention" layers), f32, packed texts;
+ * cu_seqlens is HOST memory. No model path calls these yet: they are the
+ * kernel hooks of the next hot-path row, checked against oracle/qwen3_5.py.
+ *
+ * Depthwise causal convolution then SiLU over each text's tokens, zero before
+ * its first token: out[t, c] = silu(sum_j w[c, j] x[t - K + 1 + j, c]),
+ * w [C, K]. Replaces GatedDeltaNet::causal_conv
+ * (crates/inl-late/src/qwen3_5.rs:463-479). */
+INL_API int inl_cuda_causal_conv_silu(const float* x, int64_t ldx, int C, const float* w, int K,
+                                      const int32_t* cu_seqlens_host, int n_texts, float* out, int64_t ldo,
+                                      void* stream);
+
+/* The gated delta rule per (text, value head) with the per-head gated
+ * RMSNorm and silu(z) gate: mixed [T, ld_mixed] = q (nk dk) | k (nk dk) |
+ * v (nv dv); b_in / a_in [T, ld_ab] column vh; z [T, ld_z]; out [T, ldo]
+ * nv dv columns. dk in {8, 16, 32, 64, 128}, dv <= 128, nv a multiple of nk.
+ * Replaces chunk_gated_delta_rule and the gated norm of GatedDeltaNet::forward
+ * (crates/inl-late/src/qwen3_5.rs:481-545,612-739). */
+INL_API int inl_cuda_gated_delta_rule(const float* mixed, int64_t ld_mixed, const float* b_in, const float* a_in,
+                                      int64_t ld_ab, const float* z, int64_t ld_z, const float* dt_bias,
+                                      const float* a_log, const float* norm_w, float eps, int nk, int nv, int dk,
+                                      int dv, const int32_t* cu_seqlens_host, int n_texts, float* out, int64_t ldo,
+                                      void* stream);
+
 /* Measurement hooks: with profiling on, every GEMM and attention launch of
  * the model is bracketed by CUDA events on the model's stream. kind: 0 qkv,
  * 1 o, 2 gate/up, 3 down, 4 Dense head, -1 all GEMMs; 100 attention (flops
