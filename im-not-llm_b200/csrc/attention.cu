@@ -397,6 +397,8 @@ int attention(const AttnArgs& a, cudaStream_t s) {
   }
   if (a.q_block != kFQ) return -1;
   switch (a.d) {
+    case 8:
+    case 16: return attention_small(a, s);  // tiny checkpoints
     case 32: return launch_f32<32>(a, s);
     case 64: return launch_f32<64>(a, s);
     case 128: return launch_f32<128>(a, s);

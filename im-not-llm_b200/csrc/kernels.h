@@ -235,4 +235,28 @@ struct DeltaArgs {
 // Recurrent gated delta rule with the gated RMSNorm fused; -1 on unsupported shapes.
 int gated_delta_rule(const DeltaArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- Qwen3.5 gated full attention (f32)
+struct Qwen35QkArgs {
+  float* qkv = nullptr;   // [T, ld]: q | gate per head (2 d each, hq heads), then k (hkv d), then v (hkv d)
+  long long ld = 0;
+  float* q_out = nullptr; // [T, ldq] normed, rotated q heads (d each)
+  long long ldq = 0;
+  int T = 0, hq = 0, hkv = 0, d = 0;
+  int rot = 0;            // rotary features per head (half-split rotation of the first `rot`)
+  const float* qw = nullptr;  // [d] q norm scale (1 + w folded)
+  const float* kw = nullptr;  // [d] k norm scale (1 + w folded)
+  float eps = 1e-6f;
+  const int* pos = nullptr;
+  const float* cos = nullptr;  // [max_pos, rot / 2]
+  const float* sin = nullptr;
+  int max_pos = 0;
+  int* status = nullptr;
+};
+int qk_prep_gated(const Qwen35QkArgs& a, cudaStream_t s);
+// out[t, h d + j] *= sigmoid(gate[t, h 2d + d + j]) (gate_base = the q | gate rows).
+int gate_sigmoid_mul(float* out, long long ldo, const float* gate_base, long long ldg, int T, int hq, int d,
+                     cudaStream_t s);
+// f32 attention for head_dim <= 32 on the f32 work list (32-query blocks).
+int attention_small(const AttnArgs& a, cudaStream_t s);
+
 }  // namespace inl

@@ -111,6 +111,8 @@ int parse_config(const std::string& text, ModelConfig& c) {
   else if (mt == "modernbert") c.arch = inl::ARCH_MODERNBERT;
   else if (mt == "gemma_style" || mt == "gemma3_text" || mt == "embedding_gemma2" || mt == "embeddinggemma")
     c.arch = inl::ARCH_GEMMA;
+  else if (mt == "qwen3_5" || mt == "qwen3_5_text")
+    c.arch = inl::ARCH_QWEN35;
   else
     return fail(INL_ERR_CONFIG, "config: unsupported model_type '" + mt + "'");
   c.H = static_cast<int>(num_or(root, "hidden_size", 0));
@@ -171,6 +173,43 @@ int parse_config(const std::string& text, ModelConfig& c) {
       if (strategy != "max" || act != "relu")
         return fail(INL_ERR_CONFIG, "config: only max pooling with relu activation is supported");
       if (num_or(*sp, "top_k", 0) > 0) return fail(INL_ERR_CONFIG, "config: SPLADE top_k is not supported");
+    }
+  } else if (c.arch == inl::ARCH_QWEN35) {
+    // Qwen3.5 text tower of the late-interaction engine (crates/inl-late/src/qwen3_5.rs:56-168):
+    // the same validation as Config::validate.
+    c.causal = bool_or(root, "is_causal", true);
+    if (!bool_or(root, "attn_output_gate", true))
+      return fail(INL_ERR_CONFIG, "config: only gated Qwen3.5 attention is supported");
+    if (str_or(root, "hidden_act", "silu") != "silu") return fail(INL_ERR_CONFIG, "config: hidden_act must be silu");
+    c.lin_nk = static_cast<int>(num_or(root, "linear_num_key_heads", 0));
+    c.lin_nv = static_cast<int>(num_or(root, "linear_num_value_heads", 0));
+    c.lin_dk = static_cast<int>(num_or(root, "linear_key_head_dim", 0));
+    c.lin_dv = static_cast<int>(num_or(root, "linear_value_head_dim", 0));
+    c.conv_k = static_cast<int>(num_or(root, "linear_conv_kernel_dim", 4));
+    if (c.lin_nk <= 0 || c.lin_nv <= 0 || c.lin_dk <= 0 || c.lin_dv <= 0 || c.conv_k <= 0 ||
+        c.lin_nv % c.lin_nk != 0)
+      return fail(INL_ERR_CONFIG, "config: invalid linear-attention head shapes");
+    double theta = 10000.0, factor = 1.0;
+    std::string rope_type = "default";
+    if (const inl::json::Value* rp = root.get("rope_parameters"); rp && rp->kind == inl::json::Value::Object) {
+      theta = num_or(*rp, "rope_theta", theta);
+      factor = num_or(*rp, "partial_rotary_factor", factor);
+      rope_type = str_or(*rp, "rope_type", rope_type);
+    }
+    if (rope_type != "default") return fail(INL_ERR_CONFIG, "config: unsupported rope_type " + rope_type);
+    c.theta = theta;
+    c.rot = static_cast<int>(c.d * factor);
+    if (c.rot <= 0 || c.rot % 2 != 0 || c.rot > c.d)
+      return fail(INL_ERR_CONFIG, "config: the rotary dimension must be even and at most head_dim");
+    const inl::json::Value* kinds = root.get("layer_types");
+    if (!kinds || kinds->kind != inl::json::Value::Array || static_cast<int>(kinds->arr.size()) != c.layers)
+      return fail(INL_ERR_CONFIG, "config: layer_types must list every layer");
+    c.layer_linear.assign(c.layers, 0);
+    for (int i = 0; i < c.layers; ++i) {
+      const std::string& k = kinds->arr[i].str;
+      if (k != "linear_attention" && k != "full_attention")
+        return fail(INL_ERR_CONFIG, "config: unsupported layer type " + k);
+      c.layer_linear[i] = k == "linear_attention";
     }
   } else {
     // EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:78-211)
@@ -447,6 +486,117 @@ int load_qwen3(inl_model* m, Loader& L) {
   return INL_OK;
 }
 
+// A zero-centred norm weight uploaded as its scale 1 + w (RmsNorm::load,
+// crates/inl-late/src/qwen3_5.rs:194-201).
+int vec_plus_one(inl_model* m, Loader& L, const std::string& name, int n, float** out) {
+  const TensorSrc* t = L.find(name);
+  if (!t) return fail(INL_ERR_INFERENCE, "missing weight " + L.prefix + name);
+  if (t->numel != n) return fail(INL_ERR_INFERENCE, "weight " + name + " has the wrong size");
+  std::vector<float> v(n);
+  if (t->bf16) {
+    const uint16_t* b = static_cast<const uint16_t*>(t->data);
+    for (int i = 0; i < n; ++i) {
+      const uint32_t bits = static_cast<uint32_t>(b[i]) << 16;
+      std::memcpy(&v[i], &bits, 4);
+    }
+  } else {
+    std::memcpy(v.data(), t->data, static_cast<size_t>(n) * 4);
+  }
+  for (float& x : v) x += 1.0f;
+  *out = static_cast<float*>(L.alloc(static_cast<size_t>(n) * 4));
+  if (!*out) return fail(INL_ERR_INFERENCE, "out of device memory for " + name);
+  INL_CUDA_TRY(cudaMemcpyAsync(*out, v.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, m->stream),
+               "norm upload");
+  INL_CUDA_TRY(cudaStreamSynchronize(m->stream), "norm upload");
+  return INL_OK;
+}
+
+// cos / sin [max_pos, rot / 2] of position * inv_freq computed in f32, as
+// rotary_tables does (crates/inl-late/src/qwen3_5.rs:940-958).
+int build_rope_f32(inl_model* m, double theta, int rot) {
+  const int half = rot / 2, P = m->c.max_pos;
+  std::vector<float> c(static_cast<size_t>(P) * half), s(static_cast<size_t>(P) * half);
+  const float th = static_cast<float>(theta);
+  for (int i = 0; i < half; ++i) {
+    const float inv = 1.0f / std::pow(th, static_cast<float>(2 * i) / static_cast<float>(rot));
+    for (int p = 0; p < P; ++p) {
+      const float ang = static_cast<float>(p) * inv;
+      c[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
+      s[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+    }
+  }
+  const size_t bytes = c.size() * 4;
+  float *dc = nullptr, *ds = nullptr;
+  INL_CUDA_TRY(cudaMalloc(&dc, bytes), "rope table");
+  m->allocs.push_back(dc);
+  INL_CUDA_TRY(cudaMalloc(&ds, bytes), "rope table");
+  m->allocs.push_back(ds);
+  INL_CUDA_TRY(cudaMemcpy(dc, c.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  INL_CUDA_TRY(cudaMemcpy(ds, s.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  m->cos0 = dc;
+  m->sin0 = ds;
+  return INL_OK;
+}
+
+// Qwen3.5 text tower (crates/inl-late/src/qwen3_5.rs:816-891 tensor names), f32.
+int load_qwen35(inl_model* m, Loader& L) {
+  const ModelConfig& c = m->c;
+  if (m->dtype != INL_DTYPE_F32) return fail(INL_ERR_CONFIG, "the Qwen3.5 tower runs in f32");
+  const int nk = c.lin_nk, nv = c.lin_nv, dk = c.lin_dk, dv = c.lin_dv;
+  const int conv_dim = 2 * nk * dk + nv * dv;
+  const int lin_rows = conv_dim + nv * dv + 2 * nv;
+  const int q_rows = c.hq * 2 * c.d, kv_rows = c.hkv * c.d;
+  m->gated_split = (c.I % m->gate_block) != 0;
+  const int gb = m->gated_split ? c.I : m->gate_block;
+  const long long gstride = m->gated_split ? 0 : 2LL * gb;
+  const long long up_off = m->gated_split ? c.I : gb;
+  int r;
+  if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, 0))) return r;
+  m->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    inl::LayerWeights& w = m->layers[l];
+    if ((r = vec_plus_one(m, L, p + "input_layernorm.weight", c.H, &w.ln1))) return r;
+    if ((r = vec_plus_one(m, L, p + "post_attention_layernorm.weight", c.H, &w.ln2))) return r;
+    if (c.layer_linear[l]) {
+      const std::string a = p + "linear_attn.";
+      w.w_lin_in = L.alloc(static_cast<size_t>(lin_rows) * c.H * 4);
+      w.w_lin_out = L.alloc(static_cast<size_t>(c.H) * nv * dv * 4);
+      w.conv_w = static_cast<float*>(L.alloc(static_cast<size_t>(conv_dim) * c.conv_k * 4));
+      if (!w.w_lin_in || !w.w_lin_out || !w.conv_w) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+      if ((r = L.upload(a + "in_proj_qkv.weight", conv_dim, c.H, w.w_lin_in, 0, c.H, conv_dim, 0, 0))) return r;
+      if ((r = L.upload(a + "in_proj_z.weight", nv * dv, c.H, w.w_lin_in, 0, c.H, nv * dv, 0, conv_dim))) return r;
+      if ((r = L.upload(a + "in_proj_b.weight", nv, c.H, w.w_lin_in, 0, c.H, nv, 0, conv_dim + nv * dv))) return r;
+      if ((r = L.upload(a + "in_proj_a.weight", nv, c.H, w.w_lin_in, 0, c.H, nv, 0, conv_dim + nv * dv + nv)))
+        return r;
+      if ((r = L.upload(a + "out_proj.weight", c.H, nv * dv, w.w_lin_out, 0, nv * dv, c.H, 0, 0))) return r;
+      if ((r = L.upload(a + "conv1d.weight", conv_dim, c.conv_k, w.conv_w, 0, c.conv_k, conv_dim, 0, 0))) return r;
+      if ((r = L.vec(a + "dt_bias", nv, &w.dt_bias))) return r;
+      if ((r = L.vec(a + "A_log", nv, &w.a_log))) return r;
+      if ((r = L.vec(a + "norm.weight", dv, &w.lin_norm))) return r;
+    } else {
+      const std::string a = p + "self_attn.";
+      w.wqkv = L.alloc(static_cast<size_t>(q_rows + 2 * kv_rows) * c.H * 4);
+      w.wo = L.alloc(static_cast<size_t>(c.H) * c.hq * c.d * 4);
+      if (!w.wqkv || !w.wo) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+      if ((r = L.upload(a + "q_proj.weight", q_rows, c.H, w.wqkv, 0, c.H, q_rows, 0, 0))) return r;
+      if ((r = L.upload(a + "k_proj.weight", kv_rows, c.H, w.wqkv, 0, c.H, kv_rows, 0, q_rows))) return r;
+      if ((r = L.upload(a + "v_proj.weight", kv_rows, c.H, w.wqkv, 0, c.H, kv_rows, 0, q_rows + kv_rows))) return r;
+      if ((r = L.upload(a + "o_proj.weight", c.H, c.hq * c.d, w.wo, 0, c.hq * c.d, c.H, 0, 0))) return r;
+      if ((r = vec_plus_one(m, L, a + "q_norm.weight", c.d, &w.qn))) return r;
+      if ((r = vec_plus_one(m, L, a + "k_norm.weight", c.d, &w.kn))) return r;
+    }
+    w.wgu = L.alloc(static_cast<size_t>(2) * c.I * c.H * 4);
+    w.wd = L.alloc(static_cast<size_t>(c.H) * c.I * 4);
+    if (!w.wgu || !w.wd) return fail(INL_ERR_INFERENCE, "out of device memory for weights");
+    if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, 0, c.H, gb, gstride, 0))) return r;
+    if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, 0, c.H, gb, gstride, up_off))) return r;
+    if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, 0, c.I, c.H, 0, 0))) return r;
+  }
+  if ((r = vec_plus_one(m, L, "norm.weight", c.H, &m->final_norm))) return r;
+  return build_rope_f32(m, c.theta, c.rot);
+}
+
 int upload_host(inl_model* m, void** dst, const void* src, size_t bytes) {
   void* p = nullptr;
   INL_CUDA_TRY(cudaMalloc(&p, std::max<size_t>(bytes, 4)), "device table");
@@ -628,6 +778,7 @@ int load_weights(inl_model* m, const TensorMap& t) {
     case inl::ARCH_QWEN3: r = load_qwen3(m, L); break;
     case inl::ARCH_MODERNBERT: r = load_modernbert(m, L); break;
     case inl::ARCH_GEMMA: r = load_gemma(m, L); break;
+    case inl::ARCH_QWEN35: r = load_qwen35(m, L); break;
     default: r = fail(INL_ERR_CONFIG, "unknown architecture"); break;
   }
   return r;
@@ -686,13 +837,24 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   const ModelConfig& c = m->c;
   const size_t T = token_cap(b.T);
   const size_t e = es(m);
-  const size_t qkv_cols = static_cast<size_t>(c.hq + 2 * c.hkv) * c.d;
+  size_t qkv_cols = static_cast<size_t>(c.hq + 2 * c.hkv) * c.d;
   const size_t act_cols = static_cast<size_t>(c.I);
+  size_t attn_cols = static_cast<size_t>(c.hq) * c.d;
+  size_t tmp_cols = m->gated_split ? 2 * static_cast<size_t>(c.I) : 0;
+  if (c.arch == inl::ARCH_QWEN35) {
+    // q | gate rows or the stacked DeltaNet input projection; DeltaNet output;
+    // the convolution output or the de-interleaved q heads.
+    const size_t conv_dim = 2 * static_cast<size_t>(c.lin_nk) * c.lin_dk + static_cast<size_t>(c.lin_nv) * c.lin_dv;
+    const size_t lin_cols = conv_dim + static_cast<size_t>(c.lin_nv) * c.lin_dv + 2 * static_cast<size_t>(c.lin_nv);
+    qkv_cols = std::max(static_cast<size_t>(2 * c.hq + 2 * c.hkv) * c.d, lin_cols);
+    attn_cols = std::max(attn_cols, static_cast<size_t>(c.lin_nv) * c.lin_dv);
+    tmp_cols = std::max({tmp_cols, conv_dim, static_cast<size_t>(c.hq) * c.d});
+  }
   INL_CUDA_TRY(m->h.ensure(T * c.H * e), "workspace");
   INL_CUDA_TRY(m->xn.ensure(T * c.H * e), "workspace");
   INL_CUDA_TRY(m->qkv.ensure(T * std::max(qkv_cols, act_cols) * e), "workspace");
-  INL_CUDA_TRY(m->attn.ensure(T * static_cast<size_t>(c.hq) * c.d * e), "workspace");
-  if (m->gated_split) INL_CUDA_TRY(m->tmp.ensure(T * 2 * static_cast<size_t>(c.I) * e), "workspace");
+  INL_CUDA_TRY(m->attn.ensure(T * attn_cols * e), "workspace");
+  if (tmp_cols) INL_CUDA_TRY(m->tmp.ensure(T * tmp_cols * e), "workspace");
   INL_CUDA_TRY(m->ids.ensure(T * 4), "workspace");
   const size_t parts = static_cast<size_t>((c.H + INL_SS_COLS - 1) / INL_SS_COLS);
   INL_CUDA_TRY(m->ss_a.ensure(T * parts * 4), "workspace");
@@ -1194,6 +1356,122 @@ int gemma_tower(inl_model* m, const Batch& b, int n_work) {
   return INL_OK;
 }
 
+// Qwen3.5 text tower of the late-interaction engine (Qwen35Text::forward,
+// crates/inl-late/src/qwen3_5.rs:780-915), f32; leaves the last hidden state
+// (before the final norm) in m->h. Per layer h += mixer(norm(h)), then
+// h += MLP(norm(h)); the mixer is a Gated DeltaNet (one stacked input GEMM,
+// causal convolution, recurrent delta rule with the gated norm fused, output
+// GEMM) or gated full attention (q | gate, k, v GEMM; q / k norm and partial
+// RoPE; attention; sigmoid gate; output GEMM).
+int qwen35_tower(inl_model* m, const Batch& b, int n_work) {
+  const ModelConfig& c = m->c;
+  const int T = b.T;
+  cudaStream_t s = m->stream;
+  const int nk = c.lin_nk, nv = c.lin_nv, dk = c.lin_dk, dv = c.lin_dv;
+  const int conv_dim = 2 * nk * dk + nv * dv;
+  const int lin_cols = conv_dim + nv * dv + 2 * nv;
+  const int q_rows = c.hq * 2 * c.d, kv = c.hkv * c.d, att_cols = q_rows + 2 * kv, q_out = c.hq * c.d;
+  float* qkv = m->qkv.as<float>();
+  INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, 0, c.V, c.H, 1.0f, m->h.p, 0, m->d_status, s),
+            "embedding");
+  m->launches++;
+  for (int l = 0; l < c.layers; ++l) {
+    const inl::LayerWeights& w = m->layers[l];
+    INL_K_TRY(inl::rms_norm(m->h.p, 0, c.H, w.ln1, c.eps, T, c.H, m->xn.p, 0, c.H, s), "input norm");
+    m->launches++;
+    if (c.layer_linear[l]) {
+      INL_K_TRY(linear(m, m->xn.p, c.H, w.w_lin_in, T, lin_cols, c.H, INL_EPI_BF16, 0, qkv, lin_cols, nullptr, 0, 0),
+                "linear-attention input projections");
+      INL_K_TRY(inl::causal_conv_silu(qkv, lin_cols, T, conv_dim, w.conv_w, c.conv_k, m->pos.as<int>(),
+                                      m->tmp.as<float>(), conv_dim, s),
+                "causal convolution");
+      m->launches++;
+      inl::DeltaArgs da;
+      da.mixed = m->tmp.as<float>();
+      da.ld_mixed = conv_dim;
+      da.z = qkv + conv_dim;
+      da.ld_z = lin_cols;
+      da.b_in = qkv + conv_dim + nv * dv;
+      da.a_in = da.b_in + nv;
+      da.ld_ab = lin_cols;
+      da.dt_bias = w.dt_bias;
+      da.a_log = w.a_log;
+      da.norm_w = w.lin_norm;
+      da.eps = c.eps;
+      da.nk = nk;
+      da.nv = nv;
+      da.dk = dk;
+      da.dv = dv;
+      da.cu = m->cu.as<int>();
+      da.n = b.n;
+      da.out = m->attn.as<float>();
+      da.ldo = nv * dv;
+      INL_K_TRY(inl::gated_delta_rule(da, s), "gated delta rule");
+      m->launches++;
+      INL_K_TRY(linear(m, m->attn.p, nv * dv, w.w_lin_out, T, c.H, nv * dv, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p,
+                       c.H, 1),
+                "linear-attention output projection");
+    } else {
+      INL_K_TRY(linear(m, m->xn.p, c.H, w.wqkv, T, att_cols, c.H, INL_EPI_BF16, 0, qkv, att_cols, nullptr, 0, 0),
+                "q | gate, k, v projections");
+      inl::Qwen35QkArgs qa;
+      qa.qkv = qkv;
+      qa.ld = att_cols;
+      qa.q_out = m->tmp.as<float>();
+      qa.ldq = q_out;
+      qa.T = T;
+      qa.hq = c.hq;
+      qa.hkv = c.hkv;
+      qa.d = c.d;
+      qa.rot = c.rot;
+      qa.qw = w.qn;
+      qa.kw = w.kn;
+      qa.eps = c.eps;
+      qa.pos = m->pos.as<int>();
+      qa.cos = m->cos0;
+      qa.sin = m->sin0;
+      qa.max_pos = c.max_pos;
+      qa.status = m->d_status;
+      INL_K_TRY(inl::qk_prep_gated(qa, s), "q / k norm and rope");
+      m->launches++;
+      inl::AttnArgs aa;
+      aa.q = m->tmp.p;
+      aa.ldq = q_out;
+      aa.k = qkv + q_rows;
+      aa.v = qkv + q_rows + kv;
+      aa.ldk = aa.ldv = att_cols;
+      aa.out = m->attn.p;
+      aa.ldo = q_out;
+      aa.bf16 = 0;
+      aa.hq = c.hq;
+      aa.hkv = c.hkv;
+      aa.d = c.d;
+      aa.scale = 1.0f / std::sqrt(static_cast<float>(c.d));
+      aa.causal = c.causal ? 1 : 0;
+      aa.window = -1;
+      aa.cu = m->cu.as<int>();
+      aa.n = b.n;
+      aa.work = m->work.as<int2>();
+      aa.n_work = n_work;
+      aa.q_block = inl::attention_q_block(0, c.d);
+      aa.total_rows = T;
+      aa.status = m->d_status;
+      INL_K_TRY(run_attention(m, aa, s), "attention");
+      m->launches++;
+      INL_K_TRY(inl::gate_sigmoid_mul(m->attn.as<float>(), q_out, qkv, att_cols, T, c.hq, c.d, s), "output gate");
+      m->launches++;
+      INL_K_TRY(linear(m, m->attn.p, q_out, w.wo, T, c.H, q_out, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 1),
+                "o projection");
+    }
+    INL_K_TRY(inl::rms_norm(m->h.p, 0, c.H, w.ln2, c.eps, T, c.H, m->xn.p, 0, c.H, s), "post-attention norm");
+    m->launches++;
+    INL_K_TRY(mlp_gated(m, m->xn.p, T, w.wgu, INL_ACT_SILU, qkv), "gate/up projection");
+    INL_K_TRY(linear(m, qkv, c.I, w.wd, T, c.H, c.I, INL_EPI_RESID_BF16, 0, m->h.p, c.H, m->h.p, c.H, 3),
+              "down projection");
+  }
+  return INL_OK;
+}
+
 int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b) {
   int r = check_inputs(m, ids, ids_mem, cu, n, b);
   if (r) return r;
@@ -1208,6 +1486,7 @@ int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu,
     case inl::ARCH_QWEN3: return m->fused ? qwen3_tower_fused(m, b, n_work) : qwen3_tower(m, b, n_work);
     case inl::ARCH_MODERNBERT: return modernbert_tower(m, b, n_work);
     case inl::ARCH_GEMMA: return gemma_tower(m, b, n_work);
+    case inl::ARCH_QWEN35: return qwen35_tower(m, b, n_work);
     default: return fail(INL_ERR_CONFIG, "model_type not built");
   }
 }
@@ -1348,6 +1627,8 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
   const ModelConfig& c = m->c;
   if (out_dim != 0 && c.arch != inl::ARCH_GEMMA)
     return fail(INL_ERR_CONFIG, "output_dim is only supported for EmbeddingGemma-style models");
+  if (c.arch == inl::ARCH_QWEN35)
+    return fail(INL_ERR_CONFIG, "a Qwen3.5 late tower has no pooled dense head (use forward_multivector)");
   Batch b;
   int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
   if (r) return r;

@@ -15,7 +15,7 @@
 
 namespace inl {
 
-enum Arch : int { ARCH_QWEN3 = 0, ARCH_MODERNBERT = 1, ARCH_GEMMA = 2 };
+enum Arch : int { ARCH_QWEN3 = 0, ARCH_MODERNBERT = 1, ARCH_GEMMA = 2, ARCH_QWEN35 = 3 };
 
 struct ModelConfig {
   Arch arch = ARCH_QWEN3;
@@ -44,6 +44,12 @@ struct ModelConfig {
   // SPLADE pooling (ModernBERT MLM head)
   bool decoder_bias = true;
   std::vector<int> prefix_ids, masked_vocab_ids, canonical_ids;
+  // Qwen3.5 text tower (crates/inl-late/src/qwen3_5.rs:56-168): per layer
+  // Gated DeltaNet (1) or gated full attention (0); DeltaNet head shapes,
+  // causal-convolution taps; rotary features per head (partial RoPE).
+  std::vector<char> layer_linear;
+  int lin_nk = 0, lin_nv = 0, lin_dk = 0, lin_dv = 0, conv_k = 0;
+  int rot = 0;
 };
 
 struct TensorSrc {
@@ -97,6 +103,15 @@ struct LayerWeights {
   float* ln2_post = nullptr;  // Gemma post-feedforward norm
   float* qn = nullptr;
   float* kn = nullptr;
+  // Qwen3.5 Gated DeltaNet layer: [in_proj_qkv; in_proj_z; in_proj_b; in_proj_a] stacked
+  // ([conv_dim + nv dv + 2 nv, H]), out_proj [H, nv dv], depthwise kernel [conv_dim, K],
+  // per value head dt_bias and A_log, gated-norm weight [dv] (all f32 but the projections).
+  void* w_lin_in = nullptr;
+  void* w_lin_out = nullptr;
+  float* conv_w = nullptr;
+  float* dt_bias = nullptr;
+  float* a_log = nullptr;
+  float* lin_norm = nullptr;
 };
 
 struct ProfileRec {
