@@ -58,7 +58,7 @@ extern "C" {
 typedef struct inl_model inl_model;
 
 typedef struct inl_model_info {
-  int arch;              /* 0 = qwen3, 1 = modernbert, 2 = gemma-style */
+  int arch;              /* 0 = qwen3, 1 = modernbert, 2 = gemma-style, 3 = qwen3.5 (late) */
   int dtype;             /* INL_DTYPE_* */
   int device;            /* CUDA ordinal */
   int hidden_size;

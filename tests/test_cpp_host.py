@@ -1,0 +1,51 @@
+"""The C++ host layer (include/inl_engine.hpp, im-not-llm_b200/host/): built
+with g++ and run on the CPU.
+
+* tests/cpp/test_engine.cpp: planning, BatchDeadline (timeout, then wedged),
+  the error variants and the three engines over a test-double Backend.
+* tests/cpp/backend_link.cpp: the CUDA backend links against libinl_cuda.so
+  and a model load that cannot succeed here raises an InlError (no crash)."""
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HOST = ROOT / "im-not-llm_b200" / "host"
+GXX = shutil.which("g++")
+FLAGS = ["-std=c++17", "-O1", "-Wall", "-Wextra", "-Werror", "-pthread", f"-I{ROOT / 'include'}"]
+
+pytestmark = pytest.mark.skipif(GXX is None, reason="g++ not found")
+
+
+def _run(cmd, **kw):
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, **kw)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return r.stdout
+
+
+def test_host_layer_with_a_test_backend(tmp_path):
+    exe = tmp_path / "test_engine"
+    _run([GXX, *FLAGS, str(HOST / "engine.cpp"), str(ROOT / "tests" / "cpp" / "test_engine.cpp"), "-o", str(exe)])
+    assert "all passed" in _run([str(exe)])
+
+
+def test_cuda_backend_links_and_a_failed_load_is_an_inl_error(tmp_path):
+    import torch
+
+    from im_not_llm_b200 import _native
+
+    lib = _native.LIB_PATH
+    if not lib.exists():
+        pytest.skip("libinl_cuda.so not built")
+    exe = tmp_path / "backend_link"
+    _run([GXX, *FLAGS, str(HOST / "engine.cpp"), str(HOST / "cuda_backend.cpp"),
+          str(ROOT / "tests" / "cpp" / "backend_link.cpp"), f"-L{lib.parent}", "-linl_cuda",
+          f"-Wl,-rpath,{lib.parent}", "-o", str(exe)])
+    out = _run([str(exe)]).strip()
+    code, _, message = out.partition("|")
+    if not torch.cuda.is_available():
+        assert code == "config" and message.startswith("config error: model load:"), out
+    else:  # the checkpoint path does not exist
+        assert code in ("config", "inference"), out
