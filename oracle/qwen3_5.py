@@ -105,6 +105,49 @@ def gated_delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray,
     return out.astype(np.float32)
 
 
+def gated_delta_rule_chunked(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray,
+                             beta: np.ndarray, chunk: int = 64) -> np.ndarray:
+    """The same rule in its chunked (WY) form, the structure a tensor-core
+    kernel computes (the reference's chunk_gated_delta_rule,
+    crates/inl-late/src/qwen3_5.rs:612-739, restated; the WY form of Yang et
+    al., "Parallelizing Linear Transformers with the Delta Rule over
+    Sequence Length"). Per chunk of C tokens with local cumulative decay
+    c_i = sum_{j<=i} g_j and D_ij = exp(c_i - c_j) (j <= i):
+
+        A = strictly_lower((beta k) k^T * D)       U = (I + A)^-1 (beta v)
+        W = (I + A)^-1 (beta k * exp(c))           u = U - W S
+        o = (q * exp(c)) S + lower(q k^T * D) u
+        S <- exp(c_C) S + (k * exp(c_C - c))^T u
+
+    (I + A)^-1 by forward substitution. Same shapes and result as
+    gated_delta_rule."""
+    T, H, dk = q.shape
+    dv = v.shape[2]
+    qn = l2norm(q.astype(np.float64)) * dk ** -0.5
+    kn = l2norm(k.astype(np.float64))
+    out = np.zeros((T, H, dv), dtype=np.float64)
+    for h in range(H):
+        S = np.zeros((dk, dv), dtype=np.float64)
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            C = c1 - c0
+            Q, K, V = qn[c0:c1, h], kn[c0:c1, h], v[c0:c1, h].astype(np.float64)
+            b = beta[c0:c1, h].astype(np.float64)[:, None]
+            cum = np.cumsum(g[c0:c1, h].astype(np.float64))
+            D = np.tril(np.exp(np.minimum(cum[:, None] - cum[None, :], 0.0)))
+            A = np.tril((b * K) @ K.T * D, -1)
+            M = np.eye(C) + A  # unit lower triangular: solve by forward substitution
+            Y = np.concatenate([b * V, b * K * np.exp(cum)[:, None]], axis=1)
+            X = np.zeros_like(Y)
+            for i in range(C):
+                X[i] = Y[i] - M[i, :i] @ X[:i]
+            U, W = X[:, :dv], X[:, dv:]
+            u = U - W @ S
+            out[c0:c1, h] = (Q * np.exp(cum)[:, None]) @ S + (Q @ K.T * D) @ u
+            S = np.exp(cum[-1]) * S + (K * np.exp(cum[-1] - cum)[:, None]).T @ u
+    return out.astype(np.float32)
+
+
 def gated_deltanet(weights: dict, cfg: dict, p: str, x: np.ndarray) -> np.ndarray:
     """GatedDeltaNet::forward (qwen3_5.rs:481-545) for one text; x: [T, H] normed."""
     T = x.shape[0]

@@ -61,3 +61,19 @@ def test_recurrent_delta_rule_on_a_hand_case():
         want.append(S * n)
     got = Q35.gated_delta_rule(q, k, v, g, beta)[:, 0, 0]
     assert np.allclose(got, want, atol=1e-6)
+
+
+def test_chunked_form_equals_the_recurrence():
+    """The chunked (WY) form, the structure of a tensor-core kernel, gives the
+    recurrent rule's outputs for lengths below, at and across chunk sizes."""
+    rng = np.random.default_rng(3)
+    for T, chunk, dk, dv in [(1, 64, 8, 8), (5, 4, 8, 16), (64, 64, 16, 8), (65, 64, 8, 8), (200, 64, 32, 32),
+                             (37, 8, 16, 16)]:
+        q = rng.standard_normal((T, 2, dk)).astype(np.float32)
+        k = rng.standard_normal((T, 2, dk)).astype(np.float32)
+        v = rng.standard_normal((T, 2, dv)).astype(np.float32)
+        g = -np.abs(rng.standard_normal((T, 2))).astype(np.float32)
+        beta = Q35.sigmoid(rng.standard_normal((T, 2)).astype(np.float32))
+        want = Q35.gated_delta_rule(q, k, v, g, beta)
+        got = Q35.gated_delta_rule_chunked(q, k, v, g, beta, chunk=chunk)
+        assert np.abs(got - want).max() < 1e-5, (T, chunk)
