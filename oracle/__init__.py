@@ -13,9 +13,14 @@ here. Each function cites the reference file:line it restates. Parity pins:
 * ModernBERT + SPLADE pooling: the reference's ``tiny_splade`` golden fixture
   (``crates/inl-sparse/tests/fixtures/tiny_splade/golden.json``), copied into
   ``tests/golden/`` by ``tests/golden/make_golden.py``.
-* Qwen3: no golden vector exists without the real checkpoint; pinned by the
-  reference's own unit-test invariants (textbook RMSNorm, manual half-split
-  RoPE, padding invariance, backend agreement) restated in
-  ``tests/test_oracle_qwen3.py`` and by a second-opinion comparison with
-  ``transformers`` ``Qwen3Model`` on the same random weights.
+* EmbeddingGemma-style tower: the reference's ``tiny_embeddinggemma2`` golden
+  (``crates/inl-text/tests/fixtures/tiny_embeddinggemma2/golden.json``).
+* Qwen3.5 late tower (``qwen3_5.py``): the reference's ``tiny_qwen3_5_late``
+  golden (``crates/inl-late/tests/fixtures/tiny_qwen3_5_late/golden.json``).
+* Qwen3: parity unpinned by golden vectors (partial). No golden vector exists
+  without the real checkpoint; the oracle is checked against the reference's
+  own unit-test invariants (textbook RMSNorm, manual half-split RoPE, padding
+  invariance, backend agreement) restated in ``tests/test_oracle_qwen3.py``,
+  and against a second opinion, ``transformers`` ``Qwen3Model`` on the same
+  random weights.
 """

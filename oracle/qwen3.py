@@ -11,6 +11,13 @@ pad length, a shift attention is invariant to (the reference pins this with
 its padding-invariance test, crates/inl-text/src/qwen3/mod.rs:646-669). The
 packed form used here gives every text positions 0..L-1 and attends only
 within the text, which is the same function.
+
+Parity: unpinned by golden vectors (partial). The reference's only Qwen3
+golden (crates/inl-text/tests/fixtures/qwen3embedding/golden_real.json) needs
+the real checkpoint, which is absent. tests/test_oracle_qwen3.py checks this
+restatement against the reference's own unit-test invariants and against
+transformers' Qwen3Model on the same random weights (a second opinion, not
+the reference).
 """
 from __future__ import annotations
 
