@@ -449,12 +449,28 @@ class DataParallelEmbedder:
     thread per device, batches assigned longest-processing-time first, no
     collective; results gathered on the host by input index."""
 
-    def __init__(self, models: Sequence[CudaModel], max_batch_tokens: int = DEFAULT_PACKED_TOKENS):
+    def __init__(self, models: Sequence[CudaModel], max_batch_tokens: int = DEFAULT_PACKED_TOKENS,
+                 tokenizer: TextTokenizer | None = None, max_length: int = DEFAULT_MAX_LENGTH,
+                 passage_prefix: str | None = None):
         self.models = list(models)
         self.max_batch_tokens = max_batch_tokens
+        self.tokenizer = tokenizer
+        self.max_length = max_length
+        self.passage_prefix = passage_prefix
 
-    def embed(self, tokens: Sequence[Sequence[int]]) -> list[np.ndarray]:
-        texts = [np.asarray(t, dtype=np.uint32) for t in tokens]
+    def embed(self, inputs: Sequence) -> list[np.ndarray]:
+        """Strings (passage prefix, tokenized and truncated by the tokenizer)
+        or token-id lists (truncated to max_length)."""
+        items = list(inputs)
+        kinds = {isinstance(x, str) for x in items}
+        if len(kinds) > 1:
+            raise InlError.invalid_input("inputs mix strings and token-id lists")
+        if kinds == {True}:
+            if self.tokenizer is None:
+                raise InlError.config("string inputs need a tokenizer (tokenizer=TextTokenizer.from_file(...))")
+            texts = self.tokenizer.encode([(self.passage_prefix or "") + t for t in items], self.max_length)
+        else:
+            texts = _truncate(items, self.max_length)
         lengths = [len(t) for t in texts]
         order = longest_first(lengths)
         batches = [[order[k] for k in r] for r in plan_packed([lengths[i] for i in order], self.max_batch_tokens)]
@@ -469,6 +485,9 @@ class DataParallelEmbedder:
                 for b in plan[w]:
                     ids, cu = pack(texts, batches[b])
                     out = self.models[w].embed(ids, cu)
+                    if len(out) != len(batches[b]):  # crates/inl-text/src/native.rs:674-679
+                        raise InlError.inference(f"native embedding returned {len(out)} results for "
+                                                 f"{len(batches[b])} inputs")
                     for i, v in zip(batches[b], out):
                         results[i] = v
             except BaseException as e:

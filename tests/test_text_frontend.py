@@ -69,7 +69,7 @@ class RecordingModel:
         self.dtype, self.device, self.seen = "bf16", 0, []
 
     def info(self):
-        return {"dense_dim": 2, "arch": 0, "multivector_dim": 2, "sparse_dim": 4}
+        return {"dense_dim": 2, "arch": 0, "multivector_dim": 2, "sparse_dim": 4, "is_causal": True}
 
     def _segments(self, ids, cu):
         segs = [ids[cu[i]:cu[i + 1]].tolist() for i in range(len(cu) - 1)]
@@ -157,3 +157,25 @@ def test_count_truncated_dense_and_sparse():
                for t, ids in zip(texts, tok.encode(["[D] " + t for t in texts], 9)))
     assert s.count_truncated(texts) == want == 2  # "short" and "x x x " are under 9 bytes
     assert model.seen == []  # nothing reached the model
+
+
+def test_data_parallel_embedder_takes_strings_and_checks_counts():
+    tok = _tok()
+    models = [RecordingModel(), RecordingModel()]
+    dp = inl.DataParallelEmbedder(models, max_batch_tokens=8, tokenizer=tok, max_length=9, passage_prefix="p ")
+    texts = ["a b c", "d e f g h i j k l m", "x"]
+    out = dp.embed(texts)
+    want = tok.encode(["p " + t for t in texts], 9)
+    assert [v[0] for v in out] == [len(w) for w in want]
+    assert sorted(map(tuple, models[0].seen + models[1].seen)) == sorted(tuple(w.tolist()) for w in want)
+    with pytest.raises(inl.ConfigError):
+        inl.DataParallelEmbedder(models).embed(["no tokenizer"])
+    with pytest.raises(inl.InvalidInputError):
+        dp.embed(["a", [1, 2]])
+
+    class Dropping(RecordingModel):
+        def embed(self, ids, cu, out_dim=0):
+            return super().embed(ids, cu)[:-1]
+
+    with pytest.raises(inl.InferenceError):
+        inl.DataParallelEmbedder([Dropping()]).embed([[1, 2], [3]])
