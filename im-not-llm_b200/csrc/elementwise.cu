@@ -229,6 +229,48 @@ __global__ void qk_norm_rope_kernel(QkRopeArgs a) {
   for (int e = 0; e < E; ++e) st_f<T>(row, lane * E + e, x[e]);
 }
 
+// Heads of d <= 32 features (8, 16, 32): one warp per (token, head), lane l < d
+// holds element l and its RoPE partner sits in lane l ^ (d / 2).
+template <typename T>
+__global__ void qk_norm_rope_narrow_kernel(QkRopeArgs a) {
+  const int warps = blockDim.x >> 5;
+  const long long item = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
+  if (item >= static_cast<long long>(a.T) * heads) return;
+  const int t = static_cast<int>(item / heads);
+  const int h = static_cast<int>(item - static_cast<long long>(t) * heads);
+  const int d = a.d, half = d / 2;
+  const bool on = lane < d;
+  T* row = reinterpret_cast<T*>(a.qkv) + static_cast<long long>(t) * a.ld + static_cast<long long>(h) * d;
+  const bool is_q = h < a.hq;
+  const bool is_k = !is_q && h < a.hq + a.hkv;
+  const float* w = is_q ? a.qw : (is_k ? a.kw : nullptr);
+  const bool norm = is_q ? (a.qw != nullptr) : (is_k ? (a.kw != nullptr) : true);
+  float x = on ? ld_f<T>(row, lane) : 0.f;
+  if (norm) {
+    const float inv = rsqrtf(warp_sum(x * x) / static_cast<float>(d) + a.eps);
+    float v = x * inv;
+    if (w && on) v *= w[lane];
+    x = sizeof(T) == 2 ? bf16_round(v) : v;
+  }
+  if (is_q || is_k) {
+    int p = a.pos[t];
+    if (p < 0 || p >= a.max_pos) {
+      if (lane == 0 && a.status) atomicCAS(a.status, 0, INL_DEV_BAD_INDEX);
+      p = 0;
+    }
+    const float other = __shfl_xor_sync(0xffffffffu, x, half);
+    if (on) {
+      const bool first = lane < half;
+      const int i = first ? lane : lane - half;
+      const float c = a.cos[static_cast<long long>(p) * half + i], sn = a.sin[static_cast<long long>(p) * half + i];
+      x = first ? (x * c - other * sn) : (x * c + other * sn);
+    }
+  }
+  if (on) st_f<T>(row, lane, x);
+}
+
 // ------------------------------------------------------------ positions
 __global__ void token_positions_kernel(const int* __restrict__ cu, int n, int T, int* __restrict__ pos) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -339,10 +381,11 @@ __global__ void convert_rows_kernel(const TS* __restrict__ src, int rows, int co
   }
 }
 
-// h[r] += RMSNorm(a[r]) * w   (the Gemma post-attention / post-feedforward norms)
+// h[r] = (h[r] + RMSNorm(a[r]) * w) * scale   (the Gemma post-attention / post-feedforward
+// norms; with a scale, the PLE block's post norm and the layer scalar)
 template <typename T>
 __global__ void add_rms_norm_kernel(T* __restrict__ h, const T* __restrict__ a, const float* __restrict__ w,
-                                    float eps, int rows, int H) {
+                                    float eps, int rows, int H, const float* __restrict__ scale) {
   const int warps = blockDim.x >> 5;
   const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -356,10 +399,67 @@ __global__ void add_rms_norm_kernel(T* __restrict__ h, const T* __restrict__ a, 
   }
   const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(H) + eps);
   const bool is_bf16 = sizeof(T) == 2;
+  if (scale) {
+    // the scalar in the model dtype; the sum rounded before the multiply
+    const float sc = is_bf16 ? bf16_round(*scale) : *scale;
+    for (int c = lane; c < H; c += 32) {
+      float n = ld_f<T>(ar, c) * inv * w[c];
+      if (is_bf16) n = bf16_round(n);
+      float sum = ld_f<T>(hr, c) + n;
+      if (is_bf16) sum = bf16_round(sum);
+      st_f<T>(hr, c, sum * sc);
+    }
+    return;
+  }
   for (int c = lane; c < H; c += 32) {
     float n = ld_f<T>(ar, c) * inv * w[c];
     if (is_bf16) n = bf16_round(n);  // the normed branch in the model dtype, then the add
     st_f<T>(hr, c, ld_f<T>(hr, c) + n);
+  }
+}
+
+// In place, per row of `cols`: x = RMSNorm(x * scale) * w, the product rounded
+// to the model dtype first (the per-layer embedding inputs of EmbeddingGemma 2).
+template <typename T>
+__global__ void scaled_rms_norm_kernel(T* __restrict__ x, long long rows, int cols, float scale,
+                                       const float* __restrict__ w, float eps) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  T* xr = x + row * cols;
+  const bool is_bf16 = sizeof(T) == 2;
+  float ss = 0.f;
+  for (int c = lane; c < cols; c += 32) {
+    float v = ld_f<T>(xr, c) * scale;
+    if (is_bf16) v = bf16_round(v);
+    ss += v * v;
+  }
+  const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(cols) + eps);
+  for (int c = lane; c < cols; c += 32) {
+    float v = ld_f<T>(xr, c) * scale;
+    if (is_bf16) v = bf16_round(v);
+    st_f<T>(xr, c, v * inv * w[c]);
+  }
+}
+
+// out[r, j] = act(x[r, j]) * y[r, j] with row strides (the PLE gate: the
+// activated bottleneck times this layer's slice of the per-layer inputs).
+template <typename T, int ACT>
+__global__ void act_mul_rows_kernel(const T* x, long long ldx, const T* __restrict__ y, long long ldy, int rows,
+                                    int cols, T* out, long long ldo) {
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols;
+    const int j = static_cast<int>(i - r * cols);
+    const float g = ld_f<T>(x, r * ldx + j);
+    float a;
+    if constexpr (ACT == INL_ACT_SILU) a = silu_f(g);
+    else if constexpr (ACT == INL_ACT_GELU_ERF) a = gelu_erf_f(g);
+    else a = gelu_tanh_f(g);
+    if (sizeof(T) == 2) a = bf16_round(a);
+    st_f<T>(out, r * ldo + j, a * ld_f<T>(y, r * ldy + j));
   }
 }
 
@@ -484,6 +584,11 @@ int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s) {
   const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
   const long long items = static_cast<long long>(a.T) * heads;
   const int grid = rows_grid(items, 8);
+  if (a.d == 8 || a.d == 16 || a.d == 32) {
+    if (a.bf16) qk_norm_rope_narrow_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+    else qk_norm_rope_narrow_kernel<float><<<grid, 256, 0, s>>>(a);
+    return ok(cudaGetLastError());
+  }
   const int E = a.d / 32;
   if (a.d % 32 != 0) return -1;
 #define INL_QKR(EE)                                                              \
@@ -583,15 +688,49 @@ int norm_act(const void* x, int x_bf16, long long ldx, const float* w, const flo
   return ok(cudaGetLastError());
 }
 
-int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s) {
+int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s,
+                 const float* scale) {
   if (rows <= 0) return 0;
   const int grid = rows_grid(rows, 4);
   if (bf16)
-    add_rms_norm_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<__nv_bfloat16*>(h),
-                                                             static_cast<const __nv_bfloat16*>(a), w, eps, rows, H);
+    add_rms_norm_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(a), w, eps, rows, H, scale);
   else
     add_rms_norm_kernel<float><<<grid, 128, 0, s>>>(static_cast<float*>(h), static_cast<const float*>(a), w, eps,
-                                                     rows, H);
+                                                     rows, H, scale);
+  return ok(cudaGetLastError());
+}
+
+int scaled_rms_norm(void* x, int bf16, long long rows, int cols, float scale, const float* w, float eps,
+                    cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const int grid = rows_grid(rows, 4);
+  if (bf16)
+    scaled_rms_norm_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<__nv_bfloat16*>(x), rows, cols, scale, w,
+                                                                eps);
+  else
+    scaled_rms_norm_kernel<float><<<grid, 128, 0, s>>>(static_cast<float*>(x), rows, cols, scale, w, eps);
+  return ok(cudaGetLastError());
+}
+
+int act_mul_rows(const void* x, long long ldx, const void* y, long long ldy, int bf16, int rows, int cols, int act,
+                 void* out, long long ldo, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const long long total = static_cast<long long>(rows) * cols;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+#define INL_AMR(T, A)                                                                                           \
+  act_mul_rows_kernel<T, A><<<grid, 256, 0, s>>>(static_cast<const T*>(x), ldx, static_cast<const T*>(y), ldy, \
+                                                 rows, cols, static_cast<T*>(out), ldo)
+  if (bf16) {
+    if (act == INL_ACT_SILU) INL_AMR(__nv_bfloat16, INL_ACT_SILU);
+    else if (act == INL_ACT_GELU_ERF) INL_AMR(__nv_bfloat16, INL_ACT_GELU_ERF);
+    else INL_AMR(__nv_bfloat16, INL_ACT_GELU_TANH);
+  } else {
+    if (act == INL_ACT_SILU) INL_AMR(float, INL_ACT_SILU);
+    else if (act == INL_ACT_GELU_ERF) INL_AMR(float, INL_ACT_GELU_ERF);
+    else INL_AMR(float, INL_ACT_GELU_TANH);
+  }
+#undef INL_AMR
   return ok(cudaGetLastError());
 }
 

@@ -144,8 +144,18 @@ int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, 
 int norm_act(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
              void* out, int out_bf16, long long ldo, cudaStream_t s);
 
-// h[r] += RMSNorm(a[r]) * w (row-wise, rows x H, both in the model dtype).
-int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s);
+// h[r] += RMSNorm(a[r]) * w (row-wise, rows x H, both in the model dtype); with
+// `scale` (one f32 on the device), h[r] = (h[r] + RMSNorm(a[r]) * w) * scale.
+int add_rms_norm(void* h, const void* a, int bf16, const float* w, float eps, int rows, int H, cudaStream_t s,
+                 const float* scale = nullptr);
+
+// In place over rows x cols (contiguous): x = RMSNorm(x * scale) * w.
+int scaled_rms_norm(void* x, int bf16, long long rows, int cols, float scale, const float* w, float eps,
+                    cudaStream_t s);
+
+// out[r, j] = act(x[r, j]) * y[r, j] over rows x cols with row strides (model dtype; out may be x).
+int act_mul_rows(const void* x, long long ldx, const void* y, long long ldy, int bf16, int rows, int cols, int act,
+                 void* out, long long ldo, cudaStream_t s);
 
 // dst[r] = src[idx[r]] for r < n (rows of H values).
 int gather_rows(const void* src, int bf16, long long lds, const int* idx, int n, int H, void* dst, cudaStream_t s);

@@ -218,6 +218,11 @@ int parse_config(const std::string& text, ModelConfig& c) {
     double full = num_or(root, "rope_theta", 1000000.0), slide = num_or(root, "rope_local_base_freq", 10000.0);
     nested_theta(root, "full_attention", &full);
     nested_theta(root, "sliding_attention", &slide);
+    if (const inl::json::Value* rp = root.get("rope_parameters"))  // Config::validate (gemma2.rs:157-164)
+      for (const char* kind : {"full_attention", "sliding_attention"})
+        if (const inl::json::Value* k = rp->get(kind))
+          if (std::string t = str_or(*k, "rope_type", "default"); t != "default")
+            return fail(INL_ERR_CONFIG, "config: rope_type \"" + t + "\" for " + kind);
     c.theta = full;
     c.theta_local = slide;
     c.attn_scale = 1.0f;  // unscaled scores: q and k are RMS-normalised per head
@@ -236,10 +241,41 @@ int parse_config(const std::string& text, ModelConfig& c) {
       if (c.full_every <= 0) return fail(INL_ERR_CONFIG, "config: full_attention_every_n_layers must be positive");
       for (int i = 0; i < c.layers; ++i) c.layer_global[i] = (i % c.full_every) == c.full_every - 1;
     }
-    if (const inl::json::Value* plc = root.get("per_layer_config"); plc && !plc->obj.empty())
-      return fail(INL_ERR_CONFIG, "config: per-layer head shapes are not supported by the CUDA tower");
-    if (num_or(root, "hidden_size_per_layer_input", 0) > 0)
-      return fail(INL_ERR_CONFIG, "config: per-layer embeddings (PLE) are not supported by the CUDA tower");
+    // Per-layer head shapes (Config::layer / validate, crates/inl-text/src/gemma2.rs:150-204):
+    // per_layer_config is keyed by the layer index ("05"); each entry may set
+    // head_dim and num_key_value_heads. A key that is not a layer index is an error.
+    c.layer_d.assign(c.layers, c.d);
+    c.layer_kv.assign(c.layers, c.hkv);
+    if (const inl::json::Value* plc = root.get("per_layer_config"); plc && plc->kind == inl::json::Value::Object) {
+      for (const auto& [key, over] : plc->obj) {
+        const size_t digits = key.find_first_not_of("0123456789");
+        const bool numeric = !key.empty() && digits == std::string::npos && key.size() <= 9;
+        const int index = numeric ? std::stoi(key) : -1;
+        if (index < 0 || index >= c.layers)
+          return fail(INL_ERR_CONFIG, "config: per_layer_config key \"" + key + "\" is not a layer index");
+        if (const inl::json::Value* hd = over.get("head_dim"); hd && hd->is_num())
+          c.layer_d[index] = static_cast<int>(hd->num);
+        if (const inl::json::Value* kv = over.get("num_key_value_heads"); kv && kv->is_num())
+          c.layer_kv[index] = static_cast<int>(kv->num);
+      }
+    }
+    for (int l = 0; l < c.layers; ++l) {
+      if (c.layer_d[l] <= 0 || (c.layer_d[l] & 1))
+        return fail(INL_ERR_CONFIG, "config: head_dim " + std::to_string(c.layer_d[l]) + " of layer " +
+                                        std::to_string(l));
+      if (c.layer_kv[l] <= 0 || c.hq % c.layer_kv[l] != 0)
+        return fail(INL_ERR_CONFIG, "config: " + std::to_string(c.hq) + " attention heads over " +
+                                        std::to_string(c.layer_kv[l]) + " KV heads in layer " + std::to_string(l));
+    }
+    // One rotary table per layer kind, built for the head_dim of that kind's
+    // first layer (gemma2.rs:566-572): every layer of a kind shares it.
+    for (int l = 0; l < c.layers; ++l)
+      for (int k = 0; k < l; ++k)
+        if (c.layer_global[k] == c.layer_global[l] && c.layer_d[k] != c.layer_d[l])
+          return fail(INL_ERR_CONFIG, "config: layers " + std::to_string(k) + " and " + std::to_string(l) +
+                                          " are of one attention kind with different head_dim");
+    c.ple = static_cast<int>(num_or(root, "hidden_size_per_layer_input", 0));
+    if (c.ple < 0) return fail(INL_ERR_CONFIG, "config: hidden_size_per_layer_input must not be negative");
     const std::string act = str_or(root, "hidden_activation", "gelu_pytorch_tanh");
     if (act != "gelu_pytorch_tanh") return fail(INL_ERR_CONFIG, "config: hidden_activation must be gelu_pytorch_tanh");
     c.dense_dims = int_list(root.get("dense_dims"));
@@ -393,13 +429,15 @@ struct Loader {
   }
 };
 
-int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, float** pairs_out = nullptr) {
-  const int half = m->c.d / 2;
+int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, float** pairs_out = nullptr,
+               int head_dim = 0) {
+  const int d = head_dim > 0 ? head_dim : m->c.d;
+  const int half = d / 2;
   const int P = m->c.max_pos;
   std::vector<float> c(static_cast<size_t>(P) * half), s(static_cast<size_t>(P) * half);
   // RotaryTable::new (crates/inl-text/src/qwen3/mod.rs:129-153): f64 angles, stored f32.
   std::vector<double> inv(half);
-  for (int i = 0; i < half; ++i) inv[i] = 1.0 / std::pow(theta, static_cast<double>(2 * i) / m->c.d);
+  for (int i = 0; i < half; ++i) inv[i] = 1.0 / std::pow(theta, static_cast<double>(2 * i) / d);
   for (int p = 0; p < P; ++p)
     for (int i = 0; i < half; ++i) {
       const double a = static_cast<double>(p) * inv[i];
@@ -664,8 +702,9 @@ int load_modernbert(inl_model* m, Loader& L) {
   return INL_OK;
 }
 
-// EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:233-494 tensor names),
-// uniform head shape, no per-layer embeddings; dense head chain kept in f32.
+// EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:233-494 tensor names):
+// per-layer head shapes, the optional per-layer embeddings (PLE) and layer
+// scalars; dense head chain kept in f32.
 int load_gemma(inl_model* m, Loader& L) {
   const ModelConfig& c = m->c;
   const int bf = m->dtype == INL_DTYPE_BF16;
@@ -673,16 +712,28 @@ int load_gemma(inl_model* m, Loader& L) {
   const int gb = m->gated_split ? c.I : m->gate_block;
   const long long gstride = m->gated_split ? 0 : 2LL * gb;
   const long long up_off = m->gated_split ? c.I : gb;
-  if (c.d % 32 != 0) return fail(INL_ERR_CONFIG, "head_dim must be a multiple of 32");
-  if (L.has("ple.per_layer_model_projection.weight"))
-    return fail(INL_ERR_CONFIG, "per-layer embeddings (PLE) are not supported by the CUDA tower");
-  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv = q_out + 2 * kv_out;
+  for (int l = 0; l < c.layers; ++l) {
+    // head_dim the q/k norm + RoPE kernel and the attention kernels of this dtype take
+    const int d = c.dl(l);
+    const bool ok = bf ? (d == 64 || d == 128 || d == 256) : (d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256);
+    if (!ok)
+      return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(d) + " of layer " + std::to_string(l) +
+                                      " is not supported by the CUDA tower in " + (bf ? "bf16" : "f32"));
+  }
+  const bool ple = c.ple > 0;
+  if (!ple && L.has("ple.per_layer_model_projection.weight"))
+    return fail(INL_ERR_CONFIG, "checkpoint has per-layer embeddings but hidden_size_per_layer_input is 0");
   const size_t es = bf ? 2 : 4;
   int r;
   if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
+  if (ple) {  // PleBlock inputs (gemma2.rs:549-560, 626-630)
+    if ((r = L.matrix("ple.per_layer_model_projection.weight", c.layers * c.ple, c.H, &m->ple_model_proj, bf))) return r;
+    if ((r = L.vec("ple.per_layer_projection_norm.weight", c.ple, &m->ple_model_norm))) return r;
+  }
   m->layers.resize(c.layers);
   for (int l = 0; l < c.layers; ++l) {
     const std::string p = "layers." + std::to_string(l) + ".";
+    const int d = c.dl(l), q_out = c.hq * d, kv_out = c.kvl(l) * d, qkv = q_out + 2 * kv_out;
     inl::LayerWeights& w = m->layers[l];
     w.wqkv = L.alloc(static_cast<size_t>(qkv) * c.H * es);
     w.wo = L.alloc(static_cast<size_t>(c.H) * q_out * es);
@@ -697,12 +748,18 @@ int load_gemma(inl_model* m, Loader& L) {
     if ((r = L.upload(p + "mlp.gate_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, 0))) return r;
     if ((r = L.upload(p + "mlp.up_proj.weight", c.I, c.H, w.wgu, bf, c.H, gb, gstride, up_off))) return r;
     if ((r = L.upload(p + "mlp.down_proj.weight", c.H, c.I, w.wd, bf, c.I, c.H, 0, 0))) return r;
-    if ((r = L.vec(p + "self_attn.q_norm.weight", c.d, &w.qn))) return r;
-    if ((r = L.vec(p + "self_attn.k_norm.weight", c.d, &w.kn))) return r;
+    if ((r = L.vec(p + "self_attn.q_norm.weight", d, &w.qn))) return r;
+    if ((r = L.vec(p + "self_attn.k_norm.weight", d, &w.kn))) return r;
     if ((r = L.vec(p + "input_layernorm.weight", c.H, &w.ln1))) return r;
     if ((r = L.vec(p + "post_attention_layernorm.weight", c.H, &w.ln1_post))) return r;
     if ((r = L.vec(p + "pre_feedforward_layernorm.weight", c.H, &w.ln2))) return r;
     if ((r = L.vec(p + "post_feedforward_layernorm.weight", c.H, &w.ln2_post))) return r;
+    if (ple) {  // PleBlock and the layer scalar (gemma2.rs:264-272, 467-469)
+      if ((r = L.matrix(p + "ple_block.per_layer_input_gate.weight", c.ple, c.H, &w.ple_gate, bf))) return r;
+      if ((r = L.matrix(p + "ple_block.per_layer_projection.weight", c.H, c.ple, &w.ple_proj, bf))) return r;
+      if ((r = L.vec(p + "ple_block.post_per_layer_input_norm.weight", c.H, &w.ple_norm))) return r;
+      if ((r = L.vec(p + "layer_scalar", 1, &w.scalar))) return r;
+    }
   }
   if ((r = L.vec("norm.weight", c.H, &m->final_norm))) return r;
   // Dense head: "dense_head.<j>.weight" chain, else the checkpoint's embedding_projection.
@@ -720,8 +777,11 @@ int load_gemma(inl_model* m, Loader& L) {
   if (bf) {  // the reference multiplies by the scale cast to bf16 (crates/inl-text/src/gemma2.rs:575-587)
     m->c.embed_scale = __bfloat162float(__float2bfloat16_rn(m->c.embed_scale));
   }
-  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0))) return r;        // full layers
-  if ((r = build_rope(m, c.theta_local, &m->cos1, &m->sin1))) return r;  // sliding layers
+  // One table per layer kind, for the head_dim of its first layer (gemma2.rs:566-572).
+  int d_full = c.d, d_slide = c.d;
+  for (int l = c.layers - 1; l >= 0; --l) (c.layer_global[l] ? d_full : d_slide) = c.dl(l);
+  if ((r = build_rope(m, c.theta, &m->cos0, &m->sin0, nullptr, d_full))) return r;          // full layers
+  if ((r = build_rope(m, c.theta_local, &m->cos1, &m->sin1, nullptr, d_slide))) return r;  // sliding layers
   return INL_OK;
 }
 
@@ -850,6 +910,15 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
     attn_cols = std::max(attn_cols, static_cast<size_t>(c.lin_nv) * c.lin_dv);
     tmp_cols = std::max({tmp_cols, conv_dim, static_cast<size_t>(c.hq) * c.d});
   }
+  if (c.arch == inl::ARCH_GEMMA) {
+    // the widest layer's q | k | v and attention output; the PLE gate [T, ple]
+    for (int l = 0; l < c.layers; ++l) {
+      qkv_cols = std::max(qkv_cols, static_cast<size_t>(c.hq + 2 * c.kvl(l)) * c.dl(l));
+      attn_cols = std::max(attn_cols, static_cast<size_t>(c.hq) * c.dl(l));
+    }
+    tmp_cols = std::max(tmp_cols, static_cast<size_t>(c.ple));
+    if (c.ple > 0) INL_CUDA_TRY(m->ple_in.ensure(T * c.layers * c.ple * e), "workspace");
+  }
   INL_CUDA_TRY(m->h.ensure(T * c.H * e), "workspace");
   INL_CUDA_TRY(m->xn.ensure(T * c.H * e), "workspace");
   INL_CUDA_TRY(m->qkv.ensure(T * std::max(qkv_cols, act_cols) * e), "workspace");
@@ -862,7 +931,8 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->pos.ensure(T * 4), "workspace");
   INL_CUDA_TRY(m->cu.ensure((text_cap(b.n) + 1) * 4), "workspace");
   INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
-  const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work) * 8 + 64;
+  if (m->qb_alt) INL_CUDA_TRY(m->work_alt.ensure(static_cast<size_t>(std::max(m->n_work_alt, 1)) * 8), "workspace");
+  const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work + m->n_work_alt) * 8 + 64;
   if (stage > m->h_stage_bytes) {
     const size_t want = std::max({stage * 2, m->h_stage_bytes * 2, size_t(1) << 20});
     if (m->h_stage) {
@@ -892,15 +962,30 @@ std::vector<std::pair<int, int2>> attention_work(const int* cu_host, int n, int 
 }
 
 int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch& b, int* n_work_out) {
-  const int qb = inl::attention_q_block(m->dtype == INL_DTYPE_BF16, m->c.d);
+  const int bf = m->dtype == INL_DTYPE_BF16;
+  const int qb = inl::attention_q_block(bf, m->c.d);
   const std::vector<std::pair<int, int2>> items = attention_work(b.cu_host, b.n, qb, m->c.causal != 0);
   const int n_work = static_cast<int>(items.size());
+  // A second list for layers whose head_dim takes another query block.
+  m->qb_alt = 0;
+  for (int l = 0; l < m->c.layers && !m->c.layer_d.empty(); ++l) {
+    const int q = inl::attention_q_block(bf, m->c.dl(l));
+    if (q != qb) m->qb_alt = q;
+  }
+  std::vector<std::pair<int, int2>> alt;
+  if (m->qb_alt) alt = attention_work(b.cu_host, b.n, m->qb_alt, m->c.causal != 0);
+  m->n_work_alt = static_cast<int>(alt.size());
   int r = ensure_workspace(m, b, n_work);
   if (r) return r;
   int* cu_stage = m->h_stage;
   std::memcpy(cu_stage, b.cu_host, static_cast<size_t>(b.n + 1) * 4);
   int2* work_stage = reinterpret_cast<int2*>(cu_stage + ((b.n + 1 + 3) & ~3));
   for (int i = 0; i < n_work; ++i) work_stage[i] = items[i].second;
+  for (int i = 0; i < m->n_work_alt; ++i) work_stage[n_work + i] = alt[i].second;
+  if (m->n_work_alt > 0)
+    INL_CUDA_TRY(cudaMemcpyAsync(m->work_alt.p, work_stage + n_work, static_cast<size_t>(m->n_work_alt) * 8,
+                                 cudaMemcpyHostToDevice, m->stream),
+                 "work list upload");
   INL_CUDA_TRY(cudaMemcpyAsync(m->cu.p, cu_stage, static_cast<size_t>(b.n + 1) * 4, cudaMemcpyHostToDevice,
                                m->stream),
                "cu_seqlens upload");
@@ -1316,30 +1401,62 @@ int modernbert_tower(inl_model* m, const Batch& b, int n_work) {
   return INL_OK;
 }
 
+// Attention arguments of one layer's head shape (per-layer head_dim and KV
+// heads); the query block and work list follow the head_dim.
+void layer_heads(inl_model* m, inl::AttnArgs& aa, int d, int kv) {
+  aa.d = d;
+  aa.hkv = kv;
+  const int qb = inl::attention_q_block(aa.bf16, d);
+  if (qb != aa.q_block && qb == m->qb_alt) {
+    aa.q_block = qb;
+    aa.work = m->work_alt.as<int2>();
+    aa.n_work = m->n_work_alt;
+  }
+}
+
 // EmbeddingGemma-style tower (crates/inl-text/src/gemma2.rs:473-494, 622-647);
-// leaves the last hidden state (before the final norm) in m->h.
+// leaves the last hidden state (before the final norm) in m->h. Per layer:
+// h += postN(Attn(inN(h))); h += postFF(MLP(preFF(h))); then, with per-layer
+// embeddings, h = (h + postPLE(proj(gelu_tanh(gate(h)) * ple_l))) * scalar,
+// where ple = RMSNorm(reshape(h0 W_ple^T * H^-1/2, [T, layers, ple])) of the
+// scaled token embeddings h0.
 int gemma_tower(inl_model* m, const Batch& b, int n_work) {
   const ModelConfig& c = m->c;
   const int bf = m->dtype == INL_DTYPE_BF16;
-  const int T = b.T, H = c.H;
-  const int q_out = c.hq * c.d, kv_out = c.hkv * c.d, qkv_cols = q_out + 2 * kv_out;
+  const int T = b.T, H = c.H, P = c.ple;
   cudaStream_t s = m->stream;
   const int plain = bf ? INL_EPI_BF16 : INL_EPI_F32;
+  const size_t e = es(m);
   INL_K_TRY(inl::embed_gather(m->ids.as<uint32_t>(), T, m->embed, bf, c.V, H, c.embed_scale, m->h.p, bf,
                               m->d_status, s),
             "embedding");
   m->launches++;
+  if (P > 0) {  // per-layer inputs, once per forward (gemma2.rs:626-630)
+    INL_K_TRY(linear(m, m->h.p, H, m->ple_model_proj, T, c.layers * P, H, plain, 0, m->ple_in.p, c.layers * P,
+                     nullptr, 0, 7),
+              "per-layer embedding projection");
+    INL_K_TRY(inl::scaled_rms_norm(m->ple_in.p, bf, static_cast<long long>(T) * c.layers, P,
+                                   static_cast<float>(std::pow(static_cast<double>(H), -0.5)), m->ple_model_norm,
+                                   c.eps, s),
+              "per-layer embedding norm");
+    m->launches++;
+  }
   for (int l = 0; l < c.layers; ++l) {
     const inl::LayerWeights& w = m->layers[l];
     const bool full = c.layer_global[l] != 0;
+    const int d = c.dl(l), kv = c.kvl(l);
+    const int q_out = c.hq * d, kv_out = kv * d, qkv_cols = q_out + 2 * kv_out;
     INL_K_TRY(inl::rms_norm(m->h.p, bf, H, w.ln1, c.eps, T, H, m->xn.p, bf, H, s), "input norm");
     INL_K_TRY(linear(m, m->xn.p, H, w.wqkv, T, qkv_cols, H, plain, 0, m->qkv.p, qkv_cols, nullptr, 0, 0), "qkv");
     inl::QkRopeArgs qa = rope_args(m, T, qkv_cols, full);
+    qa.d = d;
+    qa.hkv = kv;
     qa.qw = w.qn;
     qa.kw = w.kn;
     qa.v_norm = 1;
     INL_K_TRY(inl::qk_norm_rope(qa, s), "q/k/v norm + rope");
     inl::AttnArgs aa = attn_args(m, b, n_work, qkv_cols, q_out, kv_out);
+    layer_heads(m, aa, d, kv);
     aa.scale = c.attn_scale;
     aa.window = full ? -1 : c.sliding_window;
     INL_K_TRY(run_attention(m, aa, s), "attention");
@@ -1352,6 +1469,19 @@ int gemma_tower(inl_model* m, const Batch& b, int n_work) {
     INL_K_TRY(linear(m, m->qkv.p, c.I, w.wd, T, H, c.I, plain, 0, m->xn.p, H, nullptr, 0, 3), "down projection");
     INL_K_TRY(inl::add_rms_norm(m->h.p, m->xn.p, bf, w.ln2_post, c.eps, T, H, s), "post-feedforward norm");
     m->launches++;
+    if (P > 0) {  // PleBlock::forward and the layer scalar (gemma2.rs:279-283, 490-493)
+      INL_K_TRY(linear(m, m->h.p, H, w.ple_gate, T, P, H, plain, 0, m->tmp.p, P, nullptr, 0, 7),
+                "per-layer input gate");
+      INL_K_TRY(inl::act_mul_rows(m->tmp.p, P, static_cast<const char*>(m->ple_in.p) + static_cast<size_t>(l) * P * e,
+                                  static_cast<long long>(c.layers) * P, bf, T, P, INL_ACT_GELU_TANH, m->tmp.p, P, s),
+                "per-layer gate");
+      m->launches++;
+      INL_K_TRY(linear(m, m->tmp.p, P, w.ple_proj, T, H, P, plain, 0, m->xn.p, H, nullptr, 0, 7),
+                "per-layer projection");
+      INL_K_TRY(inl::add_rms_norm(m->h.p, m->xn.p, bf, w.ple_norm, c.eps, T, H, s, w.scalar),
+                "per-layer norm and scalar");
+      m->launches++;
+    }
   }
   return INL_OK;
 }
@@ -1830,7 +1960,8 @@ void inl_cuda_model_destroy(inl_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (void* p : m->allocs) cudaFree(p);
   for (DevBuf* d : {&m->h, &m->xn, &m->qkv, &m->attn, &m->ids, &m->cu, &m->pos, &m->work, &m->out, &m->pooled,
-                    &m->tmp, &m->ss_a, &m->ss_b, &m->speak_idx, &m->speak_seg, &m->pooled_i, &m->head_buf})
+                    &m->tmp, &m->ss_a, &m->ss_b, &m->speak_idx, &m->speak_seg, &m->pooled_i, &m->head_buf,
+                    &m->ple_in, &m->work_alt})
     d->release();
   for (auto& r : m->prof) {
     cudaEventDestroy(r.start);

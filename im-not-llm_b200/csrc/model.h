@@ -50,6 +50,14 @@ struct ModelConfig {
   std::vector<char> layer_linear;
   int lin_nk = 0, lin_nv = 0, lin_dk = 0, lin_dv = 0, conv_k = 0;
   int rot = 0;
+  // EmbeddingGemma 2 (crates/inl-text/src/gemma2.rs:78-211): head_dim and KV
+  // heads of every layer after the per_layer_config overrides (empty = d and
+  // hkv on every layer), and the per-layer embedding width
+  // (hidden_size_per_layer_input; 0 = no per-layer embeddings).
+  std::vector<int> layer_d, layer_kv;
+  int ple = 0;
+  int dl(int l) const { return layer_d.empty() ? d : layer_d[l]; }
+  int kvl(int l) const { return layer_kv.empty() ? hkv : layer_kv[l]; }
 };
 
 struct TensorSrc {
@@ -112,6 +120,13 @@ struct LayerWeights {
   float* dt_bias = nullptr;
   float* a_log = nullptr;
   float* lin_norm = nullptr;
+  // EmbeddingGemma 2 per-layer embedding block (PleBlock, crates/inl-text/src/gemma2.rs:256-283):
+  // input gate [ple, H], projection [H, ple] in the model dtype; post norm [H] and the layer
+  // scalar [1] in f32.
+  void* ple_gate = nullptr;
+  void* ple_proj = nullptr;
+  float* ple_norm = nullptr;
+  float* scalar = nullptr;
 };
 
 struct ProfileRec {
@@ -156,8 +171,18 @@ struct inl_model {
   float* open_mask = nullptr;  // [V] 1 / 0
   int* canon = nullptr;        // [V] canonical term or null
   int sparse_dim = 0;
+  // EmbeddingGemma 2 per-layer embeddings: projection of the scaled token
+  // embeddings [layers * ple, H] (model dtype) and the norm of each layer's slice [ple]
+  void* ple_model_proj = nullptr;
+  float* ple_model_norm = nullptr;
   // workspaces
   inl::DevBuf h, xn, qkv, attn, ids, cu, pos, work, out, pooled, tmp;
+  inl::DevBuf ple_in;  // [T, layers * ple] per-layer inputs of the batch
+  // Attention work list for layers whose head_dim takes another query block
+  // than c.d's (per-layer head shapes); n_work_alt = 0 when every layer shares one.
+  inl::DevBuf work_alt;
+  int qb_alt = 0;
+  int n_work_alt = 0;
   inl::DevBuf ss_a, ss_b;  // per-64-column sums of squares of h (folded RMSNorm)
   inl::DevBuf speak_idx, speak_seg, pooled_i, head_buf;  // SPLADE head scratch
   bool fused = false;      // bf16 fused layer (folded norms, QKV epilogue)

@@ -98,6 +98,37 @@ GEMMA_TINY = dict(GEMMA_STYLE, vocab_size=1000, hidden_size=256, intermediate_si
                   full_attention_every_n_layers=2, dense_dims=[512, 256])
 MATRYOSHKA_DIMS = (128, 256, 512, 768)
 
+# EmbeddingGemma 2 text tower as the reference loads it
+# (crates/inl-text/src/gemma2.rs:78-211): nested text_config, per-layer
+# embeddings (PLE) and layer scalars, per_layer_config head overrides on the
+# full layer, embedding_projection to embedding_dim. Small widths; the full
+# layer's head_dim 256 and the sliding layers' 128 take different attention
+# query blocks in bf16.
+EMBEDDING_GEMMA2_SMALL = {
+    "model_type": "embedding_gemma2",
+    "text_config": {
+        "vocab_size": 1000,
+        "hidden_size": 256,
+        "intermediate_size": 512,
+        "num_hidden_layers": 4,
+        "num_attention_heads": 4,
+        "num_key_value_heads": 2,
+        "head_dim": 128,
+        "hidden_activation": "gelu_pytorch_tanh",
+        "rms_norm_eps": 1e-6,
+        "sliding_window": 24,
+        "layer_types": ["sliding_attention", "sliding_attention", "full_attention", "sliding_attention"],
+        "hidden_size_per_layer_input": 64,
+        "embedding_dim": 128,
+        "rope_parameters": {
+            "sliding_attention": {"rope_type": "default", "rope_theta": 10_000.0},
+            "full_attention": {"rope_type": "default", "rope_theta": 1_000_000.0},
+        },
+        "max_position_embeddings": 2048,
+        "per_layer_config": {"02": {"head_dim": 256, "num_key_value_heads": 1}},
+    },
+}
+
 
 @dataclass
 class Spec:
@@ -178,6 +209,44 @@ def gemma_specs(cfg: dict) -> list[Spec]:
     return specs
 
 
+def embedding_gemma2_specs(cfg: dict) -> list[Spec]:
+    """Tensor names of crates/inl-text/src/gemma2.rs:233-560 (text tower with
+    PLE, layer scalars, per-layer head shapes and embedding_projection)."""
+    tc = cfg.get("text_config", cfg)
+    H, I, V, L = tc["hidden_size"], tc["intermediate_size"], tc["vocab_size"], tc["num_hidden_layers"]
+    hq, P = tc["num_attention_heads"], tc["hidden_size_per_layer_input"]
+    over = {int(k): v for k, v in (tc.get("per_layer_config") or {}).items()}
+    specs = [Spec("embed_tokens.weight", (V, H), "linear"),
+             Spec("ple.per_layer_model_projection.weight", (L * P, H), "linear"),
+             Spec("ple.per_layer_projection_norm.weight", (P,), "norm")]
+    for i in range(L):
+        d = over.get(i, {}).get("head_dim") or tc["head_dim"]
+        kv = over.get(i, {}).get("num_key_value_heads") or tc["num_key_value_heads"]
+        p = f"layers.{i}."
+        specs += [
+            Spec(p + "self_attn.q_proj.weight", (hq * d, H), "linear"),
+            Spec(p + "self_attn.k_proj.weight", (kv * d, H), "linear"),
+            Spec(p + "self_attn.v_proj.weight", (kv * d, H), "linear"),
+            Spec(p + "self_attn.o_proj.weight", (H, hq * d), "linear"),
+            Spec(p + "self_attn.q_norm.weight", (d,), "norm"),
+            Spec(p + "self_attn.k_norm.weight", (d,), "norm"),
+            Spec(p + "mlp.gate_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.up_proj.weight", (I, H), "linear"),
+            Spec(p + "mlp.down_proj.weight", (H, I), "linear"),
+            Spec(p + "input_layernorm.weight", (H,), "norm"),
+            Spec(p + "post_attention_layernorm.weight", (H,), "norm"),
+            Spec(p + "pre_feedforward_layernorm.weight", (H,), "norm"),
+            Spec(p + "post_feedforward_layernorm.weight", (H,), "norm"),
+            Spec(p + "ple_block.per_layer_input_gate.weight", (P, H), "linear"),
+            Spec(p + "ple_block.per_layer_projection.weight", (H, P), "linear"),
+            Spec(p + "ple_block.post_per_layer_input_norm.weight", (H,), "norm"),
+            Spec(p + "layer_scalar", (1,), "norm"),
+        ]
+    specs.append(Spec("norm.weight", (H,), "norm"))
+    specs.append(Spec("embedding_projection.weight", (tc["embedding_dim"], H), "linear"))
+    return specs
+
+
 def generate(specs: list[Spec], seed: int = 0, std: float = 0.02, norm_jitter: float = 0.0) -> dict:
     """Draw every tensor of ``specs`` in order from one PCG64 stream."""
     rng = np.random.default_rng(seed)
@@ -208,6 +277,10 @@ def modernbert_weights(cfg: dict = MODERNBERT_SPLADE, seed: int = 0, norm_jitter
 
 def gemma_weights(cfg: dict = GEMMA_STYLE, seed: int = 0, norm_jitter: float = 0.0) -> dict:
     return generate(gemma_specs(cfg), seed=seed, norm_jitter=norm_jitter)
+
+
+def embedding_gemma2_weights(cfg: dict = EMBEDDING_GEMMA2_SMALL, seed: int = 0, norm_jitter: float = 0.0) -> dict:
+    return generate(embedding_gemma2_specs(cfg), seed=seed, norm_jitter=norm_jitter)
 
 
 def late_projection(cfg: dict = QWEN3_0_6B, out: int = LATE_PROJ_OUT, seed: int = 0) -> np.ndarray:

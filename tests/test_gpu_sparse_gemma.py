@@ -162,9 +162,12 @@ def test_gemma_tiny_sharp_attention_f32(gpu):
     assert cosine_rows(got, ref).min() >= 0.99999
 
 
-def test_gemma_rejects_per_layer_embeddings_and_bad_dims(gpu, gemma_tiny):
+def test_gemma_rejects_missing_per_layer_embeddings_and_bad_dims(gpu, gemma_tiny):
+    """A config with per-layer embeddings needs their weights (a load error,
+    as the reference's VarBuilder gives); an output dim above the model's is
+    a config error."""
     cfg, w, _ = gemma_tiny
-    with pytest.raises(inl.ConfigError):
+    with pytest.raises(inl.InferenceError, match="missing weight"):
         inl.CudaModel(dict(cfg, hidden_size_per_layer_input=16), w, dtype="bf16")
     m = inl.CudaModel(cfg, w, dtype="bf16")
     ids, cu = inl.synthetic.random_texts(2, 3, 9, cfg["vocab_size"], seed=3)

@@ -88,3 +88,21 @@ def test_dense_head_variant_is_unit_length_and_matryoshka():
     ref = full[:, :16] / np.linalg.norm(full[:, :16], axis=1, keepdims=True)
     assert np.abs(short - ref).max() < 1e-6
     assert math.isclose(float(np.sqrt(32.0)), float(np.float32(np.sqrt(32.0))), rel_tol=1e-7)
+
+
+def test_synthetic_embedding_gemma2_exercises_ple_and_layer_shapes():
+    """The GPU test's synthetic EmbeddingGemma 2 is sensitive to what it
+    checks: dropping the per-layer embeddings, or the layer scalars, moves
+    the oracle's embeddings well beyond the bf16 floor (cosine 0.999)."""
+    import im_not_llm_b200 as inl
+
+    cfg = inl.synthetic.EMBEDDING_GEMMA2_SMALL
+    w = inl.synthetic.embedding_gemma2_weights(cfg, seed=2, norm_jitter=0.1)
+    assert G.layer_shape(cfg["text_config"], 2) == ("full_attention", 256, 1)
+    ids, cu = inl.synthetic.random_texts(4, 20, 120, cfg["text_config"]["vocab_size"], seed=5)
+    ref = G.embed(w, cfg, ids, cu, prefix="")
+    no_ple = G.embed({k: v for k, v in w.items() if not k.startswith("ple.")}, cfg, ids, cu, prefix="")
+    unit = {k: (np.ones_like(v) * 1.5 if k.endswith("layer_scalar") else v) for k, v in w.items()}
+    scaled = G.embed(unit, cfg, ids, cu, prefix="")
+    for other in (no_ple, scaled):
+        assert ((ref * other).sum(-1)).min() < 0.999
