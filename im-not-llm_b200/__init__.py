@@ -6,11 +6,11 @@ from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  
 from .model import CudaModel  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder, LateTask,  # noqa: F401
                      SparseEncoder, SparseVector, TextEmbedder, TextOptions)
-from .text import TextTokenizer  # noqa: F401
+from .text import Gemma2Task, TextTokenizer, gemma2_document  # noqa: F401
 from . import planner, synthetic, text  # noqa: F401
 
 __all__ = [
-    "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "InferenceError",
+    "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "Gemma2Task", "InferenceError",
     "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
-    "TextTokenizer", "TimeoutError_", "planner", "synthetic", "text",
+    "TextTokenizer", "TimeoutError_", "gemma2_document", "planner", "synthetic", "text",
 ]

@@ -18,6 +18,8 @@ reference's left / right padding does not change a text's result.
 """
 from __future__ import annotations
 
+import enum
+
 import threading
 from pathlib import Path
 from typing import Sequence
@@ -93,3 +95,42 @@ class TextTokenizer:
     def token_to_id(self, token: str) -> int | None:
         """The id of ``token`` if it is one vocabulary entry, else None."""
         return self._plain.token_to_id(token)
+
+
+class Gemma2Task(enum.Enum):
+    """EmbeddingGemma 2 prompt templates from the model card
+    (crates/inl-text/src/gemma2.rs:802-857). The prompts are caller-controlled:
+    ``TextEmbedder`` applies none on its own. Use ``apply`` to build the
+    prefixed text, or set ``TextOptions.query_prefix`` / ``passage_prefix`` to
+    ``Gemma2Task.<task>.prefix``."""
+    SEARCH_QUERY = "task: search result | query: {text}"
+    QUERY = "task: query | query: {text}"
+    QUESTION_ANSWERING = "task: question answering | query: {text}"
+    FACT_CHECKING = "task: fact checking | query: {text}"
+    CLASSIFICATION = "task: classification | query: {text}"
+    CLUSTERING = "task: clustering | query: {text}"
+    CODE_RETRIEVAL = "task: code retrieval | query: {text}"
+    DOCUMENT = "title: none | text: {text}"
+
+    @property
+    def template(self) -> str:
+        return self.value
+
+    @property
+    def prefix(self) -> str:
+        """The constant text the template puts before ``{text}``."""
+        return self.value[: -len("{text}")]
+
+    def apply(self, text: str) -> str:
+        return self.prefix + text
+
+    @property
+    def is_query(self) -> bool:
+        """Every task but DOCUMENT is query-side."""
+        return self is not Gemma2Task.DOCUMENT
+
+
+def gemma2_document(title: str, text: str) -> str:
+    """``title: {title} | text: {text}`` for a titled document
+    (crates/inl-text/src/gemma2.rs:859-862)."""
+    return f"title: {title} | text: {text}"

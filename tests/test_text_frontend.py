@@ -179,3 +179,33 @@ def test_data_parallel_embedder_takes_strings_and_checks_counts():
 
     with pytest.raises(inl.InferenceError):
         inl.DataParallelEmbedder([Dropping()]).embed([[1, 2], [3]])
+
+
+def test_gemma2_task_prefixes_match_the_model_card():
+    """crates/inl-text/src/gemma2.rs:1090-1122 restated."""
+    T = inl.Gemma2Task
+    assert T.SEARCH_QUERY.prefix == "task: search result | query: "
+    assert T.SEARCH_QUERY.apply("what causes the northern lights?") == \
+        "task: search result | query: what causes the northern lights?"
+    assert T.DOCUMENT.prefix == "title: none | text: "
+    assert T.DOCUMENT.apply("a passage") == "title: none | text: a passage"
+    assert inl.gemma2_document("Guide", "a passage") == "title: Guide | text: a passage"
+    assert T.SEARCH_QUERY.is_query and not T.DOCUMENT.is_query
+    for task in (T.QUERY, T.QUESTION_ANSWERING, T.FACT_CHECKING, T.CLASSIFICATION, T.CLUSTERING, T.CODE_RETRIEVAL):
+        assert task.prefix.startswith("task: ") and task.is_query
+        assert task.template == task.prefix + "{text}"
+
+
+def test_gemma2_task_prefix_through_the_embedder_options():
+    """A task prefix set as the query / passage prefix reaches the tokenizer
+    exactly as Gemma2Task.apply builds it."""
+    tok = _tok()
+    model = RecordingModel()
+    opts = inl.TextOptions(query_prefix=inl.Gemma2Task.SEARCH_QUERY.prefix,
+                           passage_prefix=inl.Gemma2Task.DOCUMENT.prefix)
+    e = inl.TextEmbedder(lambda: model, opts, tokenizer=tok)
+    e.embed_query("a b")
+    e.embed(["c d"])
+    want = tok.encode([inl.Gemma2Task.SEARCH_QUERY.apply("a b"), inl.Gemma2Task.DOCUMENT.apply("c d")],
+                      opts.max_length)
+    assert [list(s) for s in model.seen] == [w.tolist() for w in want]
