@@ -11,12 +11,14 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "../../include/inl_cuda.h"
 #include "../../include/inl_cuda_kernels.h"
+#include "checkpoint.h"
 #include "common.cuh"
 #include "model.h"
 
@@ -1684,9 +1686,20 @@ int inl_cuda_model_create(const char* config_json, const char* safetensors_path,
     inl_cuda_model_destroy(m);
     return fail(INL_ERR_CONFIG, "safetensors_path is NULL");
   }
-  MappedFile mf;
+  // One file, or every shard of a model.safetensors.index.json; a tensor
+  // named in two shards takes the later file's copy.
+  std::vector<std::string> files;
+  std::string error;
+  if (!inl::checkpoint_files(safetensors_path, &files, &error)) {
+    inl_cuda_model_destroy(m);
+    return fail(INL_ERR_INFERENCE, error);
+  }
+  std::vector<std::unique_ptr<MappedFile>> maps;
   TensorMap t;
-  r = read_safetensors(safetensors_path, mf, t);
+  for (const std::string& f : files) {
+    maps.push_back(std::make_unique<MappedFile>());
+    if ((r = read_safetensors(f.c_str(), *maps.back(), t))) break;
+  }
   if (!r) r = load_weights(m, t);
   if (r) {
     inl_cuda_model_destroy(m);

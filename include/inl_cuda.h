@@ -72,7 +72,10 @@ typedef struct inl_model_info {
 } inl_model_info;
 
 /* Load a model from an HF-style config.json text and a safetensors file
- * (f32 or bf16 tensors, checkpoint tensor names). Replaces the candle load in
+ * (f32 or bf16 tensors, checkpoint tensor names), or the
+ * model.safetensors.index.json of a sharded checkpoint: its weight_map's
+ * files, sorted and each once, are read from the index's directory
+ * (safetensors_weight_files, crates/inl-core/src/hub.rs:324-353). Replaces the candle load in
  * Qwen3Embedder::from_hf (crates/inl-text/src/qwen3/mod.rs:378-411),
  * ModernBertMlm::load (crates/inl-sparse/src/modernbert.rs:469-520) and
  * Gemma2Embedder::from_hf (crates/inl-text/src/gemma2.rs:671-700). */

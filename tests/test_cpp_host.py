@@ -3,6 +3,7 @@ with g++ and run on the CPU.
 
 * tests/cpp/test_engine.cpp: planning, BatchDeadline (timeout, then wedged),
   the error variants and the three engines over a test-double Backend.
+* tests/cpp/test_checkpoint.cpp: the shard list of a sharded checkpoint's index.
 * tests/cpp/backend_link.cpp: the CUDA backend links against libinl_cuda.so
   and a model load that cannot succeed here raises an InlError (no crash)."""
 import shutil
@@ -29,6 +30,15 @@ def test_host_layer_with_a_test_backend(tmp_path):
     exe = tmp_path / "test_engine"
     _run([GXX, *FLAGS, str(HOST / "engine.cpp"), str(ROOT / "tests" / "cpp" / "test_engine.cpp"), "-o", str(exe)])
     assert "all passed" in _run([str(exe)])
+
+
+def test_sharded_checkpoint_resolution(tmp_path):
+    """csrc/checkpoint.h: the files a model load reads for a .safetensors
+    path or a model.safetensors.index.json (crates/inl-core/src/hub.rs:324-353)."""
+    exe = tmp_path / "test_checkpoint"
+    _run([GXX, *FLAGS, f"-I{ROOT / 'im-not-llm_b200' / 'csrc'}", str(ROOT / "tests" / "cpp" / "test_checkpoint.cpp"),
+          "-o", str(exe)])
+    assert "all passed" in _run([str(exe), str(tmp_path)])
 
 
 def test_cuda_backend_links_and_a_failed_load_is_an_inl_error(tmp_path):
