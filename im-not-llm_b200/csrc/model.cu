@@ -658,7 +658,11 @@ int load_modernbert(inl_model* m, Loader& L) {
   const int gb = m->gated_split ? c.I : m->gate_block;
   const long long gstride = m->gated_split ? 0 : 2LL * gb;
   const long long up_off = m->gated_split ? c.I : gb;
-  if (c.d % 32 != 0) return fail(INL_ERR_CONFIG, "head_dim must be a multiple of 32");
+  // head_dim the RoPE kernel and the attention kernels of this dtype take
+  if (!(bf ? (c.d == 64 || c.d == 128 || c.d == 256)
+           : (c.d == 8 || c.d == 16 || c.d == 32 || c.d == 64 || c.d == 128 || c.d == 256)))
+    return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(c.d) + " is not supported by the CUDA tower in " +
+                                    (bf ? "bf16" : "f32"));
   const size_t es = bf ? 2 : 4;
   int r;
   if ((r = L.matrix("model.embeddings.tok_embeddings.weight", c.V, c.H, &m->embed, bf))) return r;
