@@ -7,10 +7,10 @@ from .model import CudaModel  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder, LateTask,  # noqa: F401
                      SparseEncoder, SparseVector, TextEmbedder, TextOptions)
 from .text import Gemma2Task, TextTokenizer, gemma2_document  # noqa: F401
-from . import planner, synthetic, text  # noqa: F401
+from . import loading, planner, synthetic, text  # noqa: F401
 
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "Gemma2Task", "InferenceError",
     "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
-    "TextTokenizer", "TimeoutError_", "gemma2_document", "planner", "synthetic", "text",
+    "TextTokenizer", "TimeoutError_", "gemma2_document", "loading", "planner", "synthetic", "text",
 ]

@@ -341,6 +341,24 @@ __global__ void rows_l2_kernel(const float* __restrict__ x, long long ldx, int r
   for (int c = lane; c < D; c += 32) out[row * ldo + c] = xr[c] * inv;
 }
 
+__global__ void bias_rows_l2_kernel(float* x, long long ldx, int rows, int D, const float* __restrict__ bias,
+                                    int normalize, float clamp_min) {
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float* xr = x + row * ldx;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) {
+    const float v = bias ? xr[c] + bias[c] : xr[c];
+    xr[c] = v;
+    ss += v * v;
+  }
+  const float inv = normalize ? 1.0f / fmaxf(sqrtf(warp_sum(ss)), clamp_min) : 1.0f;
+  if (normalize)
+    for (int c = lane; c < D; c += 32) xr[c] *= inv;
+}
+
 template <typename T>
 __global__ void segment_mean_kernel(const T* __restrict__ x, long long ldx, const int* __restrict__ cu, int n,
                                     int H, float* __restrict__ out) {
@@ -636,6 +654,13 @@ int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n,
     segment_mean_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, cu, n, H, out);
   else
     segment_mean_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, cu, n, H, out);
+  return ok(cudaGetLastError());
+}
+
+int bias_rows_l2_f32(float* x, long long ldx, int rows, int D, const float* bias, int normalize, float clamp_min,
+                     cudaStream_t s) {
+  if (rows <= 0) return 0;
+  bias_rows_l2_kernel<<<rows_grid(rows, 8), 256, 0, s>>>(x, ldx, rows, D, bias, normalize, clamp_min);
   return ok(cudaGetLastError());
 }
 

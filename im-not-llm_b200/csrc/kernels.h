@@ -174,6 +174,11 @@ int splade_finish(const int* pooled, int n, int V, const float* bias, float shif
 int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min, float* out, long long ldo,
                 cudaStream_t s);
 
+// In place over rows x D (row stride ldx): x += bias (if given), then, with
+// normalize, x /= max(||x||, clamp_min).
+int bias_rows_l2_f32(float* x, long long ldx, int rows, int D, const float* bias, int normalize, float clamp_min,
+                     cudaStream_t s);
+
 // Segment mean over packed rows: out[i] = mean_{t in text i} x[t] (f32 out) .
 int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, float* out,
                  cudaStream_t s);

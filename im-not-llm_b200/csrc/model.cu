@@ -1718,7 +1718,9 @@ int inl_cuda_model_set_dense_head(inl_model* m, const float* weight, int out_fea
   if (!m || !weight) return fail(INL_ERR_CONFIG, "NULL model or weight");
   if (in_features != m->c.H)
     return fail(INL_ERR_CONFIG, "Dense in_features must equal hidden_size (" + std::to_string(m->c.H) + ")");
-  if (out_features <= 0 || out_features % 8 != 0) return fail(INL_ERR_CONFIG, "Dense out_features must be a multiple of 8");
+  if (out_features <= 0) return fail(INL_ERR_CONFIG, "Dense out_features must be positive");
+  if (m->dtype == INL_DTYPE_BF16 && out_features % 8 != 0)  // the bf16 GEMM's output rows are 16-byte aligned
+    return fail(INL_ERR_CONFIG, "Dense out_features must be a multiple of 8 in bf16");
   INL_CUDA_TRY(cudaSetDevice(m->device), "cudaSetDevice");
   TensorMap t;
   TensorSrc w;
@@ -1737,6 +1739,12 @@ int inl_cuda_model_set_dense_head(inl_model* m, const float* weight, int out_fea
   m->proj_bias = nullptr;
   if (bias && (r = L.vec("linear.bias", out_features, &m->proj_bias))) return r;
   m->proj_out = out_features;
+  return INL_OK;
+}
+
+int inl_cuda_model_set_dense_normalize(inl_model* m, int normalize) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  m->proj_normalize = normalize != 0;
   return INL_OK;
 }
 
@@ -1859,11 +1867,18 @@ int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int ids_mem,
   INL_K_TRY(linear(m, m->xn.p, c.H, m->proj, b.T, m->proj_out, c.H, INL_EPI_F32, 0, m->out.p, m->proj_out, nullptr,
                    0, 4),
             "dense projection");
-  if (m->proj_bias) return fail(INL_ERR_CONFIG, "Dense bias is not supported yet");
-  INL_K_TRY(inl::rows_l2_f32(m->out.as<float>(), m->proj_out, b.T, m->proj_out, 1e-12f, m->out.as<float>(),
-                             m->proj_out, m->stream),
-            "normalize");
-  m->launches++;
+  if (m->proj_bias || !m->proj_normalize) {
+    // + bias, then F.normalize when the model has a Normalize module (native.rs:650-656)
+    INL_K_TRY(inl::bias_rows_l2_f32(m->out.as<float>(), m->proj_out, b.T, m->proj_out, m->proj_bias,
+                                    m->proj_normalize ? 1 : 0, 1e-12f, m->stream),
+              "bias / normalize");
+    m->launches++;
+  } else {
+    INL_K_TRY(inl::rows_l2_f32(m->out.as<float>(), m->proj_out, b.T, m->proj_out, 1e-12f, m->out.as<float>(),
+                               m->proj_out, m->stream),
+              "normalize");
+    m->launches++;
+  }
   return finish(m, m->out.p, bytes, out, out_mem);
 }
 

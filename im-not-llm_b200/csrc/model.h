@@ -161,6 +161,7 @@ struct inl_model {
   void* proj = nullptr;
   float* proj_bias = nullptr;
   int proj_out = 0;
+  bool proj_normalize = true;  // L2 after the projection (the Normalize module)
   // SPLADE / MLM head (ModernBERT)
   void* head_dense = nullptr;
   float* head_norm = nullptr;

@@ -23,6 +23,7 @@ reference's options. Token-id lists are truncated to ``max_length``.
 """
 from __future__ import annotations
 
+import dataclasses
 import json
 import threading
 import time
@@ -32,6 +33,7 @@ from typing import Callable, Sequence
 
 import numpy as np
 
+from . import loading
 from .errors import InlError
 from .model import CudaModel
 from .planner import assign_lpt, batch_cost, longest_first, pack, plan_packed
@@ -222,6 +224,16 @@ class _EngineBase:
 class TextEmbedder(_EngineBase):
     """DenseEngine over a CudaModel (Qwen3 last-token or Gemma-style mean pooling)."""
 
+    @classmethod
+    def from_model_dir(cls, model_dir: str | Path, options: TextOptions | None = None, device: int = 0,
+                       dtype: str | None = None) -> "TextEmbedder":
+        """A Qwen3 or EmbeddingGemma 2 model directory (config.json, weights,
+        tokenizer.json), loaded on first use; dtype defaults to bf16 for Qwen3
+        and f32 for EmbeddingGemma 2 (crates/inl-text/src/native.rs:406-470, 871-890)."""
+        spec = loading.dense_model(model_dir, dtype)
+        return cls(lambda: CudaModel(spec.config, spec.weights, device, spec.dtype), options or TextOptions(),
+                   tokenizer=TextTokenizer.from_file(spec.tokenizer))
+
     def load(self) -> EngineInfo:
         m = self._model().model
         info = m.info()
@@ -340,6 +352,38 @@ class LateEncoder(_EngineBase):
 
     TASKS = ("query", "document")
 
+    @classmethod
+    def from_model_dir(cls, model_dir: str | Path, options: TextOptions | None = None, device: int = 0,
+                       dtype: str = "f32", max_length: int | None = None) -> "LateEncoder":
+        """A Sentence-Transformers late-interaction directory (Transformer,
+        Dense, optional MultiVectorMask and Normalize modules), loaded on first
+        use: the tower, its Dense head (+ bias) and the Normalize flag; task
+        prompts, lengths and skiplist from the directory
+        (crates/inl-late/src/native.rs:455-620)."""
+        spec = loading.late_model(model_dir)
+        tok = TextTokenizer.from_file(spec.tokenizer)
+        tasks = LateTask.from_model_dir(model_dir, tok, max_length)
+
+        def load() -> CudaModel:
+            from safetensors.numpy import load_file
+
+            try:
+                dense = load_file(str(spec.dense_weights))
+            except Exception as e:
+                raise InlError.inference(f"native late model Dense weight load failed: {e}") from e
+            if "linear.weight" not in dense or (spec.dense_bias and "linear.bias" not in dense):
+                raise InlError.inference("native late model Dense weight load failed: linear.weight / linear.bias")
+            m = CudaModel(spec.config, spec.weights, device, dtype)
+            try:
+                m.set_dense_head(dense["linear.weight"], dense["linear.bias"] if spec.dense_bias else None,
+                                 normalize=spec.normalize)
+            except BaseException:
+                m.close()
+                raise
+            return m
+
+        return cls(load, options or TextOptions(), tokenizer=tok, tasks=tasks)
+
     def __init__(self, loader: Callable[[], CudaModel], options: TextOptions,
                  tokenizer: TextTokenizer | None = None, tasks: dict[str, LateTask] | None = None):
         super().__init__(loader, options, tokenizer)
@@ -403,6 +447,20 @@ class SparseVector:
 
 class SparseEncoder(_EngineBase):
     """SparseEngine over a ModernBERT + SPLADE CudaModel."""
+
+    @classmethod
+    def from_model_dir(cls, model_dir: str | Path, options: TextOptions | None = None, device: int = 0,
+                       dtype: str = "f32") -> "SparseEncoder":
+        """A Sentence-Transformers SPLADE directory (config.json, modules.json
+        and its SPLADE pooling module, weights, tokenizer.json), loaded on
+        first use; the context is capped by max_position_embeddings
+        (crates/inl-sparse/src/native.rs:245, 424-500)."""
+        spec = loading.sparse_model(model_dir)
+        opts = options or TextOptions.sparse()
+        if spec.positions and opts.max_length > spec.positions:
+            opts = dataclasses.replace(opts, max_length=spec.positions)
+        return cls(lambda: CudaModel(spec.config, spec.weights, device, dtype), opts,
+                   tokenizer=TextTokenizer.from_file(spec.tokenizer))
 
     def load(self) -> EngineInfo:
         m = self._model().model

@@ -71,11 +71,14 @@ class CudaModel:
         N.check(N.lib().inl_cuda_model_info(self.handle, ctypes.byref(i)), "model info")
         return {f: getattr(i, f) for f, _ in N.ModelInfo._fields_}
 
-    def set_dense_head(self, weight: np.ndarray, bias: np.ndarray | None = None) -> None:
+    def set_dense_head(self, weight: np.ndarray, bias: np.ndarray | None = None, normalize: bool = True) -> None:
+        """The late model's Dense projection [out, in] (+ bias); ``normalize``:
+        whether the model has a Normalize module after it."""
         w = np.ascontiguousarray(weight, dtype=np.float32)
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         N.check(N.lib().inl_cuda_model_set_dense_head(self.handle, w.ctypes.data, w.shape[0], w.shape[1],
                                                       None if b is None else b.ctypes.data), "Dense head")
+        N.check(N.lib().inl_cuda_model_set_dense_normalize(self.handle, 1 if normalize else 0), "Dense head")
 
     @property
     def stream(self) -> int:

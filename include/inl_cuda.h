@@ -91,10 +91,17 @@ INL_API int inl_cuda_model_create_from_tensors(const char* config_json, int n_te
 
 /* Attach the Sentence-Transformers Dense projection of a late-interaction
  * model: weight [out_features, in_features] f32 (linear.weight), optional
- * bias [out_features]. Replaces the Dense load of
+ * bias [out_features]. in_features is hidden_size; out_features is any
+ * positive width in f32, a multiple of 8 in bf16. Replaces the Dense load of
  * crates/inl-late/src/native.rs:546-567. */
 INL_API int inl_cuda_model_set_dense_head(inl_model* m, const float* weight, int out_features, int in_features,
                                   const float* bias);
+
+/* Whether forward_multivector L2-normalises each token vector after the Dense
+ * projection and bias, x / max(||x||, 1e-12) (1, the default), or returns the
+ * projection as it is (0): the late model's Normalize module is optional
+ * (crates/inl-late/src/native.rs:472-483, 650-656). */
+INL_API int inl_cuda_model_set_dense_normalize(inl_model* m, int normalize);
 
 /* Dense embeddings [n_texts, info.dense_dim] f32, unit length.
  * Qwen3: final RMSNorm of each text's last token, x / sqrt(sum x^2 + 1e-12)

@@ -91,3 +91,14 @@ def test_ple_checkpoint_without_ple_weights_fails_at_load(gpu, small_model):
     partial = {k: v for k, v in w.items() if not k.startswith("ple.")}
     with pytest.raises(inl.InferenceError, match="missing weight"):
         inl.CudaModel(cfg, partial, dtype="f32")
+
+
+def test_tiny_embeddinggemma2_from_the_model_dir(gpu):
+    """TextEmbedder.from_model_dir: architecture and dtype (f32) from the
+    directory, the fixture's tokenizer, the golden at max_length 64."""
+    golden = json.loads((GOLDEN / "golden.json").read_text())
+    case = next(c for c in golden["cases"] if c["max_length"] == 64)
+    emb = inl.TextEmbedder.from_model_dir(GOLDEN, inl.TextOptions(max_length=64))
+    for i, (got, want) in enumerate(zip(emb.embed(golden["texts"]), case["batched"])):
+        assert np.abs(np.asarray(got) - np.asarray(want, dtype=np.float32)).max() < TOLERANCE, i
+    emb.unload()

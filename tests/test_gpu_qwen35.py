@@ -50,3 +50,46 @@ def test_tiny_late_tower_matches_the_references_golden(gpu, batch_size, which):
             if got.size:
                 assert np.abs(got - want).max() < TOLERANCE, (case["task"], which, i)
     enc.unload()
+
+
+def test_dense_bias_and_a_model_without_normalize(gpu):
+    """The late head's optional pieces (crates/inl-late/src/native.rs:650-656):
+    a Dense bias, and no L2 when the model has no Normalize module; every
+    token vector, skiplist not applied, against oracle/qwen3_5.py."""
+    from safetensors.numpy import load_file
+
+    from oracle import qwen3_5 as Q35
+
+    cfg = json.loads((LATE / "config.json").read_text())
+    weights = load_file(str(LATE / "model.safetensors"))
+    dense = load_file(str(LATE / "1_Dense" / "model.safetensors"))["linear.weight"]
+    bias = (np.random.default_rng(4).standard_normal(dense.shape[0]) * 0.1).astype(np.float32)
+    tok = inl.TextTokenizer.from_file(LATE / "tokenizer.json")
+    rows = tok.encode_untruncated(["a short text", "and a second, somewhat longer one"])
+    ids = np.concatenate(rows)
+    cu = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    m = inl.CudaModel(cfg, str(LATE / "model.safetensors"), dtype="f32")
+    try:
+        for normalize in (True, False):
+            m.set_dense_head(dense, bias, normalize=normalize)
+            got = m.encode_multivector(ids, cu)
+            want = np.concatenate([Q35.late_vectors(weights, cfg, dense, bias, r, normalize=normalize) for r in rows])
+            assert got.shape == want.shape
+            assert np.abs(got - want).max() < TOLERANCE * max(1.0, float(np.abs(want).max()))
+    finally:
+        m.close()
+
+
+def test_tiny_late_tower_from_the_model_dir(gpu):
+    """The same golden through LateEncoder.from_model_dir: modules, Dense,
+    Normalize, prompts, lengths and skiplist read from the directory."""
+    golden = json.loads((LATE / "golden.json").read_text())
+    enc = inl.LateEncoder.from_model_dir(LATE)
+    for case in golden["cases"]:
+        out = enc.encode(golden["texts"], task=case["task"])
+        for i, (got, want) in enumerate(zip(out, case["batched"])):
+            want = np.asarray(want, dtype=np.float32).reshape(len(want), -1)
+            assert got.shape == want.shape, (case["task"], i)
+            if got.size:
+                assert np.abs(got - want).max() < TOLERANCE, (case["task"], i)
+    enc.unload()
