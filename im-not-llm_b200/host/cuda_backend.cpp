@@ -73,7 +73,8 @@ class CudaBackend : public Backend {
 
 std::unique_ptr<Backend> cuda_backend(const std::string& config_json, const std::string& safetensors_path, int device,
                                       const std::string& dtype, const std::vector<float>& dense_head_weight,
-                                      int dense_out, int dense_in) {
+                                      int dense_out, int dense_in, const std::vector<float>& dense_head_bias,
+                                      bool dense_normalize) {
   if (dtype != "bf16" && dtype != "f32") throw ConfigError("dtype must be bf16 or f32");
   inl_model* m = nullptr;
   check(inl_cuda_model_create(config_json.c_str(), safetensors_path.c_str(), device,
@@ -83,7 +84,12 @@ std::unique_ptr<Backend> cuda_backend(const std::string& config_json, const std:
   if (!dense_head_weight.empty()) {
     if (static_cast<size_t>(dense_out) * dense_in != dense_head_weight.size())
       throw ConfigError("Dense head weight has the wrong size");
-    check(inl_cuda_model_set_dense_head(m, dense_head_weight.data(), dense_out, dense_in, nullptr), "Dense head");
+    if (!dense_head_bias.empty() && dense_head_bias.size() != static_cast<size_t>(dense_out))
+      throw ConfigError("Dense head bias has the wrong size");
+    check(inl_cuda_model_set_dense_head(m, dense_head_weight.data(), dense_out, dense_in,
+                                        dense_head_bias.empty() ? nullptr : dense_head_bias.data()),
+          "Dense head");
+    check(inl_cuda_model_set_dense_normalize(m, dense_normalize ? 1 : 0), "Dense head");
   }
   return backend;
 }

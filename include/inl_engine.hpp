@@ -121,11 +121,14 @@ class Backend {
   virtual std::vector<float> multivector(const Packed& batch) = 0;
 };
 
-// The model on a GPU through include/inl_cuda.h; dtype "bf16" or "f32".
-// dense_head_weight ([out, in] f32, may be empty) is attached for late models.
+// The model on a GPU through include/inl_cuda.h; dtype "bf16" or "f32";
+// safetensors_path is one file or a sharded checkpoint's index.json. For late
+// models, dense_head_weight ([out, in] f32, may be empty), its optional bias
+// [out] and whether the model has a Normalize module after the Dense.
 std::unique_ptr<Backend> cuda_backend(const std::string& config_json, const std::string& safetensors_path, int device,
                                       const std::string& dtype, const std::vector<float>& dense_head_weight = {},
-                                      int dense_out = 0, int dense_in = 0);
+                                      int dense_out = 0, int dense_in = 0,
+                                      const std::vector<float>& dense_head_bias = {}, bool dense_normalize = true);
 
 // ------------------------------------------------------------------ engines
 struct EngineInfo {  // crates/inl-core/src/engine.rs:10-26
