@@ -5,12 +5,12 @@ from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  
                      TimeoutError_)
 from .model import CudaModel  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder, LateTask,  # noqa: F401
-                     SparseEncoder, SparseVector, TextEmbedder, TextOptions)
+                     SparseEncoder, SparseVector, TextEmbedder, TextIdentity, TextOptions)
 from .text import Gemma2Task, TextTokenizer, gemma2_document  # noqa: F401
 from . import loading, planner, synthetic, text  # noqa: F401
 
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "Gemma2Task", "InferenceError",
-    "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextOptions",
+    "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextIdentity", "TextOptions",
     "TextTokenizer", "TimeoutError_", "gemma2_document", "loading", "planner", "synthetic", "text",
 ]

@@ -105,6 +105,17 @@ class EngineInfo:
     modalities: list = field(default_factory=lambda: ["text"])
 
 
+@dataclass(frozen=True)
+class TextIdentity:
+    """The embedding space of a TextEmbedder (crates/inl-text/src/native.rs:156-167):
+    model id, output dimension, resolved dtype, device kind, context."""
+    id: str
+    dimension: int
+    dtype: str
+    device: str
+    max_length: int
+
+
 @dataclass
 class TextOptions:
     """Subset of TextOptions (crates/inl-text/src/native.rs:172-287) that the
@@ -235,10 +246,17 @@ class TextEmbedder(_EngineBase):
                    tokenizer=TextTokenizer.from_file(spec.tokenizer))
 
     def load(self) -> EngineInfo:
+        """Loads the model; a requested output_dim the model cannot give is a
+        config error here, as at the reference's load (native.rs:438-440)."""
         m = self._model().model
-        info = m.info()
-        dim = self.options.output_dim or info["dense_dim"]
+        dim = self._output_dim(m) or m.info()["dense_dim"]
         return EngineInfo(self.options.id, dim, m.dtype, f"cuda:{m.device}", "fused", self.options.max_length)
+
+    def identity(self) -> "TextIdentity":
+        """The embedding space this embedder produces; loads the model
+        (crates/inl-text/src/native.rs:476-488)."""
+        info = self.load()
+        return TextIdentity(self.options.id, info.dimension, info.dtype, "cuda", self.options.max_length)
 
     def _output_dim(self, model: CudaModel) -> int:
         """resolve_output_dim (crates/inl-text/src/native.rs:793-817)."""
@@ -395,6 +413,11 @@ class LateEncoder(_EngineBase):
         return EngineInfo(self.options.id, m.info()["multivector_dim"], m.dtype, f"cuda:{m.device}", "fused",
                           self.tasks["document"].length)
 
+    def identity(self) -> EngineInfo:
+        """The token-vector space; loads the model; max_length is the
+        document context (crates/inl-late/src/native.rs:256-270)."""
+        return self.load()
+
     def encode(self, inputs: Sequence, task: str = "document") -> list[np.ndarray]:
         setup = self.tasks.get(task)
         if setup is None:
@@ -466,6 +489,10 @@ class SparseEncoder(_EngineBase):
         m = self._model().model
         return EngineInfo(self.options.id, m.info()["sparse_dim"], m.dtype, f"cuda:{m.device}", "fused",
                           self.options.max_length)
+
+    def identity(self) -> EngineInfo:
+        """The sparse space; loads the model (crates/inl-sparse/src/native.rs:271-283)."""
+        return self.load()
 
     def encode(self, inputs: Sequence) -> list[SparseVector]:
         """Documents (strings get the passage marker) or token-id lists."""

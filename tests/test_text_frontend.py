@@ -209,3 +209,17 @@ def test_gemma2_task_prefix_through_the_embedder_options():
     want = tok.encode([inl.Gemma2Task.SEARCH_QUERY.apply("a b"), inl.Gemma2Task.DOCUMENT.apply("c d")],
                       opts.max_length)
     assert [list(s) for s in model.seen] == [w.tolist() for w in want]
+
+
+def test_identity_and_output_dim_checked_at_load():
+    """identity (crates/inl-text/src/native.rs:476-488; sparse :271-283, late
+    :256-270) loads the model; an output_dim the model cannot give is a config
+    error at load (native.rs:438-440)."""
+    model = RecordingModel()
+    e = inl.TextEmbedder(lambda: model, inl.TextOptions(id="m", max_length=9))
+    ident = e.identity()
+    assert (ident.id, ident.dimension, ident.dtype, ident.device, ident.max_length) == ("m", 2, "bf16", "cuda", 9)
+    with pytest.raises(inl.ConfigError, match="only supported for EmbeddingGemma 2"):
+        inl.TextEmbedder(lambda: RecordingModel(), inl.TextOptions(output_dim=128)).load()
+    s = inl.SparseEncoder(lambda: RecordingModel(), inl.TextOptions.sparse(id="s"))
+    assert s.identity().dimension == 4 and s.is_loaded()
