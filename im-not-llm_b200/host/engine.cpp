@@ -223,16 +223,34 @@ EngineInfo info_of(const Options& o, int dim, const ModelInfo& mi, size_t max_le
 }
 }  // namespace
 
+// resolve_output_dim (crates/inl-text/src/native.rs:793-817): Matryoshka
+// output only for EmbeddingGemma-style models (arch 2), at their trained
+// sizes, never wider than the model's embeddings. 0 = the model's own width.
+static int resolve_output_dim(const std::optional<int>& requested, const ModelInfo& mi) {
+  if (!requested) return 0;
+  const int dim = *requested;
+  if (mi.arch != 2) throw ConfigError("output_dim is only supported for EmbeddingGemma 2 models");
+  if (dim != 128 && dim != 256 && dim != 512 && dim != 768)
+    throw ConfigError("output_dim " + std::to_string(dim) +
+                      " is not supported by EmbeddingGemma 2: use one of [128, 256, 512, 768]");
+  if (dim > mi.dense_dim)
+    throw ConfigError("output_dim " + std::to_string(dim) + " exceeds the model's " + std::to_string(mi.dense_dim) +
+                      "-dimensional embeddings");
+  return dim;
+}
+
 EngineInfo TextEmbedder::load() {
   const ModelInfo mi = model()->backend->info();
-  return info_of(options_, options_.output_dim ? *options_.output_dim : mi.dense_dim, mi, options_.max_length);
+  const int out_dim = resolve_output_dim(options_.output_dim, mi);
+  return info_of(options_, out_dim ? out_dim : mi.dense_dim, mi, options_.max_length);
 }
 
 std::vector<std::vector<float>> TextEmbedder::embed(const Tokens& texts) {
   const Tokens t = truncate(texts, options_.max_length);
   if (t.empty()) return {};
-  const int out_dim = options_.output_dim ? *options_.output_dim : 0;
-  const int dim = out_dim ? out_dim : model()->backend->info().dense_dim;
+  const ModelInfo mi = model()->backend->info();
+  const int out_dim = resolve_output_dim(options_.output_dim, mi);
+  const int dim = out_dim ? out_dim : mi.dense_dim;
   return run_batches<std::vector<float>>(
       "native embedding", t, [out_dim, dim](Backend& b, const Packed& p) {
         const std::vector<float> flat = b.dense(p, out_dim);

@@ -41,10 +41,12 @@ struct Fake : Backend {
   std::atomic<int>* calls;
   double delay = 0;
   bool drop = false, nan = false;
+  int arch = 0, dense_dim = 4;
   explicit Fake(std::atomic<int>* c) : calls(c) {}
   ModelInfo info() override {
     ModelInfo m;
-    m.dense_dim = 4;
+    m.arch = arch;
+    m.dense_dim = dense_dim;
     m.sparse_dim = 5;
     m.multivector_dim = 2;
     return m;
@@ -141,6 +143,18 @@ int main() {
     CHECK(e2.embed(texts_of({10}))[0][0] == 4.f);
     TextEmbedder e3([&] { auto f = std::make_unique<Fake>(&calls); f->drop = true; return f; }, Options{});
     CHECK(throws<InferenceError>([&] { e3.embed(texts_of({2, 3})); }));
+    // output_dim: EmbeddingGemma-style models only, trained sizes, not wider than the model
+    Options o4;
+    o4.output_dim = 128;
+    TextEmbedder e4([&] { return std::make_unique<Fake>(&calls); }, o4);
+    CHECK(throws<ConfigError>([&] { e4.load(); }));
+    CHECK(throws<ConfigError>([&] { e4.embed(texts_of({2})); }));
+    TextEmbedder e5([&] { auto f = std::make_unique<Fake>(&calls); f->arch = 2; f->dense_dim = 768; return f; }, o4);
+    CHECK(e5.load().dimension == 128);
+    Options o6;
+    o6.output_dim = 300;
+    TextEmbedder e6([&] { auto f = std::make_unique<Fake>(&calls); f->arch = 2; f->dense_dim = 768; return f; }, o6);
+    CHECK(throws<ConfigError>([&] { e6.load(); }));
   }
 
   // ---------------- deadline: a stuck forward times out, later calls fail fast
