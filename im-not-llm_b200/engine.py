@@ -156,6 +156,17 @@ class _Loaded:
         self.gate = threading.Lock()
 
 
+def _check_encoder_options(options: TextOptions) -> None:
+    """The sparse and late encoders refuse these options when they are built
+    (crates/inl-sparse/src/native.rs:197-210, crates/inl-late/src/native.rs:184-197)."""
+    s = options.per_batch_timeout_seconds if options.per_batch_timeout_seconds is not None else options.timeout_seconds
+    if not s or s <= 0:
+        raise InlError.config("timeout_seconds / per_batch_timeout_seconds must be greater than 0 for the native "
+                              "encoder")
+    if options.batch_size <= 0:
+        raise InlError.config("batch_size must be greater than 0")
+
+
 class _EngineBase:
     def __init__(self, loader: Callable[[], CudaModel], options: TextOptions,
                  tokenizer: TextTokenizer | None = None):
@@ -213,6 +224,8 @@ class _EngineBase:
     def _run_batches(self, what: str, texts: list[np.ndarray], forward) -> list:
         if not texts:
             return []
+        if self.options.batch_size <= 0:  # crates/inl-text/src/native.rs:552-556
+            raise InlError.inference("batch_size must be greater than 0")
         self.deadline.ensure_healthy(what)
         loaded = self._model()
         budget = self.options.batch_timeout()
@@ -404,6 +417,9 @@ class LateEncoder(_EngineBase):
 
     def __init__(self, loader: Callable[[], CudaModel], options: TextOptions,
                  tokenizer: TextTokenizer | None = None, tasks: dict[str, LateTask] | None = None):
+        _check_encoder_options(options)
+        if options.max_length <= 0:  # crates/inl-late/src/native.rs:198-202
+            raise InlError.config("max_length must be greater than 0")
         super().__init__(loader, options, tokenizer)
         default = LateTask(length=options.max_length)
         self.tasks = {name: (tasks or {}).get(name, default) for name in self.TASKS}
@@ -470,6 +486,10 @@ class SparseVector:
 
 class SparseEncoder(_EngineBase):
     """SparseEngine over a ModernBERT + SPLADE CudaModel."""
+
+    def __init__(self, loader: Callable[[], CudaModel], options: TextOptions, tokenizer: TextTokenizer | None = None):
+        _check_encoder_options(options)
+        super().__init__(loader, options, tokenizer)
 
     @classmethod
     def from_model_dir(cls, model_dir: str | Path, options: TextOptions | None = None, device: int = 0,

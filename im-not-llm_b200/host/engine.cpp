@@ -174,6 +174,8 @@ template <typename R>
 std::vector<R> EngineBase::run_batches(const std::string& what, const Tokens& texts,
                                        std::function<std::vector<R>(Backend&, const Packed&)> forward) {
   if (texts.empty()) return {};
+  if (options_.batch_size == 0)  // crates/inl-text/src/native.rs:552-556
+    throw InferenceError("batch_size must be greater than 0");
   deadline_.ensure_healthy(what);
   std::shared_ptr<Loaded> loaded = model();
   const double budget = options_.batch_timeout();
@@ -262,6 +264,20 @@ std::vector<std::vector<float>> TextEmbedder::embed(const Tokens& texts) {
       });
 }
 
+namespace {
+// The sparse and late encoders refuse these options when they are built.
+void check_encoder_options(const Options& o) {
+  const double s = o.per_batch_timeout_seconds ? *o.per_batch_timeout_seconds : o.timeout_seconds;
+  if (!(s > 0))
+    throw ConfigError("timeout_seconds / per_batch_timeout_seconds must be greater than 0 for the native encoder");
+  if (o.batch_size == 0) throw ConfigError("batch_size must be greater than 0");
+}
+}  // namespace
+
+SparseEncoder::SparseEncoder(Loader loader, Options options) : EngineBase(std::move(loader), std::move(options)) {
+  check_encoder_options(options_);
+}
+
 EngineInfo SparseEncoder::load() {
   const ModelInfo mi = model()->backend->info();
   return info_of(options_, mi.sparse_dim, mi, options_.max_length);
@@ -283,7 +299,10 @@ std::vector<SparseVector> SparseEncoder::encode(const Tokens& texts) {
 }
 
 LateEncoder::LateEncoder(Loader loader, Options options, LateTask query, LateTask document)
-    : EngineBase(std::move(loader), std::move(options)), query_(std::move(query)), document_(std::move(document)) {}
+    : EngineBase(std::move(loader), std::move(options)), query_(std::move(query)), document_(std::move(document)) {
+  check_encoder_options(options_);
+  if (query_.length == 0 || document_.length == 0) throw ConfigError("max_length must be greater than 0");
+}
 
 EngineInfo LateEncoder::load() {
   const ModelInfo mi = model()->backend->info();

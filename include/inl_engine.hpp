@@ -199,10 +199,11 @@ class TextEmbedder : public EngineBase {
   std::vector<std::vector<float>> embed(const Tokens& texts);
 };
 
-// SparseEngine (crates/inl-sparse/src/lib.rs:236-252).
+// SparseEngine (crates/inl-sparse/src/lib.rs:236-252). Construction refuses
+// a zero timeout or batch_size with a ConfigError (native.rs:197-210).
 class SparseEncoder : public EngineBase {
  public:
-  using EngineBase::EngineBase;
+  SparseEncoder(Loader loader, Options options);
   EngineInfo load();
   std::vector<SparseVector> encode(const Tokens& texts);
 };
@@ -215,6 +216,8 @@ struct LateTask {
 };
 
 // LateEngine (crates/inl-late/src/lib.rs:38-55): one vector per kept token.
+// Construction refuses a zero timeout, batch_size or task length with a
+// ConfigError (native.rs:184-202).
 class LateEncoder : public EngineBase {
  public:
   LateEncoder(Loader loader, Options options, LateTask query = {}, LateTask document = {});

@@ -155,6 +155,21 @@ int main() {
     o6.output_dim = 300;
     TextEmbedder e6([&] { auto f = std::make_unique<Fake>(&calls); f->arch = 2; f->dense_dim = 768; return f; }, o6);
     CHECK(throws<ConfigError>([&] { e6.load(); }));
+    // batch_size 0: an inference error when embedding; sparse / late refuse it when built
+    Options z;
+    z.batch_size = 0;
+    TextEmbedder e7([&] { return std::make_unique<Fake>(&calls); }, z);
+    CHECK(e7.embed({}).empty());
+    CHECK(throws<InferenceError>([&] { e7.embed(texts_of({2})); }));
+    CHECK(throws<ConfigError>([&] { SparseEncoder s([&] { return std::make_unique<Fake>(&calls); }, z); }));
+    CHECK(throws<ConfigError>([&] { LateEncoder l([&] { return std::make_unique<Fake>(&calls); }, z); }));
+    Options t0;
+    t0.timeout_seconds = 0;
+    CHECK(throws<ConfigError>([&] { SparseEncoder s([&] { return std::make_unique<Fake>(&calls); }, t0); }));
+    LateTask empty_task;
+    empty_task.length = 0;
+    CHECK(throws<ConfigError>(
+        [&] { LateEncoder l([&] { return std::make_unique<Fake>(&calls); }, Options{}, empty_task); }));
   }
 
   // ---------------- deadline: a stuck forward times out, later calls fail fast

@@ -223,3 +223,21 @@ def test_identity_and_output_dim_checked_at_load():
         inl.TextEmbedder(lambda: RecordingModel(), inl.TextOptions(output_dim=128)).load()
     s = inl.SparseEncoder(lambda: RecordingModel(), inl.TextOptions.sparse(id="s"))
     assert s.identity().dimension == 4 and s.is_loaded()
+
+
+def test_option_refusals_of_the_three_engines():
+    """batch_size 0: an inference error when the dense engine embeds
+    (crates/inl-text/src/native.rs:552-556); a config error when a sparse or
+    late encoder is built, as are a zero timeout and late max_length 0
+    (crates/inl-sparse/src/native.rs:197-210, crates/inl-late/src/native.rs:184-202)."""
+    e = inl.TextEmbedder(lambda: RecordingModel(), inl.TextOptions(batch_size=0))
+    assert e.embed([]) == []
+    with pytest.raises(inl.InferenceError, match="batch_size must be greater than 0"):
+        e.embed([[1, 2]])
+    for bad in (dict(batch_size=0), dict(timeout_seconds=0), dict(per_batch_timeout_seconds=0)):
+        with pytest.raises(inl.ConfigError):
+            inl.SparseEncoder(lambda: RecordingModel(), inl.TextOptions.sparse(**bad))
+        with pytest.raises(inl.ConfigError):
+            inl.LateEncoder(lambda: RecordingModel(), inl.TextOptions(**bad))
+    with pytest.raises(inl.ConfigError, match="max_length"):
+        inl.LateEncoder(lambda: RecordingModel(), inl.TextOptions(max_length=0))
