@@ -461,14 +461,62 @@ class LateEncoder(_EngineBase):
 
 
 class SparseVector:
-    """Sorted term ids with positive weights (SparseVector::from_pairs,
-    crates/inl-sparse/src/lib.rs:51-62: pairs with weight <= 0 are dropped)."""
+    """Term ids strictly ascending, every weight finite and > 0 (a zero weight
+    is the absence of a term): SparseVector, crates/inl-sparse/src/lib.rs:13-90."""
 
     __slots__ = ("indices", "values")
 
     def __init__(self, indices: np.ndarray, values: np.ndarray):
         self.indices = indices
         self.values = values
+
+    @classmethod
+    def new(cls, indices, values) -> "SparseVector":
+        """Validate and wrap parallel indices / values (lib.rs:24-46)."""
+        idx = np.asarray(indices, dtype=np.uint32)
+        val = np.asarray(values, dtype=np.float32)
+        if idx.shape != val.shape or idx.ndim != 1:
+            raise InlError.inference(f"sparse vector has {idx.size} indices but {val.size} values")
+        bad = np.nonzero(idx[1:] <= idx[:-1])[0]
+        if bad.size:
+            raise InlError.inference(f"sparse vector indices must be strictly ascending (saw {idx[bad[0]]} then "
+                                     f"{idx[bad[0] + 1]})")
+        wrong = np.nonzero(~(np.isfinite(val) & (val > 0)))[0]
+        if wrong.size:
+            raise InlError.inference(f"sparse vector weights must be finite and positive (saw {val[wrong[0]]})")
+        return cls(idx, val)
+
+    @classmethod
+    def from_pairs(cls, pairs) -> "SparseVector":
+        """Sort by index, keep the largest weight of a repeated index, drop
+        weights that are not finite and positive; never fails (lib.rs:48-62)."""
+        best: dict[int, float] = {}
+        for i, w in pairs:
+            w = float(np.float32(w))
+            if np.isfinite(w) and w > 0 and w > best.get(int(i), 0.0):
+                best[int(i)] = w
+        keys = sorted(best)
+        return cls(np.asarray(keys, dtype=np.uint32), np.asarray([best[k] for k in keys], dtype=np.float32))
+
+    def is_empty(self) -> bool:
+        return len(self.indices) == 0
+
+    def __eq__(self, other) -> bool:
+        return (isinstance(other, SparseVector) and np.array_equal(self.indices, other.indices)
+                and np.array_equal(self.values, other.values))
+
+    def to_json(self) -> str:
+        """{"indices": [...], "values": [...]} (the serde form of lib.rs:18)."""
+        return json.dumps({"indices": [int(i) for i in self.indices], "values": [float(v) for v in self.values]})
+
+    @classmethod
+    def from_json(cls, text: str) -> "SparseVector":
+        """Parses and re-validates (lib.rs:92-110)."""
+        try:
+            d = json.loads(text)
+            return cls.new(d["indices"], d["values"])
+        except (ValueError, KeyError, TypeError) as e:
+            raise InlError.inference(f"sparse vector JSON is invalid: {e}") from e
 
     @classmethod
     def from_dense(cls, row: np.ndarray) -> "SparseVector":

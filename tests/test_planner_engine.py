@@ -240,3 +240,26 @@ def test_data_parallel_embedder_gathers_by_index():
     for t, v in zip(texts, out):
         assert v[0] == len(t) and v[1] == t[0]
     assert all(m.calls > 0 for m in models)
+
+
+def test_sparse_vector_contract():
+    """crates/inl-sparse/src/lib.rs:258-318 restated: new validates, from_pairs
+    sorts / merges by max / drops unusable weights, dot sums shared terms, the
+    JSON form round-trips and re-validates."""
+    SV = inl.SparseVector
+    v = SV.new([1, 4, 9], [0.5, 2.0, 0.25])
+    assert v.indices.tolist() == [1, 4, 9] and v.values.tolist() == [0.5, 2.0, 0.25]
+    assert len(v) == 3 and not v.is_empty()
+    for idx, val in [([1, 2], [1.0]), ([2, 1], [1.0, 1.0]), ([1, 1], [1.0, 1.0]), ([1], [0.0]), ([1], [-0.5]),
+                     ([1], [float("nan")]), ([1], [float("inf")])]:
+        with pytest.raises(inl.InferenceError):
+            SV.new(idx, val)
+    p = SV.from_pairs([(7, 1.0), (3, 0.5), (7, 2.5), (5, 0.0), (6, -1.0), (8, float("nan"))])
+    assert p.indices.tolist() == [3, 7] and p.values.tolist() == [0.5, 2.5]
+    left, right = SV.new([1, 3, 5], [2.0, 1.0, 4.0]), SV.new([3, 4, 5], [10.0, 7.0, 0.5])
+    assert left.dot(right) == 1.0 * 10.0 + 4.0 * 0.5 == right.dot(left)
+    assert left.dot(SV.from_pairs([])) == 0.0
+    w = SV.new([2, 9], [1.5, 0.5])
+    assert SV.from_json(w.to_json()) == w
+    with pytest.raises(inl.InferenceError):
+        SV.from_json('{"indices":[2,1],"values":[1.0,1.0]}')
