@@ -434,15 +434,29 @@ class LateEncoder(_EngineBase):
         document context (crates/inl-late/src/native.rs:256-270)."""
         return self.load()
 
-    def encode(self, inputs: Sequence, task: str = "document") -> list[np.ndarray]:
+    def _setup(self, task: str) -> LateTask:
         setup = self.tasks.get(task)
         if setup is None:
             raise InlError.invalid_input(f"unknown late task {task!r}: use 'query' or 'document'")
+        return setup
+
+    def _rows(self, inputs: Sequence, setup: LateTask) -> list[np.ndarray]:
+        """Strings: the task's prompt in front, tokenized, cut at the task's
+        length (native.rs:292-305); token-id lists: cut at the task's length."""
         items = list(inputs)
         if self._is_text(items):
-            rows = [ids[:setup.length] for ids in self.tokenizer.encode_untruncated([setup.prompt + t for t in items])]
-        else:
-            rows = _truncate(items, setup.length)
+            return [ids[:setup.length] for ids in self.tokenizer.encode_untruncated([setup.prompt + t for t in items])]
+        return _truncate(items, setup.length)
+
+    def token_counts(self, inputs: Sequence, task: str = "document") -> list[int]:
+        """Tokens the model sees per input for ``task``: prompt included,
+        after the task's truncation (LateEngine::token_counts,
+        crates/inl-late/src/lib.rs:44-46, native.rs:727-735)."""
+        return [len(r) for r in self._rows(inputs, self._setup(task))]
+
+    def encode(self, inputs: Sequence, task: str = "document") -> list[np.ndarray]:
+        setup = self._setup(task)
+        rows = self._rows(inputs, setup)
         skip = np.fromiter(sorted(setup.skip), dtype=np.uint32) if setup.skip else None
 
         def forward(model: CudaModel, ids, cu):

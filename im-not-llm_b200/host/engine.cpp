@@ -309,9 +309,22 @@ EngineInfo LateEncoder::load() {
   return info_of(options_, mi.multivector_dim, mi, document_.length);
 }
 
+const LateTask& LateEncoder::setup(const std::string& task) const {
+  if (task == "query") return query_;
+  if (task == "document") return document_;
+  throw InvalidInputError("unknown late task '" + task + "': use 'query' or 'document'");
+}
+
+std::vector<size_t> LateEncoder::token_counts(const Tokens& texts, const std::string& task) const {
+  const size_t length = setup(task).length;
+  std::vector<size_t> out;
+  out.reserve(texts.size());
+  for (const auto& t : texts) out.push_back(std::min(t.size(), length));
+  return out;
+}
+
 std::vector<std::vector<std::vector<float>>> LateEncoder::encode(const Tokens& texts, const std::string& task) {
-  const LateTask* setup = task == "query" ? &query_ : (task == "document" ? &document_ : nullptr);
-  if (!setup) throw InvalidInputError("unknown late task '" + task + "': use 'query' or 'document'");
+  const LateTask* setup = &this->setup(task);
   const Tokens t = truncate(texts, setup->length);
   if (t.empty()) return {};
   const size_t D = static_cast<size_t>(model()->backend->info().multivector_dim);

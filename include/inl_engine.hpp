@@ -224,8 +224,12 @@ class LateEncoder : public EngineBase {
   EngineInfo load();
   // task: "query" or "document"
   std::vector<std::vector<std::vector<float>>> encode(const Tokens& texts, const std::string& task = "document");
+  // Tokens the model sees per input for `task`, after the task's cut
+  // (LateEngine::token_counts, crates/inl-late/src/lib.rs:44-46).
+  std::vector<size_t> token_counts(const Tokens& texts, const std::string& task = "document") const;
 
  private:
+  const LateTask& setup(const std::string& task) const;
   LateTask query_, document_;
 };
 

@@ -218,6 +218,9 @@ int main() {
     CHECK(qry[0].size() == 7);
     CHECK(throws<InvalidInputError>([&] { l.encode(t, "passage"); }));
     CHECK(l.load().max_length == 5 && l.load().dimension == 2);
+    CHECK((l.token_counts(texts_of({7, 3}), "document") == std::vector<size_t>{5, 3}));
+    CHECK((l.token_counts(texts_of({7, 3}), "query") == std::vector<size_t>{7, 3}));
+    CHECK(throws<InvalidInputError>([&] { l.token_counts(t, "passage"); }));
   }
 
   std::printf("all passed\n");

@@ -83,3 +83,15 @@ def test_late_encoder_keeps_the_references_vectors_per_task():
     # token-id lists: cut at the task's length, skiplist applied
     ids = np.array([5] * 30, dtype=np.uint32)
     assert len(enc.encode([ids], task="query")[0]) == 24
+
+
+def test_late_token_counts_per_task_match_the_references_lengths():
+    """LateEngine::token_counts(texts, task) (crates/inl-late/src/lib.rs:44-46):
+    prompt included, after the task's cut; the golden's recorded lengths."""
+    tok, tasks, golden = _setup()
+    enc = inl.LateEncoder(lambda: TokenEchoModel(), inl.TextOptions(), tokenizer=tok, tasks=tasks)
+    for case in golden["cases"]:
+        assert enc.token_counts(golden["texts"], task=case["task"]) == case["lengths"], case["task"]
+    assert not enc.is_loaded()
+    with pytest.raises(inl.InvalidInputError):
+        enc.token_counts(["x"], task="passage")
