@@ -36,6 +36,8 @@ METRIC = "embedded tokens/sec (Qwen3-0.6B arch, bf16)"
 BATCH_TOKENS = 65536
 N_TEXTS = 65536
 CPU_SAMPLE_TOKENS = 2048  # tokens of one CPU-baseline step
+REF_TIME_BUDGET_S = 150.0  # CPU seconds the reference arm's timed steps may take together
+REF_MIN_SAMPLE_TOKENS = 256
 
 
 def _peaks():
@@ -197,11 +199,15 @@ def run_reference(args, world, rank):
     cfg = dict(inl.synthetic.QWEN3_0_6B)
     weights = inl.synthetic.qwen3_weights(cfg, seed=0)
     texts, _, lengths = corpus_batches()
-    for w in range(args.warmup):
-        cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=512, seed=100 + w)
+    # The warm-up samples (at least one) also measure this host's rate; each
+    # timed step's sample is then sized so all steps fit REF_TIME_BUDGET_S.
+    rate = 0.0
+    for w in range(max(args.warmup, 1)):
+        rate = cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=512, seed=100 + w)[0]
+    per_step = int(np.clip(rate * REF_TIME_BUDGET_S / max(args.steps, 1), REF_MIN_SAMPLE_TOKENS, CPU_SAMPLE_TOKENS))
     rates, toks, secs = [], 0, 0.0
     for s in range(args.steps):
-        r, n, _, dt = cpu_reference_rate(weights, cfg, texts, lengths, seed=s)
+        r, n, _, dt = cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=per_step, seed=s)
         rates.append(r)
         toks += n
         secs += dt
@@ -213,7 +219,9 @@ def run_reference(args, world, rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "cfg5 corpus, bounded CPU sample per step", "sample_tokens_per_step": toks // max(args.steps, 1)},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} samples of ~{CPU_SAMPLE_TOKENS} tokens of the cfg5 corpus, numpy f32 restatement of crates/inl-text/src/qwen3/mod.rs with BLAS on {cores} threads"},
+                         "sample": f"{args.steps} samples of ~{per_step} tokens of the cfg5 corpus (sized from the "
+                                   f"warm-up rate to fit {REF_TIME_BUDGET_S:.0f} s), numpy f32 restatement of "
+                                   f"crates/inl-text/src/qwen3/mod.rs with BLAS on {cores} threads"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
