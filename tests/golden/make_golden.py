@@ -8,7 +8,8 @@ checkpoint plus the golden outputs the reference's tests assert against.
   * tiny_splade            crates/inl-sparse/tests/fixtures/tiny_splade/
                            (ModernBERT MLM + ShiftedTopKSpladePooling; asserted by
                            crates/inl-sparse/src/modernbert.rs:1034-1057, |dw| <= 1e-4,
-                           identical term sets)
+                           identical term sets). Directory layout kept, as
+                           the loader follows modules.json.
   * tiny_embeddinggemma2   crates/inl-text/tests/fixtures/tiny_embeddinggemma2/
                            (EmbeddingGemma 2 text tower; asserted by
                            crates/inl-text/src/gemma2.rs:941-967, |d| < 2e-5)
@@ -28,15 +29,16 @@ HERE = Path(__file__).resolve().parent
 FIXTURES = {
     "tiny_splade": ("crates/inl-sparse/tests/fixtures/tiny_splade",
                     ["config.json", "model.safetensors", "golden.json", "1_ShiftedTopKSpladePooling/config.json",
-                     "tokenizer.json"]),
+                     "tokenizer.json", "modules.json", "config_sentence_transformers.json"]),
     "tiny_embeddinggemma2": ("crates/inl-text/tests/fixtures/tiny_embeddinggemma2",
                              ["config.json", "model.safetensors", "golden.json", "tokenizer.json"]),
     "tiny_qwen3_5_late": ("crates/inl-late/tests/fixtures/tiny_qwen3_5_late",
                           ["config.json", "config_sentence_transformers.json", "sentence_bert_config.json",
                            "modules.json", "2_MultiVectorMask/config.json", "tokenizer.json", "golden.json",
-                           "model.safetensors", "1_Dense/config.json", "1_Dense/model.safetensors"]),
+                           "model.safetensors", "1_Dense/config.json", "1_Dense/model.safetensors",
+                           "3_Normalize/config.json"]),
 }
-KEEP_DIRS = {"tiny_qwen3_5_late"}
+KEEP_DIRS = {"tiny_qwen3_5_late", "tiny_splade"}
 
 
 def main(ref_root: str) -> None:

@@ -27,7 +27,7 @@ pytestmark = [pytest.mark.gpu,
 
 def _config():
     cfg = json.loads((GOLDEN / "config.json").read_text())
-    cfg["splade"] = json.loads((GOLDEN / "1_ShiftedTopKSpladePooling__config.json").read_text())
+    cfg["splade"] = json.loads((GOLDEN / "1_ShiftedTopKSpladePooling" / "config.json").read_text())
     return cfg
 
 
@@ -76,3 +76,16 @@ def test_tiny_splade_through_the_sparse_encoder(gpu, batch_size, which):
         for i, (v, want) in enumerate(zip(out, case[which])):
             _assert_term_weights(v.indices, v.values, want, f'{case["kind"]}/{case["max_length"]} {which}[{i}]')
     model.close()
+
+
+def test_tiny_splade_from_the_model_dir(gpu):
+    """SparseEncoder.from_model_dir on the fixture as the reference lays it
+    out: modules.json names the pooling module, the markers are the
+    defaults, the context is capped at max_position_embeddings (64)."""
+    golden = json.loads((GOLDEN / "golden.json").read_text())
+    case = next(c for c in golden["cases"] if c["kind"] == "document" and c["max_length"] == 64)
+    enc = inl.SparseEncoder.from_model_dir(GOLDEN)
+    assert enc.options.max_length == 64
+    for i, (v, want) in enumerate(zip(enc.encode(case["texts"]), case["batched"])):
+        _assert_term_weights(v.indices, v.values, want, f"from_model_dir[{i}]")
+    enc.unload()

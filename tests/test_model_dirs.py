@@ -1,8 +1,8 @@
 """Model directories read as the reference's native engines read them
 (im-not-llm_b200/loading.py and the engines' from_model_dir), on the CPU: the
 lazy loader is called with a stand-in CudaModel that records what it would
-load. Fixtures are the reference's tiny checkpoints (tests/golden/), laid out
-as model directories where the copy flattened them."""
+load. Fixtures are the reference's tiny checkpoints (tests/golden/), in the
+reference's directory layout."""
 import json
 import shutil
 from pathlib import Path
@@ -40,16 +40,8 @@ def recording(monkeypatch):
 
 
 def _splade_dir(tmp_path):
-    src = GOLDEN / "tiny_splade"
     d = tmp_path / "splade"
-    (d / "1_ShiftedTopKSpladePooling").mkdir(parents=True)
-    for name in ("config.json", "model.safetensors", "tokenizer.json"):
-        shutil.copy(src / name, d / name)
-    shutil.copy(src / "1_ShiftedTopKSpladePooling__config.json", d / "1_ShiftedTopKSpladePooling" / "config.json")
-    (d / "modules.json").write_text(json.dumps([
-        {"idx": 0, "name": "0", "path": "", "type": "sentence_transformers.models.MLMTransformer"},
-        {"idx": 1, "name": "1", "path": "1_ShiftedTopKSpladePooling",
-         "type": "kure.ShiftedTopKSpladePooling"}]))
+    shutil.copytree(GOLDEN / "tiny_splade", d)
     return d
 
 
@@ -92,7 +84,7 @@ def test_sparse_dir_reads_the_pooling_module_and_caps_the_context(tmp_path, reco
     assert e.options.query_prefix == "[Q] " and e.options.passage_prefix == "[D] "
     assert e.options.max_length == 64  # max_position_embeddings of the fixture
     m = e._model().model
-    pooling = json.loads((GOLDEN / "tiny_splade" / "1_ShiftedTopKSpladePooling__config.json").read_text())
+    pooling = json.loads((GOLDEN / "tiny_splade" / "1_ShiftedTopKSpladePooling" / "config.json").read_text())
     assert m.config["splade"] == pooling and m.dtype == "f32"
     (d / "modules.json").write_text(json.dumps([{"path": "", "type": "x.Transformer"}]))
     with pytest.raises(inl.InferenceError, match="no SPLADE pooling module"):

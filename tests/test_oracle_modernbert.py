@@ -19,7 +19,7 @@ def load_tiny_splade():
     from safetensors.numpy import load_file
 
     cfg = json.loads((GOLDEN / "config.json").read_text())
-    pooling = json.loads((GOLDEN / "1_ShiftedTopKSpladePooling__config.json").read_text())
+    pooling = json.loads((GOLDEN / "1_ShiftedTopKSpladePooling" / "config.json").read_text())
     weights = load_file(str(GOLDEN / "model.safetensors"))
     golden = json.loads((GOLDEN / "golden.json").read_text())
     return cfg, pooling, weights, golden
