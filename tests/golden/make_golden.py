@@ -1,7 +1,9 @@
 """Copy the reference's own golden fixtures for the encoder path into
 tests/golden/, so that the parity tests run where the reference tree is absent.
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
+
+REFERENCE_ROOT is the root of a checkout of the reference repository.
 
 Copied as-is (no regeneration): each fixture is a tiny random Hugging Face
 checkpoint plus the golden outputs the reference's tests assert against.
@@ -53,4 +55,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_ROOT")
+    main(sys.argv[1])
