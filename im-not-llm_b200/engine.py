@@ -14,7 +14,8 @@
   batches, ``SparseVector`` results (positive weights only, sorted term ids),
   non-finite output is an error.
 * ``DataParallelEmbedder`` — one model per GPU, one host thread per GPU,
-  packed batches assigned longest-processing-time first; no collective.
+  packed batches assigned longest-processing-time first; no collective;
+  dense ``embed``, ``encode_sparse`` and ``encode_late``.
 
 Inputs are strings or token-id lists. Strings go through the model's
 tokenizer.json (``text.TextTokenizer``, the reference's settings: special
@@ -612,9 +613,11 @@ class SparseEncoder(_EngineBase):
 
 
 class DataParallelEmbedder:
-    """Dense embedding over several GPUs: one CudaModel replica and one host
-    thread per device, batches assigned longest-processing-time first, no
-    collective; results gathered on the host by input index."""
+    """Dense, sparse or late encoding over several GPUs: one CudaModel replica
+    and one host thread per device, batches assigned longest-processing-time
+    first, no collective; results gathered on the host by input index. The
+    per-batch checks are those of the single-GPU engines (result count,
+    finite sparse and late outputs)."""
 
     def __init__(self, models: Sequence[CudaModel], max_batch_tokens: int = DEFAULT_PACKED_TOKENS,
                  tokenizer: TextTokenizer | None = None, max_length: int = DEFAULT_MAX_LENGTH,
@@ -625,9 +628,9 @@ class DataParallelEmbedder:
         self.max_length = max_length
         self.passage_prefix = passage_prefix
 
-    def embed(self, inputs: Sequence) -> list[np.ndarray]:
-        """Strings (passage prefix, tokenized and truncated by the tokenizer)
-        or token-id lists (truncated to max_length)."""
+    def _texts(self, inputs: Sequence, prefix: str | None, max_length: int, cut_after: bool = False) -> list:
+        """Strings (prefix, tokenized and truncated by the tokenizer, or cut
+        after tokenizing for the late tasks) or token-id lists (truncated)."""
         items = list(inputs)
         kinds = {isinstance(x, str) for x in items}
         if len(kinds) > 1:
@@ -635,9 +638,13 @@ class DataParallelEmbedder:
         if kinds == {True}:
             if self.tokenizer is None:
                 raise InlError.config("string inputs need a tokenizer (tokenizer=TextTokenizer.from_file(...))")
-            texts = self.tokenizer.encode([(self.passage_prefix or "") + t for t in items], self.max_length)
-        else:
-            texts = _truncate(items, self.max_length)
+            prefixed = [(prefix or "") + t for t in items]
+            if cut_after:
+                return [ids[:max_length] for ids in self.tokenizer.encode_untruncated(prefixed)]
+            return self.tokenizer.encode(prefixed, max_length)
+        return _truncate(items, max_length)
+
+    def _run(self, what: str, texts: list, forward) -> list:
         lengths = [len(t) for t in texts]
         order = longest_first(lengths)
         batches = [[order[k] for k in r] for r in plan_packed([lengths[i] for i in order], self.max_batch_tokens)]
@@ -651,10 +658,9 @@ class DataParallelEmbedder:
             try:
                 for b in plan[w]:
                     ids, cu = pack(texts, batches[b])
-                    out = self.models[w].embed(ids, cu)
+                    out = forward(self.models[w], ids, cu)
                     if len(out) != len(batches[b]):  # crates/inl-text/src/native.rs:674-679
-                        raise InlError.inference(f"native embedding returned {len(out)} results for "
-                                                 f"{len(batches[b])} inputs")
+                        raise InlError.inference(f"{what} returned {len(out)} results for {len(batches[b])} inputs")
                     for i, v in zip(batches[b], out):
                         results[i] = v
             except BaseException as e:
@@ -668,3 +674,44 @@ class DataParallelEmbedder:
         if errors:
             raise errors[0]
         return results
+
+    def embed(self, inputs: Sequence) -> list[np.ndarray]:
+        """Dense unit vectors, one per input."""
+        texts = self._texts(inputs, self.passage_prefix, self.max_length)
+        return self._run("native embedding", texts, lambda m, ids, cu: m.embed(ids, cu))
+
+    def encode_sparse(self, inputs: Sequence) -> list[SparseVector]:
+        """SPLADE vectors, one per input (passage_prefix is the "[D] " marker
+        for sparse models); non-finite weights are an error
+        (crates/inl-sparse/src/native.rs:536-540)."""
+        texts = self._texts(inputs, self.passage_prefix, self.max_length)
+
+        def forward(m, ids, cu):
+            dense = m.encode_sparse(ids, cu)
+            if not np.all(np.isfinite(dense)):
+                raise InlError.inference("native sparse encoder produced non-finite weights")
+            return [SparseVector.from_dense(row) for row in dense]
+
+        return self._run("native sparse", texts, forward)
+
+    def encode_late(self, inputs: Sequence, task: LateTask | None = None) -> list[np.ndarray]:
+        """Per-token vectors for one late task: its prompt in front, the ids
+        cut at its length, its skiplist tokens' vectors dropped; non-finite
+        values are an error (crates/inl-late/src/native.rs:631-683)."""
+        setup = task or LateTask(length=self.max_length)
+        texts = self._texts(inputs, setup.prompt, setup.length, cut_after=True)
+        skip = np.fromiter(sorted(setup.skip), dtype=np.uint32) if setup.skip else None
+
+        def forward(m, ids, cu):
+            flat = m.encode_multivector(ids, cu)
+            out = []
+            for i in range(len(cu) - 1):
+                v = flat[cu[i]:cu[i + 1]]
+                if skip is not None:
+                    v = v[~np.isin(ids[cu[i]:cu[i + 1]], skip)]
+                if not np.all(np.isfinite(v)):
+                    raise InlError.inference("native late encoder produced non-finite values")
+                out.append(v)
+            return out
+
+        return self._run("native late", texts, forward)

@@ -263,3 +263,50 @@ def test_sparse_vector_contract():
     assert SV.from_json(w.to_json()) == w
     with pytest.raises(inl.InferenceError):
         SV.from_json('{"indices":[2,1],"values":[1.0,1.0]}')
+
+
+class _EchoReplica:
+    """A GPU replica stand-in: sparse row = one-hot of (length % 4), late
+    vectors = (token id, position); optional NaN output."""
+
+    def __init__(self, nan=False):
+        self.calls, self.nan = 0, nan
+
+    def info(self):
+        return {"is_causal": 0}
+
+    def encode_sparse(self, ids, cu):
+        self.calls += 1
+        out = np.zeros((len(cu) - 1, 4), dtype=np.float32)
+        for i in range(len(cu) - 1):
+            out[i, (cu[i + 1] - cu[i]) % 4] = np.nan if self.nan else 1.0 + i * 0
+        return out
+
+    def encode_multivector(self, ids, cu):
+        self.calls += 1
+        out = np.zeros((len(ids), 2), dtype=np.float32)
+        out[:, 0] = ids
+        for i in range(len(cu) - 1):
+            out[cu[i]:cu[i + 1], 1] = np.arange(cu[i + 1] - cu[i])
+        if self.nan:
+            out[0, 0] = np.nan
+        return out
+
+
+def test_data_parallel_sparse_and_late_gather_by_index():
+    reps = [_EchoReplica(), _EchoReplica(), _EchoReplica()]
+    dp = inl.DataParallelEmbedder(reps, max_batch_tokens=30, max_length=50)
+    texts = _texts(40, seed=5)
+    sv = dp.encode_sparse(texts)
+    for t, v in zip(texts, sv):
+        assert v.indices.tolist() == [len(t) % 4] and v.values.tolist() == [1.0]
+    task = inl.LateTask(length=6, skip=frozenset({3}))
+    late = dp.encode_late(texts, task)
+    for t, v in zip(texts, late):
+        kept = [x for x in list(t)[:6] if x != 3]
+        assert v[:, 0].tolist() == kept
+    assert all(r.calls > 0 for r in reps)
+    with pytest.raises(inl.InferenceError, match="non-finite"):
+        inl.DataParallelEmbedder([_EchoReplica(nan=True)]).encode_sparse([[1, 2]])
+    with pytest.raises(inl.InferenceError, match="non-finite"):
+        inl.DataParallelEmbedder([_EchoReplica(nan=True)]).encode_late([[1, 2]])
