@@ -171,7 +171,8 @@ INL_API int inl_cuda_gated_delta_rule(const float* mixed, int64_t ld_mixed, cons
 
 /* Measurement hooks: with profiling on, every GEMM and attention launch of
  * the model is bracketed by CUDA events on the model's stream. kind: 0 qkv,
- * 1 o, 2 gate/up, 3 down, 4 Dense head, -1 all GEMMs; 100 attention (flops
+ * 1 o, 2 gate/up, 3 down, 4 Dense head, 5 SPLADE head dense, 6 SPLADE
+ * decoder, 7 per-layer-embedding GEMMs, -1 all GEMMs; 100 attention (flops
  * reported as 0). The reference has no counterpart (its profiling was
  * external, nsys). */
 INL_API int inl_cuda_model_set_profiling(inl_model* m, int enable);
