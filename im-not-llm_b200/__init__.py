@@ -3,7 +3,7 @@ embedding engines on sm_100a, behind a C ABI (libinl_cuda.so) and a Python
 host layer that mirrors the reference's engine API."""
 from .errors import (ConfigError, InferenceError, InlError, InvalidInputError,  # noqa: F401
                      TimeoutError_)
-from .model import CudaModel  # noqa: F401
+from .model import CudaModel, config_check  # noqa: F401
 from .engine import (BatchDeadline, DataParallelEmbedder, EngineInfo, LateEncoder, LateTask,  # noqa: F401
                      SparseEncoder, SparseVector, TextEmbedder, TextIdentity, TextOptions)
 from .text import Gemma2Task, TextTokenizer, gemma2_document  # noqa: F401
@@ -12,5 +12,5 @@ from . import loading, planner, synthetic, text  # noqa: F401
 __all__ = [
     "BatchDeadline", "ConfigError", "CudaModel", "DataParallelEmbedder", "EngineInfo", "Gemma2Task", "InferenceError",
     "InlError", "InvalidInputError", "LateEncoder", "LateTask", "SparseEncoder", "SparseVector", "TextEmbedder", "TextIdentity", "TextOptions",
-    "TextTokenizer", "TimeoutError_", "gemma2_document", "loading", "planner", "synthetic", "text",
+    "TextTokenizer", "TimeoutError_", "config_check", "gemma2_document", "loading", "planner", "synthetic", "text",
 ]

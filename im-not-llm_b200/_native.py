@@ -33,7 +33,7 @@ EXPORTED = (
     "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
     "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2", "inl_cuda_gemm_bf16_ex",
     "inl_cuda_attention_noalloc", "inl_cuda_causal_conv_silu", "inl_cuda_gated_delta_rule",
-    "inl_cuda_model_set_dense_normalize",
+    "inl_cuda_model_set_dense_normalize", "inl_cuda_config_check",
 )
 
 
@@ -74,6 +74,7 @@ def _declare(lib: ctypes.CDLL) -> None:
             c_int, [c_char_p, c_int, P(c_char_p), P(c_void_p), P(c_i64), c_int, c_int, P(c_void_p)]),
         "inl_cuda_model_set_dense_head": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
         "inl_cuda_model_set_dense_normalize": (c_int, [c_void_p, c_int]),
+        "inl_cuda_config_check": (c_int, [c_char_p, c_int, c_void_p]),
         "inl_cuda_forward_dense": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int]),
         "inl_cuda_forward_multivector": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),
         "inl_cuda_forward_sparse": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),

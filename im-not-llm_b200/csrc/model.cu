@@ -478,6 +478,27 @@ int build_rope(inl_model* m, double theta, float** cos_out, float** sin_out, flo
   return INL_OK;
 }
 
+// Shapes and dtypes the CUDA towers take, checked before any weight is read:
+// the head_dim the RoPE and attention kernels of the dtype support, and the
+// Qwen3.5 tower's f32.
+bool head_dim_supported(int d, int bf16) {
+  return bf16 ? (d == 64 || d == 128 || d == 256) : (d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256);
+}
+
+int shape_support(const ModelConfig& c, int dtype) {
+  const int bf = dtype == INL_DTYPE_BF16;
+  if (c.arch == inl::ARCH_QWEN35 && bf) return fail(INL_ERR_CONFIG, "the Qwen3.5 tower runs in f32");
+  if (c.arch == inl::ARCH_MODERNBERT && !head_dim_supported(c.d, bf))
+    return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(c.d) + " is not supported by the CUDA tower in " +
+                                    (bf ? "bf16" : "f32"));
+  if (c.arch == inl::ARCH_GEMMA)
+    for (int l = 0; l < c.layers; ++l)
+      if (!head_dim_supported(c.dl(l), bf))
+        return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(c.dl(l)) + " of layer " + std::to_string(l) +
+                                        " is not supported by the CUDA tower in " + (bf ? "bf16" : "f32"));
+  return INL_OK;
+}
+
 // Qwen3 weights (crates/inl-text/src/qwen3/mod.rs:180-330 tensor names).
 int load_qwen3(inl_model* m, Loader& L) {
   const ModelConfig& c = m->c;
@@ -581,7 +602,7 @@ int build_rope_f32(inl_model* m, double theta, int rot) {
 // Qwen3.5 text tower (crates/inl-late/src/qwen3_5.rs:816-891 tensor names), f32.
 int load_qwen35(inl_model* m, Loader& L) {
   const ModelConfig& c = m->c;
-  if (m->dtype != INL_DTYPE_F32) return fail(INL_ERR_CONFIG, "the Qwen3.5 tower runs in f32");
+  if (int e = shape_support(c, m->dtype)) return e;
   const int nk = c.lin_nk, nv = c.lin_nv, dk = c.lin_dk, dv = c.lin_dv;
   const int conv_dim = 2 * nk * dk + nv * dv;
   const int lin_rows = conv_dim + nv * dv + 2 * nv;
@@ -658,13 +679,9 @@ int load_modernbert(inl_model* m, Loader& L) {
   const int gb = m->gated_split ? c.I : m->gate_block;
   const long long gstride = m->gated_split ? 0 : 2LL * gb;
   const long long up_off = m->gated_split ? c.I : gb;
-  // head_dim the RoPE kernel and the attention kernels of this dtype take
-  if (!(bf ? (c.d == 64 || c.d == 128 || c.d == 256)
-           : (c.d == 8 || c.d == 16 || c.d == 32 || c.d == 64 || c.d == 128 || c.d == 256)))
-    return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(c.d) + " is not supported by the CUDA tower in " +
-                                    (bf ? "bf16" : "f32"));
-  const size_t es = bf ? 2 : 4;
   int r;
+  if ((r = shape_support(c, m->dtype))) return r;
+  const size_t es = bf ? 2 : 4;
   if ((r = L.matrix("model.embeddings.tok_embeddings.weight", c.V, c.H, &m->embed, bf))) return r;
   if ((r = L.vec("model.embeddings.norm.weight", c.H, &m->emb_norm))) return r;
   m->layers.resize(c.layers);
@@ -718,19 +735,12 @@ int load_gemma(inl_model* m, Loader& L) {
   const int gb = m->gated_split ? c.I : m->gate_block;
   const long long gstride = m->gated_split ? 0 : 2LL * gb;
   const long long up_off = m->gated_split ? c.I : gb;
-  for (int l = 0; l < c.layers; ++l) {
-    // head_dim the q/k norm + RoPE kernel and the attention kernels of this dtype take
-    const int d = c.dl(l);
-    const bool ok = bf ? (d == 64 || d == 128 || d == 256) : (d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256);
-    if (!ok)
-      return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(d) + " of layer " + std::to_string(l) +
-                                      " is not supported by the CUDA tower in " + (bf ? "bf16" : "f32"));
-  }
+  int r;
+  if ((r = shape_support(c, m->dtype))) return r;
   const bool ple = c.ple > 0;
   if (!ple && L.has("ple.per_layer_model_projection.weight"))
     return fail(INL_ERR_CONFIG, "checkpoint has per-layer embeddings but hidden_size_per_layer_input is 0");
   const size_t es = bf ? 2 : 4;
-  int r;
   if ((r = L.matrix("embed_tokens.weight", c.V, c.H, &m->embed, bf))) return r;
   if (ple) {  // PleBlock inputs (gemma2.rs:549-560, 626-630)
     if ((r = L.matrix("ple.per_layer_model_projection.weight", c.layers * c.ple, c.H, &m->ple_model_proj, bf))) return r;
@@ -1983,6 +1993,31 @@ int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
   out->sparse_dim = m->sparse_dim;
   out->max_text_tokens = m->c.max_pos;
   out->is_causal = m->c.causal ? 1 : 0;
+  return INL_OK;
+}
+
+int inl_cuda_config_check(const char* config_json, int dtype, inl_model_info* out) {
+  if (!config_json || !out) return fail(INL_ERR_CONFIG, "NULL argument");
+  if (dtype != INL_DTYPE_F32 && dtype != INL_DTYPE_BF16) return fail(INL_ERR_CONFIG, "unknown dtype");
+  ModelConfig c;
+  int r = parse_config(config_json, c);
+  if (r) return r;
+  if (c.H % 8 != 0) return fail(INL_ERR_CONFIG, "hidden_size must be a multiple of 8");
+  if ((r = shape_support(c, dtype))) return r;
+  *out = inl_model_info{};
+  out->arch = c.arch;
+  out->dtype = dtype;
+  out->device = -1;
+  out->hidden_size = c.H;
+  out->num_layers = c.layers;
+  out->vocab_size = c.V;
+  out->dense_dim = (c.arch == inl::ARCH_GEMMA && !c.dense_dims.empty()) ? c.dense_dims.back() : c.H;
+  out->multivector_dim = 0;
+  out->sparse_dim = c.arch != inl::ARCH_MODERNBERT ? 0
+                    : c.canonical_ids.empty() ? c.V
+                                              : *std::max_element(c.canonical_ids.begin(), c.canonical_ids.end()) + 1;
+  out->max_text_tokens = c.max_pos;
+  out->is_causal = c.causal ? 1 : 0;
   return INL_OK;
 }
 

@@ -35,6 +35,17 @@ def _ptr(a) -> tuple[int, int]:
     raise TypeError(f"expected a numpy array or a device pointer, got {type(a).__name__}")
 
 
+def config_check(config: dict, dtype: str = "bf16") -> dict:
+    """Parse and validate ``config`` (a config.json dict; the SPLADE pooling
+    block under "splade") for ``dtype`` without a GPU or weights, as a model
+    load would before reading any weight. Returns the model's info fields
+    (device -1, multivector_dim 0); a refused config raises its InlError."""
+    i = N.ModelInfo()
+    N.check(N.lib().inl_cuda_config_check(json.dumps(config).encode(), _dtype_code(dtype), ctypes.byref(i)),
+            "config")
+    return {f: getattr(i, f) for f, _ in N.ModelInfo._fields_}
+
+
 class CudaModel:
     """A model resident on ``cuda:device``."""
 

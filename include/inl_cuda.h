@@ -89,6 +89,14 @@ INL_API int inl_cuda_model_create_from_tensors(const char* config_json, int n_te
                                        const float* const* data, const int64_t* numels, int device, int dtype,
                                        inl_model** out);
 
+/* Parse and validate a config.json text for `dtype` without a device or
+ * weights: the checks inl_cuda_model_create makes before loading (the
+ * reference's Config::parse / validate of each tower, the SPLADE pooling
+ * block, the shapes the CUDA towers take in that dtype). On success `out`
+ * describes the model as inl_cuda_model_info would, with device -1 and
+ * multivector_dim 0. */
+INL_API int inl_cuda_config_check(const char* config_json, int dtype, inl_model_info* out);
+
 /* Attach the Sentence-Transformers Dense projection of a late-interaction
  * model: weight [out_features, in_features] f32 (linear.weight), optional
  * bias [out_features]. in_features is hidden_size; out_features is any
