@@ -19,6 +19,18 @@ void check(int status, const std::string& what) {
   if (status != INL_OK) throw_status(status, what + ": " + last_error());
 }
 
+ModelInfo to_info(const inl_model_info& i) {
+  ModelInfo o;
+  o.arch = i.arch;
+  o.hidden = i.hidden_size;
+  o.dense_dim = i.dense_dim;
+  o.sparse_dim = i.sparse_dim;
+  o.multivector_dim = i.multivector_dim;
+  o.dtype = i.dtype == INL_DTYPE_BF16 ? "bf16" : "f32";
+  o.device = i.device;
+  return o;
+}
+
 class CudaBackend : public Backend {
  public:
   explicit CudaBackend(inl_model* m) : m_(m) {}
@@ -29,15 +41,7 @@ class CudaBackend : public Backend {
   ModelInfo info() override {
     inl_model_info i{};
     check(inl_cuda_model_info(m_, &i), "model info");
-    ModelInfo o;
-    o.arch = i.arch;
-    o.hidden = i.hidden_size;
-    o.dense_dim = i.dense_dim;
-    o.sparse_dim = i.sparse_dim;
-    o.multivector_dim = i.multivector_dim;
-    o.dtype = i.dtype == INL_DTYPE_BF16 ? "bf16" : "f32";
-    o.device = i.device;
-    return o;
+    return to_info(i);
   }
 
   std::vector<float> dense(const Packed& b, int out_dim) override {
@@ -70,6 +74,13 @@ class CudaBackend : public Backend {
 };
 
 }  // namespace
+
+ModelInfo check_config(const std::string& config_json, const std::string& dtype) {
+  if (dtype != "bf16" && dtype != "f32") throw ConfigError("dtype must be bf16 or f32");
+  inl_model_info i{};
+  check(inl_cuda_config_check(config_json.c_str(), dtype == "bf16" ? INL_DTYPE_BF16 : INL_DTYPE_F32, &i), "config");
+  return to_info(i);
+}
 
 std::unique_ptr<Backend> cuda_backend(const std::string& config_json, const std::string& safetensors_path, int device,
                                       const std::string& dtype, const std::vector<float>& dense_head_weight,

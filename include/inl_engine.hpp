@@ -121,6 +121,11 @@ class Backend {
   virtual std::vector<float> multivector(const Packed& batch) = 0;
 };
 
+// Parses and validates a config.json text for dtype "bf16" or "f32" without a
+// device (inl_cuda_config_check): the ModelInfo a load would report (device -1,
+// multivector_dim 0), or the InlError a load would raise before reading weights.
+ModelInfo check_config(const std::string& config_json, const std::string& dtype);
+
 // The model on a GPU through include/inl_cuda.h; dtype "bf16" or "f32";
 // safetensors_path is one file or a sharded checkpoint's index.json. For late
 // models, dense_head_weight ([out, in] f32, may be empty), its optional bias
