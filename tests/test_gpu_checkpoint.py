@@ -45,3 +45,18 @@ def test_sharded_checkpoint_loads_like_the_single_file(gpu, tmp_path):
     (tmp_path / "broken.index.json").write_text(json.dumps({"metadata": {}}))
     with pytest.raises(inl.InferenceError, match="weight_map"):
         inl.CudaModel(cfg, str(tmp_path / "broken.index.json"), dtype="f32")
+
+
+def test_config_check_agrees_with_a_loaded_model(gpu):
+    """inl_cuda_config_check reports what inl_cuda_model_info reports after
+    the load (but the device and the late Dense width)."""
+    cfg = json.loads((GOLDEN / "config.json").read_text())
+    want = inl.config_check(cfg, "f32")
+    m = inl.CudaModel(cfg, str(GOLDEN / "model.safetensors"), dtype="f32")
+    try:
+        got = m.info()
+    finally:
+        m.close()
+    for key in ("arch", "dtype", "hidden_size", "num_layers", "vocab_size", "dense_dim", "sparse_dim",
+                "max_text_tokens", "is_causal"):
+        assert got[key] == want[key], key
