@@ -130,3 +130,14 @@ def test_malformed_configs():
             inl.config_check(bad, "f32")
     with pytest.raises(inl.ConfigError):
         inl.config_check(inl.synthetic.QWEN3_TINY, "f16")
+
+
+def test_null_arguments_are_config_errors():
+    import ctypes
+
+    from im_not_llm_b200 import _native as N
+
+    info = N.ModelInfo()
+    assert N.lib().inl_cuda_config_check(None, N.INL_DTYPE_F32, ctypes.byref(info)) == 1  # INL_ERR_CONFIG
+    assert N.lib().inl_cuda_config_check(b"{}", N.INL_DTYPE_F32, None) == 1  # INL_ERR_CONFIG
+    assert N.lib().inl_cuda_config_check(b"not json", N.INL_DTYPE_F32, ctypes.byref(info)) == 1  # INL_ERR_CONFIG
