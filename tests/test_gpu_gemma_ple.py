@@ -3,9 +3,9 @@ embeddings (PLE), layer scalars and per_layer_config head shapes
 (crates/inl-text/src/gemma2.rs:78-662).
 
 * The reference's tiny_embeddinggemma2 golden through the TextEmbedder facade
-  and the fixture's tokenizer, f32: every vector within 2e-5, batched and one
-  text per forward, at max_length 64 and 9 (the assertion of
-  crates/inl-text/src/gemma2.rs:941-967). Its head_dim 16 (sliding) and 32
+  and the fixture's tokenizer, f32: cosine > 0.99999 per vector (the
+  reference's own bound for its GPU run, gemma2.rs:1057-1072) and 1e-4 per
+  component, batched and one text per forward, at max_length 64 and 9. Its head_dim 16 (sliding) and 32
   (full) run on the narrow q/k norm + RoPE kernel and the f32 attention.
 * A synthetic EmbeddingGemma 2 (head_dim 128 sliding, 256 full with one KV
   head, PLE 64) against oracle/gemma.py in f32 and bf16; in bf16 the two head
@@ -23,7 +23,12 @@ import im_not_llm_b200 as inl
 from oracle import gemma as G
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_embeddinggemma2"
-TOLERANCE = 2e-5  # crates/inl-text/src/gemma2.rs:941-967
+# The reference's bound for its GPU f32 run against the golden: cosine > 0.99999
+# per row (metal_f32_matches_the_reference, crates/inl-text/src/gemma2.rs:1057-1072);
+# its CPU run is held to |d| < 2e-5 (:941-967). Here both: the cosine bound,
+# and 1e-4 on every component.
+COSINE = 0.99999
+TOLERANCE = 1e-4
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
@@ -45,8 +50,9 @@ def test_tiny_embeddinggemma2_matches_the_references_golden(gpu, batch_size, whi
                                tokenizer=tok)
         out = emb.embed(golden["texts"])
         for i, (got, want) in enumerate(zip(out, case[which])):
-            assert np.abs(np.asarray(got) - np.asarray(want, dtype=np.float32)).max() < TOLERANCE, \
-                (case["max_length"], which, i)
+            got, want = np.asarray(got), np.asarray(want, dtype=np.float32)
+            assert _cosine_rows(got, want) > COSINE, (case["max_length"], which, i)
+            assert np.abs(got - want).max() < TOLERANCE, (case["max_length"], which, i)
     model.close()
 
 
@@ -100,5 +106,6 @@ def test_tiny_embeddinggemma2_from_the_model_dir(gpu):
     case = next(c for c in golden["cases"] if c["max_length"] == 64)
     emb = inl.TextEmbedder.from_model_dir(GOLDEN, inl.TextOptions(max_length=64))
     for i, (got, want) in enumerate(zip(emb.embed(golden["texts"]), case["batched"])):
-        assert np.abs(np.asarray(got) - np.asarray(want, dtype=np.float32)).max() < TOLERANCE, i
+        got, want = np.asarray(got), np.asarray(want, dtype=np.float32)
+        assert _cosine_rows(got, want) > COSINE and np.abs(got - want).max() < TOLERANCE, i
     emb.unload()
