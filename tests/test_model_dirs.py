@@ -143,3 +143,17 @@ def test_missing_files_are_inference_errors(tmp_path):
     (tmp_path / "config.json").write_text("{not json")
     with pytest.raises(inl.InferenceError, match="is invalid"):
         loading.dense_model(tmp_path)
+
+
+def test_late_dir_dense_bias_must_be_in_the_weights(tmp_path, recording):
+    """A Dense config with "bias": true needs linear.bias in its weights
+    (crates/inl-late/src/native.rs:559-566); the error comes at load."""
+    d = _late_dir(tmp_path)
+    cfg = json.loads((d / "1_Dense" / "config.json").read_text())
+    cfg["bias"] = True
+    (d / "1_Dense" / "config.json").write_text(json.dumps(cfg))
+    e = inl.LateEncoder.from_model_dir(d)
+    assert loading.late_model(d).dense_bias
+    with pytest.raises(inl.InferenceError, match="Dense weight load failed"):
+        e._model()
+    assert not e.is_loaded()
