@@ -247,6 +247,17 @@ EngineInfo TextEmbedder::load() {
   return info_of(options_, out_dim ? out_dim : mi.dense_dim, mi, options_.max_length);
 }
 
+TextIdentity TextEmbedder::identity() {
+  const EngineInfo info = load();
+  TextIdentity t;
+  t.id = info.model_id;
+  t.dimension = info.dimension;
+  t.dtype = info.dtype;
+  t.device = "cuda";
+  t.max_length = options_.max_length;
+  return t;
+}
+
 std::vector<std::vector<float>> TextEmbedder::embed(const Tokens& texts) {
   const Tokens t = truncate(texts, options_.max_length);
   if (t.empty()) return {};

@@ -196,11 +196,21 @@ class EngineBase {
   BatchDeadline deadline_;
 };
 
+// The embedding space of a TextEmbedder (crates/inl-text/src/native.rs:156-167).
+struct TextIdentity {
+  std::string id;
+  int dimension = 0;
+  std::string dtype;
+  std::string device;  // "cuda"
+  size_t max_length = 0;
+};
+
 // DenseEngine (crates/inl-core/src/engine.rs:66-84) as TextEmbedder implements it.
 class TextEmbedder : public EngineBase {
  public:
   using EngineBase::EngineBase;
   EngineInfo load();
+  TextIdentity identity();  // loads the model (native.rs:476-488)
   std::vector<std::vector<float>> embed(const Tokens& texts);
 };
 
@@ -210,6 +220,7 @@ class SparseEncoder : public EngineBase {
  public:
   SparseEncoder(Loader loader, Options options);
   EngineInfo load();
+  EngineInfo identity() { return load(); }  // crates/inl-sparse/src/native.rs:271-283
   std::vector<SparseVector> encode(const Tokens& texts);
 };
 
@@ -227,6 +238,7 @@ class LateEncoder : public EngineBase {
  public:
   LateEncoder(Loader loader, Options options, LateTask query = {}, LateTask document = {});
   EngineInfo load();
+  EngineInfo identity() { return load(); }  // crates/inl-late/src/native.rs:256-270
   // task: "query" or "document"
   std::vector<std::vector<std::vector<float>>> encode(const Tokens& texts, const std::string& task = "document");
   // Tokens the model sees per input for `task`, after the task's cut

@@ -151,6 +151,8 @@ int main() {
     CHECK(throws<ConfigError>([&] { e4.embed(texts_of({2})); }));
     TextEmbedder e5([&] { auto f = std::make_unique<Fake>(&calls); f->arch = 2; f->dense_dim = 768; return f; }, o4);
     CHECK(e5.load().dimension == 128);
+    const TextIdentity ident = e5.identity();
+    CHECK(ident.dimension == 128 && ident.device == "cuda" && ident.max_length == o4.max_length);
     Options o6;
     o6.output_dim = 300;
     TextEmbedder e6([&] { auto f = std::make_unique<Fake>(&calls); f->arch = 2; f->dense_dim = 768; return f; }, o6);
