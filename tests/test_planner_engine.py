@@ -310,3 +310,40 @@ def test_data_parallel_sparse_and_late_gather_by_index():
         inl.DataParallelEmbedder([_EchoReplica(nan=True)]).encode_sparse([[1, 2]])
     with pytest.raises(inl.InferenceError, match="non-finite"):
         inl.DataParallelEmbedder([_EchoReplica(nan=True)]).encode_late([[1, 2]])
+
+
+from hypothesis import given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+
+@settings(max_examples=200, deadline=None)
+@given(lengths=st.lists(st.integers(0, 300), max_size=60), budget=st.integers(1, 800),
+       max_texts=st.one_of(st.none(), st.integers(1, 10)))
+def test_plan_packed_properties(lengths, budget, max_texts):
+    """For any lengths: consecutive ranges covering every input once, each
+    within the real-token budget and the text cap unless it is one input."""
+    order = inl.planner.longest_first(lengths)
+    sorted_lengths = [lengths[i] for i in order]
+    plan = inl.planner.plan_packed(sorted_lengths, budget, max_texts)
+    flat = [k for r in plan for k in r]
+    assert flat == list(range(len(lengths)))
+    for r in plan:
+        assert len(r) >= 1
+        if len(r) > 1:
+            assert sum(sorted_lengths[k] for k in r) <= budget
+            assert max_texts is None or len(r) <= max_texts
+    # longest first, ties in input order
+    assert all(sorted_lengths[i] >= sorted_lengths[i + 1] for i in range(len(sorted_lengths) - 1))
+
+
+@settings(max_examples=100, deadline=None)
+@given(costs=st.lists(st.floats(0, 100, allow_nan=False), max_size=40), workers=st.integers(1, 8))
+def test_assign_lpt_properties(costs, workers):
+    """Every batch assigned once; the heaviest worker is within the LPT bound
+    (at most the average load plus the largest single cost)."""
+    plan = inl.planner.assign_lpt(costs, workers)
+    assert len(plan) == workers
+    assert sorted(b for w in plan for b in w) == list(range(len(costs)))
+    loads = [sum(costs[b] for b in w) for w in plan]
+    if costs:
+        assert max(loads) <= sum(costs) / workers + max(costs) + 1e-9
