@@ -347,3 +347,21 @@ def test_assign_lpt_properties(costs, workers):
     loads = [sum(costs[b] for b in w) for w in plan]
     if costs:
         assert max(loads) <= sum(costs) / workers + max(costs) + 1e-9
+
+
+@settings(max_examples=200, deadline=None)
+@given(a=st.lists(st.tuples(st.integers(0, 50), st.one_of(st.floats(-2, 5, width=32),
+                                                          st.sampled_from([float("nan"), float("inf")]))),
+                  max_size=30),
+       b=st.lists(st.tuples(st.integers(0, 50), st.floats(0.125, 5, width=32)), max_size=30))
+def test_sparse_vector_properties(a, b):
+    """from_pairs always yields a vector new() accepts; the JSON form
+    round-trips; dot is symmetric and equals the dense inner product."""
+    va, vb = inl.SparseVector.from_pairs(a), inl.SparseVector.from_pairs(b)
+    for v in (va, vb):
+        assert inl.SparseVector.new(v.indices, v.values) == v
+        assert inl.SparseVector.from_json(v.to_json()) == v
+    dense = np.zeros((2, 51), dtype=np.float64)
+    dense[0, va.indices] = va.values
+    dense[1, vb.indices] = vb.values
+    assert va.dot(vb) == pytest.approx(vb.dot(va)) == pytest.approx(float(dense[0] @ dense[1]), rel=1e-5, abs=1e-6)
