@@ -59,3 +59,22 @@ def test_cuda_backend_links_and_a_failed_load_is_an_inl_error(tmp_path):
         assert code == "config" and message.startswith("config error: model load:"), out
     else:  # the checkpoint path does not exist
         assert code in ("config", "inference"), out
+
+
+def test_host_layer_under_address_and_undefined_behaviour_sanitizers(tmp_path):
+    """The same host tests built with -fsanitize=address,undefined: no memory
+    error or undefined behaviour in the planners, the deadline's detached
+    workers, the engines or the shard list."""
+    exe = tmp_path / "test_engine_asan"
+    flags = [f for f in FLAGS if f != "-O1"] + ["-O1", "-g", "-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+                                                "-fno-sanitize-recover=all"]
+    probe = subprocess.run([GXX, *flags, "-x", "c++", "-", "-o", str(tmp_path / "probe")], input="int main(){}",
+                           capture_output=True, text=True, timeout=120)
+    if probe.returncode != 0:
+        pytest.skip("g++ has no sanitizer runtime here")
+    _run([GXX, *flags, str(HOST / "engine.cpp"), str(ROOT / "tests" / "cpp" / "test_engine.cpp"), "-o", str(exe)])
+    assert "all passed" in _run([str(exe)])
+    chk = tmp_path / "test_checkpoint_asan"
+    _run([GXX, *flags, f"-I{ROOT / 'im-not-llm_b200' / 'csrc'}", str(ROOT / "tests" / "cpp" / "test_checkpoint.cpp"),
+          "-o", str(chk)])
+    assert "all passed" in _run([str(chk), str(tmp_path)])
