@@ -78,3 +78,17 @@ def test_host_layer_under_address_and_undefined_behaviour_sanitizers(tmp_path):
     _run([GXX, *flags, f"-I{ROOT / 'im-not-llm_b200' / 'csrc'}", str(ROOT / "tests" / "cpp" / "test_checkpoint.cpp"),
           "-o", str(chk)])
     assert "all passed" in _run([str(chk), str(tmp_path)])
+
+
+def test_host_layer_under_thread_sanitizer(tmp_path):
+    """The engine tests under -fsanitize=thread: the gate, the load lock and
+    the deadline's worker hand-off are free of data races."""
+    flags = [f for f in FLAGS if f != "-O1"] + ["-O1", "-g", "-fsanitize=thread"]
+    probe = subprocess.run([GXX, *flags, "-x", "c++", "-", "-o", str(tmp_path / "probe")], input="int main(){}",
+                           capture_output=True, text=True, timeout=120)
+    if probe.returncode != 0:
+        pytest.skip("g++ has no thread sanitizer runtime here")
+    exe = tmp_path / "test_engine_tsan"
+    _run([GXX, *flags, str(HOST / "engine.cpp"), str(ROOT / "tests" / "cpp" / "test_engine.cpp"), "-o", str(exe)])
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "all passed" in r.stdout and "WARNING: ThreadSanitizer" not in r.stderr, r.stderr
