@@ -3,9 +3,7 @@ Qwen3.5 linear-attention pieces, checked against oracle/qwen3_5.py, which is
 itself pinned on the reference's tiny_qwen3_5_late golden.
 
 The argument checks run on the host before any CUDA call, so they are tested
-on CPU. The GPU parity test has not run on a GPU yet: the kernels were
-written after this build's last GPU session, so it stays skipped until its
-first run on a B200."""
+on CPU; the parity test against the oracle runs on the GPU."""
 import ctypes
 
 import numpy as np
@@ -39,7 +37,6 @@ def test_hook_argument_checks_need_no_gpu():
 
 
 @pytest.mark.gpu
-@pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")
 @pytest.mark.parametrize("nk,nv,dk,dv", [(2, 4, 8, 8), (2, 2, 16, 64), (1, 2, 128, 128)])
 def test_conv_and_delta_rule_match_the_oracle(gpu, nk, nv, dk, dv):
     import torch

@@ -2,10 +2,7 @@
 model as the single file: the tiny EmbeddingGemma 2 golden checkpoint split
 in two shards, embeddings equal to the single-file load's bit for bit (the
 shard list follows crates/inl-core/src/hub.rs:324-353); an index without a
-weight_map is an inference error.
-
-Written after this build's last GPU session; skipped until its first run on
-a B200."""
+weight_map is an inference error."""
 import json
 from pathlib import Path
 
@@ -16,8 +13,7 @@ import im_not_llm_b200 as inl
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_embeddinggemma2"
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
+pytestmark = pytest.mark.gpu
 
 
 def test_sharded_checkpoint_loads_like_the_single_file(gpu, tmp_path):

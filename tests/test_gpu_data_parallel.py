@@ -1,17 +1,13 @@
 """DataParallelEmbedder with real models: two replicas on cuda:0 driven by
 two host threads give the single model's embeddings (same texts, other
-batch compositions), and the sparse path the single model's SPLADE rows.
-
-Written after this build's last GPU session; skipped until its first run on
-a B200."""
+batch compositions), and the sparse path the single model's SPLADE rows."""
 import numpy as np
 import pytest
 
 import im_not_llm_b200 as inl
 from tests.conftest import cosine_rows
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
+pytestmark = pytest.mark.gpu
 
 
 def test_two_replicas_match_one_model(gpu):

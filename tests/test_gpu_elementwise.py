@@ -89,15 +89,12 @@ def test_norms(gpu, x, out, H, ln):
         assert err < 2e-6, err
 
 
-_NARROW_PENDING = pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")
-
-
 # head_dim 8 / 16 / 32: the narrow warp layout (EmbeddingGemma 2 tiny checkpoints)
 @pytest.mark.parametrize("dt", [F32, BF16])
 @pytest.mark.parametrize("d,hq,hkv,v_norm", [(128, 16, 8, 0), (64, 12, 12, 0), (256, 3, 1, 1),
-                                             pytest.param(16, 4, 2, 1, marks=_NARROW_PENDING),
-                                             pytest.param(32, 4, 1, 1, marks=_NARROW_PENDING),
-                                             pytest.param(8, 2, 2, 0, marks=_NARROW_PENDING)])
+                                             (16, 4, 2, 1),
+                                             (32, 4, 1, 1),
+                                             (8, 2, 2, 0)])
 def test_qk_norm_rope(gpu, dt, d, hq, hkv, v_norm):
     import torch
 

@@ -9,10 +9,7 @@ embeddings (PLE), layer scalars and per_layer_config head shapes
   (full) run on the narrow q/k norm + RoPE kernel and the f32 attention.
 * A synthetic EmbeddingGemma 2 (head_dim 128 sliding, 256 full with one KV
   head, PLE 64) against oracle/gemma.py in f32 and bf16; in bf16 the two head
-  dims take different attention query blocks (the second work list).
-
-The PLE and per-layer-shape path was written after this build's last GPU
-session; these tests stay skipped until their first run on a B200."""
+  dims take different attention query blocks (the second work list)."""
 import json
 from pathlib import Path
 
@@ -30,8 +27,7 @@ GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_embeddinggemma2"
 COSINE = 0.99999
 TOLERANCE = 1e-4
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
+pytestmark = pytest.mark.gpu
 
 
 def _cosine_rows(a, b):

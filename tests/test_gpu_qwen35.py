@@ -2,11 +2,8 @@
 tiny_qwen3_5_late golden: every kept token vector within 1e-4, batched and
 one text per forward, query and document tasks (the assertion of
 crates/inl-late/tests/tiny_golden.rs), through the LateEncoder facade with
-the fixture's tokenizer, prompts, lengths and skiplist.
-
-The tower was written after this build's last GPU session. Its oracle
-(oracle/qwen3_5.py) is pinned on the same golden on CPU, but the CUDA path has
-not run yet, so these tests stay skipped until their first run on a B200."""
+the fixture's tokenizer, prompts, lengths and skiplist. The oracle
+(oracle/qwen3_5.py) is pinned on the same golden on the CPU."""
 import json
 from pathlib import Path
 
@@ -18,8 +15,7 @@ import im_not_llm_b200 as inl
 LATE = Path(__file__).resolve().parent / "golden" / "tiny_qwen3_5_late"
 TOLERANCE = 1e-4  # crates/inl-late/tests/tiny_golden.rs:24-26
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
+pytestmark = pytest.mark.gpu
 
 
 def _encoder(batch_size):

@@ -6,10 +6,7 @@ logit shift of 2, two prefix tokens that are also masked, and a canonical
 fold of 72 terms onto 62; its head_dim 8 runs on the narrow RoPE kernel and
 the small f32 attention. Once through CudaModel on the recorded ids, once
 through the SparseEncoder facade from the texts ("[D] " / "[Q] " markers,
-the fixture's tokenizer).
-
-Written after this build's last GPU session; skipped until its first run on
-a B200."""
+the fixture's tokenizer)."""
 import json
 from pathlib import Path
 
@@ -21,8 +18,7 @@ import im_not_llm_b200 as inl
 GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_splade"
 TOLERANCE = 1e-4  # crates/inl-sparse/src/modernbert.rs:1014-1057
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skip(reason="written after the last GPU session of its build; first run on a B200 pending")]
+pytestmark = pytest.mark.gpu
 
 
 def _config():
