@@ -351,11 +351,8 @@ template <int D>
 int launch_flash(const AttnArgs& a, cudaStream_t s) {
   auto kern = flash_fwd_bf16_kernel<D>;
   constexpr int bytes = FlashSmem<D>::BYTES;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -3;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};  // one bit per device
+  if (set_smem_limit_once(kern, bytes, attr) != cudaSuccess) return -3;
   dim3 grid(a.n_work, a.hq);
   kern<<<grid, 128, bytes, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
@@ -365,11 +362,8 @@ template <int D>
 int launch_f32(const AttnArgs& a, cudaStream_t s) {
   auto kern = attn_f32_kernel<D>;
   constexpr int bytes = (kFQ * D + kFK * (D + 1) + kFK * D) * 4;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -3;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};  // one bit per device
+  if (set_smem_limit_once(kern, bytes, attr) != cudaSuccess) return -3;
   dim3 grid(a.n_work, a.hq);
   kern<<<grid, 128, bytes, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
@@ -380,6 +374,11 @@ int launch_f32(const AttnArgs& a, cudaStream_t s) {
 int attention_q_block(int bf16, int d) {
   if (bf16) return attention_tc_supported(d) ? 128 : kBM;
   return kFQ;
+}
+
+bool attention_supported(int bf16, int d) {
+  if (bf16) return d == 64 || d == 128 || d == 256;
+  return d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256;
 }
 
 int attention(const AttnArgs& a, cudaStream_t s) {

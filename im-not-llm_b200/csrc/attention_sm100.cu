@@ -632,13 +632,8 @@ int launch_fa(const AttnArgs& a, long long total_rows, cudaStream_t s) {
   // Pair the query heads of a GQA group when the group size is even.
   const bool pair = (a.hq / a.hkv) % 2 == 0;
   auto kern = pair ? fa_sm100_kernel<D, true> : fa_sm100_kernel<D, false>;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
-  static bool attr[2][64] = {};  // the attribute is per kernel and device
-  if (!attr[pair][dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return -3;
-    attr[pair][dev] = true;
-  }
+  static std::atomic<unsigned long long> attr[2] = {};  // per kernel, one bit per device
+  if (set_smem_limit_once(kern, C::SMEM, attr[pair]) != cudaSuccess) return -3;
   FaParams p;
   p.cu = a.cu;
   p.work = a.work;

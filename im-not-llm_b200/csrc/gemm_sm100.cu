@@ -703,12 +703,14 @@ bool make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long lo
 }
 
 int num_sms() {
-  static int n = 0;
+  // per device: a process may drive GPUs of different SM counts
+  static std::atomic<int> count[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = count[dev].load(std::memory_order_relaxed);
   if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    count[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -719,16 +721,9 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
                         int* status, int max_ctas, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_tn_kernel<BN, EPI, ACT>;
-  int dev = 0;
-  cudaError_t derr = cudaGetDevice(&dev);
-  if (derr != cudaSuccess) return derr;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  static bool attr_set[64] = {};  // per instantiation and device
-  if (!attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static std::atomic<unsigned long long> attr_set{0};  // per instantiation, one bit per device
+  cudaError_t aerr = set_smem_limit_once(kern, C::SMEM_BYTES, attr_set);
+  if (aerr != cudaSuccess) return aerr;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
@@ -742,16 +737,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
                              const EpiArgs& e, int* status, int max_ctas, cudaStream_t stream) {
   using C = PairCfg;
   auto kern = gemm_bf16_pair_kernel<EPI, ACT>;
-  int dev = 0;
-  cudaError_t derr = cudaGetDevice(&dev);
-  if (derr != cudaSuccess) return derr;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  static bool attr_set[64] = {};  // per instantiation and device
-  if (!attr_set[dev]) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
-  }
+  static std::atomic<unsigned long long> attr_set{0};  // per instantiation, one bit per device
+  cudaError_t aerr = set_smem_limit_once(kern, C::SMEM_BYTES, attr_set);
+  if (aerr != cudaSuccess) return aerr;
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + C::BN - 1) / C::BN);
   int pairs = num_sms() / 2;
   if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 // Every bf16 epilogue first multiplies the accumulator by the row scale
 // r = rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps) when ss_in is given (the
 // RMSNorm of the A rows, folded: RMSNorm(x) W^T = r * (x (W diag(w))^T)).
@@ -73,6 +75,24 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream);
 bool make_tma_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
                       int box_rows, int box_cols);
 int num_sms_cached();
+
+// Raises a kernel's dynamic shared-memory limit on the current device, once
+// per (kernel, device). The attribute belongs to the device that is current
+// when it is set, so a process driving several GPUs sets it on each. `done`
+// holds one bit per device and is shared by host threads; setting the
+// attribute twice from two threads is harmless.
+template <typename Kernel>
+inline cudaError_t set_smem_limit_once(Kernel kern, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const unsigned long long bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return err;
+}
 
 struct GemmF32Args {
   const float* A = nullptr;
@@ -223,6 +243,9 @@ int attention_tc(const AttnArgs& a, long long total_rows, cudaStream_t s);
 
 // Number of query rows per work item the attention kernels expect.
 int attention_q_block(int bf16, int d);
+
+// Whether attention() has a kernel for this dtype and head_dim.
+bool attention_supported(int bf16, int d);
 
 // ---------------------------------------------------------------- Gated DeltaNet (Qwen3.5 linear attention)
 // out[t, c] = silu(sum_j w[c, j] x[t - K + 1 + j, c]) over each text's tokens (pos[t] = position in its text).
