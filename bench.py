@@ -12,9 +12,10 @@ time). ``value`` = real tokens of all ranks / max over ranks of the device
 time of K steps with ids already in HBM; ``e2e`` = the same through the public
 API with pinned host ids and host outputs, copies inside the timed region.
 
-``--impl reference`` times the CPU reference arm on the host cores: the numpy
-restatement of the reference's forward (oracle/qwen3.py), each step a bounded
-sample of the same corpus; rank 0 only.
+``--impl reference`` times the CPU reference arm on the host cores: the
+torch-CPU f32 (MKL) restatement of the reference's forward
+(oracle/qwen3_torch.py, pinned to the numpy restatement oracle/qwen3.py), each
+step a bounded sample of the same corpus; rank 0 only.
 """
 from __future__ import annotations
 
@@ -35,9 +36,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "embedded tokens/sec (Qwen3-0.6B arch, bf16)"
 BATCH_TOKENS = 65536
 N_TEXTS = 65536
-CPU_SAMPLE_TOKENS = 2048  # tokens of one CPU-baseline step
+CPU_SAMPLE_TOKENS = 8192  # tokens of one CPU-baseline sample (10-30 s of CPU work)
 REF_TIME_BUDGET_S = 150.0  # CPU seconds the reference arm's timed steps may take together
 REF_MIN_SAMPLE_TOKENS = 256
+REF_MAX_SAMPLE_TOKENS = 8192
 
 
 def _peaks():
@@ -123,35 +125,56 @@ def corpus_batches():
     return texts, batches, lengths
 
 
-def cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=CPU_SAMPLE_TOKENS, seed=0):
-    """Tokens/s of the numpy restatement on a bounded sample of the corpus."""
-    from oracle import qwen3 as Q
-
+def cpu_sample(texts, lengths, budget_tokens: int, seed: int):
+    """A bounded CPU sample of the corpus: texts drawn uniformly at random
+    (long ones included, so the sample keeps the corpus's length mix) until
+    about ``budget_tokens`` real tokens; packed as (ids, cu, texts, tokens)."""
     rng = np.random.default_rng(seed)
     picked, total = [], 0
     for i in rng.permutation(len(texts)):
-        if total + lengths[i] > budget_tokens:
-            continue
-        picked.append(i)
+        picked.append(int(i))
         total += int(lengths[i])
-        if total > budget_tokens * 0.9:
+        if total >= budget_tokens:
             break
     ids = np.concatenate([texts[i] for i in picked])
     cu = np.zeros(len(picked) + 1, dtype=np.int32)
     np.cumsum([lengths[i] for i in picked], out=cu[1:])
+    return ids, cu, len(picked), total
+
+
+def cpu_reference_rate(cpu_model, texts, lengths, budget_tokens=CPU_SAMPLE_TOKENS, seed=0):
+    """Tokens/s of the torch-CPU f32 restatement (oracle/qwen3_torch.py, MKL
+    on every host thread) on a bounded sample of the corpus."""
+    ids, cu, n, total = cpu_sample(texts, lengths, budget_tokens, seed)
     t0 = time.perf_counter()
-    Q.embed_last(weights, cfg, ids, cu)
+    cpu_model.embed_last(ids, cu)
     dt = time.perf_counter() - t0
-    return total / dt, total, len(picked), dt
+    return total / dt, total, n, dt
 
 
-def rank_share(batches: list, rank: int, world: int, steps: int, warmup: int) -> list:
-    """The batches one rank runs, warm-up first: every ``world``-th batch of
-    the corpus. The timed steps are the rank's whole share when ``steps``
-    covers it, else ``steps`` batches spaced evenly over it (the share runs
-    longest to shortest, so a prefix would over-weight the attention-heavy
-    2k-token texts); the warm-up batches come from the same spread."""
-    mine = batches[rank::world]
+def cpu_model(weights, cfg):
+    import torch
+
+    from oracle import qwen3_torch as QT
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    return QT.Qwen3Cpu(weights, cfg), threads
+
+
+def rank_share(batches: list, costs: list, rank: int, world: int, steps: int, warmup: int) -> list:
+    """The batches one rank runs, warm-up first. The corpus's batches are
+    dealt to the ranks longest-processing-time first on their forward cost
+    (``planner.assign_lpt`` over ``planner.batch_cost``), so every rank holds
+    about the same work and no rank always draws the heaviest batch. The
+    timed steps are the rank's whole share when ``steps`` covers it, else
+    ``steps`` batches spaced evenly over the share in descending cost (a
+    prefix would over-weight the attention-heavy 2k-token texts); the warm-up
+    batches come from the same spread."""
+    import im_not_llm_b200 as inl
+
+    share = inl.planner.assign_lpt(costs, world)[rank]  # heaviest first
+    mine = [batches[b] for b in share]
     if steps >= len(mine):
         timed = [mine[i % len(mine)] for i in range(steps)]
     else:
@@ -199,29 +222,29 @@ def run_reference(args, world, rank):
     cfg = dict(inl.synthetic.QWEN3_0_6B)
     weights = inl.synthetic.qwen3_weights(cfg, seed=0)
     texts, _, lengths = corpus_batches()
+    model, threads = cpu_model(weights, cfg)
     # The warm-up samples (at least one) also measure this host's rate; each
     # timed step's sample is then sized so all steps fit REF_TIME_BUDGET_S.
     rate = 0.0
     for w in range(max(args.warmup, 1)):
-        rate = cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=512, seed=100 + w)[0]
-    per_step = int(np.clip(rate * REF_TIME_BUDGET_S / max(args.steps, 1), REF_MIN_SAMPLE_TOKENS, CPU_SAMPLE_TOKENS))
-    rates, toks, secs = [], 0, 0.0
+        rate = cpu_reference_rate(model, texts, lengths, budget_tokens=512, seed=100 + w)[0]
+    per_step = int(np.clip(rate * REF_TIME_BUDGET_S / max(args.steps, 1), REF_MIN_SAMPLE_TOKENS, REF_MAX_SAMPLE_TOKENS))
+    toks, secs = 0, 0.0
     for s in range(args.steps):
-        r, n, _, dt = cpu_reference_rate(weights, cfg, texts, lengths, budget_tokens=per_step, seed=s)
-        rates.append(r)
+        _, n, _, dt = cpu_reference_rate(model, texts, lengths, budget_tokens=per_step, seed=s)
         toks += n
         secs += dt
     value = toks / secs
-    cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / max(args.steps, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "cfg5 corpus, bounded CPU sample per step", "sample_tokens_per_step": toks // max(args.steps, 1)},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} samples of ~{per_step} tokens of the cfg5 corpus (sized from the "
-                                   f"warm-up rate to fit {REF_TIME_BUDGET_S:.0f} s), numpy f32 restatement of "
-                                   f"crates/inl-text/src/qwen3/mod.rs with BLAS on {cores} threads"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} samples of ~{per_step} tokens of the cfg5 corpus (texts drawn "
+                                   f"uniformly, long ones included; sized from the warm-up rate to fit "
+                                   f"{REF_TIME_BUDGET_S:.0f} s), torch-CPU f32 restatement of "
+                                   f"crates/inl-text/src/qwen3/mod.rs (MKL) on {threads} threads"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -238,7 +261,8 @@ def run_ours(args, world, rank, local):
     model = inl.CudaModel(cfg, weights, device=local, dtype="bf16")
     texts, batches, lengths = corpus_batches()
     need = args.warmup + args.steps
-    sel = rank_share(batches, rank, world, args.steps, args.warmup)
+    costs = [inl.planner.batch_cost([lengths[i] for i in b]) for b in batches]
+    sel = rank_share(batches, costs, rank, world, args.steps, args.warmup)
     packed = [inl.planner.pack(texts, b) for b in sel]
     # inputs resident in HBM for the device-timed leg
     dev_ids = [torch.from_numpy(p[0].view(np.int32)).cuda() for p in packed]
@@ -256,8 +280,7 @@ def run_ours(args, world, rank, local):
         model.embed(dev_ids[i].data_ptr(), packed[i][1], out=dev_out.data_ptr())
     torch.cuda.synchronize()
 
-    # ---------------- device-timed leg (value) with GEMM events (roofline)
-    model.set_profiling(True)
+    # ---------------- device-timed leg (value): no per-launch events inside
     model.launch_count(reset=True)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     tokens = 0
@@ -281,6 +304,17 @@ def run_ours(args, world, rank, local):
     barrier()
     ms = start.elapsed_time(stop)
     launches = model.launch_count()
+
+    # ---------------- profiled pass (roofline): the same steps again, with CUDA
+    # events around every GEMM and attention launch on the model's stream
+    model.set_profiling(True)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for i in range(args.warmup, need):
+        model.embed(dev_ids[i].data_ptr(), packed[i][1], out=dev_out.data_ptr())
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prof_step_ms = p0.elapsed_time(p1)
     prof = model.profile(-1)
     kinds = {name: model.profile(k) for k, name in enumerate(("qkv", "o", "gate_up", "down"))}
     attn_prof = model.profile(100)  # attention launches
@@ -325,13 +359,15 @@ def run_ours(args, world, rank, local):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} bf16 sustained",
                          "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
-                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch, mean "
-                                         "over one bench step's 112 launches (ncu, profiles/launches_cfg5_bench.md); "
-                                         "algorithmic bytes per launch ~6.1e8",
+                         "traffic_source": "fixed figure from one ncu capture of a config-5 step (mean "
+                                           "dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch), "
+                                           "not measured by this run; algorithmic bytes per launch ~6.1e8",
+                         "timing": "per-launch CUDA events in a second pass over the same steps; value is "
+                                   "timed without them",
                          "gemm_launches": prof["launches"], "gemm_ms": prof["ms"],
-                         "gemm_share_of_step": prof["ms"] / ms if ms > 0 else None,
+                         "gemm_share_of_step": prof["ms"] / prof_step_ms if prof_step_ms > 0 else None,
                          "attention_ms_per_step": attn_prof["ms"] / args.steps,
-                         "attention_share_of_step": attn_prof["ms"] / ms if ms > 0 else None,
+                         "attention_share_of_step": attn_prof["ms"] / prof_step_ms if prof_step_ms > 0 else None,
                          "by_projection": {k: {"ms_per_step": v["ms"] / args.steps,
                                                "tflops": v["flops"] / (v["ms"] / 1000.0) / 1e12 if v["ms"] else 0.0}
                                            for k, v in kinds.items()}},
@@ -343,10 +379,13 @@ def run_ours(args, world, rank, local):
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            r, n, k, dt = cpu_reference_rate(weights, cfg, texts, lengths)
-            line["cpu_baseline"] = {"value": r, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                                    "sample": f"{k} texts / {n} tokens of the cfg5 corpus through the numpy f32 "
-                                              f"restatement (oracle/qwen3.py), BLAS on {os.cpu_count()} threads, {dt:.1f}s"}
+            cm, threads = cpu_model(weights, cfg)
+            cpu_reference_rate(cm, texts, lengths, budget_tokens=256, seed=99)  # warm-up
+            r, n, k, dt = cpu_reference_rate(cm, texts, lengths)
+            line["cpu_baseline"] = {"value": r, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                    "sample": f"{k} texts / {n} tokens of the cfg5 corpus (drawn uniformly) through "
+                                              f"the torch-CPU f32 restatement (oracle/qwen3_torch.py, MKL) on "
+                                              f"{threads} threads, {dt:.1f}s"}
         emit(line)
     model.close()
 

@@ -1,7 +1,8 @@
 """The multi-GPU side of bench.py on CPU: two ranks over gloo (127.0.0.1).
 
-`bench.py --gpus N` runs one process per GPU. Each rank takes every N-th
-packed batch (`rank_share`) and the timing stats are combined across ranks
+`bench.py --gpus N` runs one process per GPU. The packed batches are dealt
+to the ranks longest-processing-time first on their forward cost
+(`rank_share`), and the timing stats are combined across ranks
 (`reduce_timing`: max of the times, sum of the tokens); rank 0 prints the
 line. The same helpers run here on CPU tensors with the gloo backend."""
 import socket
@@ -19,6 +20,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+# the costs of 11 batches, heaviest first as the longest-first planner leaves them
+COSTS = [9.0, 8.0, 7.0, 6.0, 5.0, 4.0, 3.0, 2.5, 2.0, 1.5, 1.0]
+
+
 def _rank(rank: int, world: int, port: int, out_dir: str) -> None:
     import json
     from datetime import timedelta
@@ -32,8 +37,8 @@ def _rank(rank: int, world: int, port: int, out_dir: str) -> None:
                             timeout=timedelta(seconds=60))
     try:
         got = bench.reduce_timing(10.0 + rank, 20.0 + 3 * rank, 100 * (rank + 1), world, "cpu")
-        share = bench.rank_share(list(range(11)), rank, world, steps=50, warmup=3)
-        spread = bench.rank_share(list(range(101)), rank, world, steps=4, warmup=3)
+        share = bench.rank_share(list(range(11)), COSTS, rank, world, steps=50, warmup=3)
+        spread = bench.rank_share(list(range(101)), [1.0] * 101, rank, world, steps=4, warmup=3)
         (Path(out_dir) / f"rank{rank}.json").write_text(json.dumps({"reduce": got, "share": share,
                                                                    "spread": spread}))
     finally:
@@ -53,13 +58,17 @@ def test_two_ranks_share_batches_and_reduce_timing(tmp_path):
         assert r["reduce"] == [11.0, 23.0, 300.0]  # max, max, sum
     # whole shares (steps >= share): disjoint, together every batch, warm-up from the share
     s0, s1 = res[0]["share"], res[1]["share"]
-    assert set(s0) == {0, 2, 4, 6, 8, 10} and set(s1) == {1, 3, 5, 7, 9}
+    assert set(s0).isdisjoint(s1) and set(s0) | set(s1) == set(range(11))
     assert len(s0) == len(s1) == 53 and s0[:3] == s0[3:6]
+    # LPT: batch 0 to rank 0, batch 1 to rank 1, then each to the lighter rank;
+    # the loads differ by at most the lightest batch
+    loads = [sum(COSTS[b] for b in set(r)) for r in (s0, s1)]
+    assert abs(loads[0] - loads[1]) <= min(COSTS)
+    assert s0[3] == 0 and s1[3] == 1  # each share runs heaviest first
     # spread (steps < share): evenly spaced over the rank's share, first and last included
     sp0, sp1 = res[0]["spread"], res[1]["spread"]
-    # rank 0 holds 51 batches (indices 0, 16, 33, 50), rank 1 holds 50 (0, 16, 32, 49)
-    assert sp0[3:] == [0, 32, 66, 100] and sp1[3:] == [1, 33, 65, 99]
-    assert sp0[:3] == sp0[3:6]
+    assert len(sp0) == len(sp1) == 7 and sp0[:3] == sp0[3:6]
+    assert set(sp0[3:]).isdisjoint(sp1[3:])
 
 
 def test_single_rank_needs_no_process_group():
@@ -68,4 +77,4 @@ def test_single_rank_needs_no_process_group():
 
     assert bench.reduce_timing(5.0, 6.0, 7, 1, "cpu") == (5.0, 6.0, 7.0)
     with pytest.raises(Exception):
-        bench.rank_share([], 0, 1, 2, 1)  # an empty share has nothing to time
+        bench.rank_share([], [], 0, 1, 2, 1)  # an empty share has nothing to time

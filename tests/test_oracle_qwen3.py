@@ -153,3 +153,22 @@ def test_late_head_normalizes_every_token(tiny):
     out = Q.encode_late(w, cfg, proj, ids, cu)
     assert out.shape == (cu[-1], 32)
     assert np.allclose(np.linalg.norm(out, axis=-1), 1.0, atol=1e-5)
+
+
+def test_torch_restatement_matches_the_numpy_oracle(tiny):
+    """oracle/qwen3_torch.py (the fast CPU checker and the bench's CPU arm) is
+    the same function as oracle/qwen3.py: dense last-token vectors and late
+    per-token vectors, texts of 1 to 300 tokens, f32 throughout."""
+    from oracle import qwen3_torch as QT
+
+    cfg, w = tiny
+    ids, cu = inl.synthetic.random_texts(6, 1, 300, cfg["vocab_size"], seed=6)
+    m = QT.Qwen3Cpu(w, cfg)
+    dense = m.embed_last(ids, cu)
+    want = Q.embed_last(w, cfg, ids, cu)
+    assert cosine_rows(dense, want).min() > 0.99999
+    assert np.abs(dense - want).max() < 1e-5
+    proj = inl.synthetic.late_projection(cfg, out=32)
+    late = m.encode_late(proj, ids, cu)
+    want_late = Q.encode_late(w, cfg, proj, ids, cu)
+    assert cosine_rows(late, want_late).min() > 0.99999
