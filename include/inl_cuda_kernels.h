@@ -103,12 +103,16 @@ INL_API int inl_cuda_attention(const void* q, const void* k, const void* v, int6
  * lives in one file-scope device array of 288.5 KiB that every GPU loading the
  * library holds until exit, so a call takes at most 8192 texts and 32768
  * query blocks (a block is 128 query rows for bf16 head_dim 64/128, 64 for
- * bf16 head_dim 256, 32 for f32); larger calls return INL_ERR_INVALID_INPUT. The
- * first call on each device looks up the array's device address with that
- * device current; make that first call before any stream capture. All calls
- * share the array and would race if they overlapped on the GPU, so each call
- * holds a process-wide lock until its stream has drained. A bounded device
- * wait that runs out returns INL_ERR_TIMEOUT. */
+ * bf16 head_dim 256, 32 for f32); larger calls return INL_ERR_INVALID_INPUT.
+ * The work list is built on the device, heaviest first like the allocating
+ * entry point's. The first call on each device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture. All calls share the array and would race if they overlapped on
+ * the GPU, so each call holds a process-wide lock and waits for its stream to
+ * drain before it returns; for that reason a stream that is capturing is
+ * refused with INL_ERR_CONFIG before any work is queued. Argument errors are
+ * found before any work is queued. A bounded device wait that runs out
+ * returns INL_ERR_TIMEOUT. */
 INL_API int inl_cuda_attention_noalloc(const void* q, const void* k, const void* v, int64_t ldq, int64_t ldk,
                                        int64_t ldv, void* out, int64_t ldo, int dtype, int hq, int hkv, int d,
                                        float scale, int causal, int window, const int32_t* cu_seqlens_host,

@@ -7,14 +7,21 @@ more query blocks) and must not be affected by them. Outputs start as NaN so a
 row the kernel skipped shows up. Tolerances are the attention tests': max
 |diff| < 2e-2 for bf16, 2e-5 for f32.
 
-This file is collected last so that it runs both after the other GPU tests
-(the library's other entry points have already allocated on the device) and
-alone in a fresh process.
+This file is collected last so that its GPU tests run after the other GPU
+tests (the library's other entry points have already allocated on the
+device); one of them repeats the two calls in a child process whose first
+call into the library is the no-allocation one, so the per-device lookup of
+the array's address is covered on a fresh process too.
 """
 import ctypes
+import subprocess
+import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
 
 TOL = {"bf16": 2e-2, "f32": 2e-5}
 
@@ -46,6 +53,16 @@ def _run_both(torch, N_, dtype, lengths, hq, hkv, d, causal, window, seed):
     return outs
 
 
+CALLS = [
+    # first call: long texts, many query blocks, GQA 16/8 (Qwen3-0.6B heads)
+    dict(lengths=[2048, 1537, 129, 5, 1, 300, 0, 700], hq=16, hkv=8, causal=0, window=-1, seed=11),
+    # second call: fewer and shorter texts, causal + window, GQA 4/1
+    dict(lengths=[7, 64, 65, 33, 130], hq=4, hkv=1, causal=1, window=16, seed=12),
+    # third call: causal, texts of equal and different block counts, an empty one
+    dict(lengths=[640, 129, 640, 0, 1, 257, 1000, 3], hq=16, hkv=8, causal=1, window=-1, seed=13),
+]
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype,d", [("bf16", 128), ("bf16", 64), ("f32", 64)])
 def test_noalloc_attention_matches_allocating_entry_point_twice(gpu, dtype, d):
@@ -53,13 +70,7 @@ def test_noalloc_attention_matches_allocating_entry_point_twice(gpu, dtype, d):
 
     from im_not_llm_b200 import _native as N_
 
-    calls = [
-        # first call: long texts, many query blocks, GQA 16/8 (Qwen3-0.6B heads)
-        dict(lengths=[2048, 1537, 129, 5, 1, 300, 0, 700], hq=16, hkv=8, causal=0, window=-1, seed=11),
-        # second call: fewer and shorter texts, causal + window, GQA 4/1
-        dict(lengths=[7, 64, 65, 33, 130], hq=4, hkv=1, causal=1, window=16, seed=12),
-    ]
-    for c in calls:
+    for c in CALLS:
         got, want = _run_both(torch, N_, dtype, c["lengths"], c["hq"], c["hkv"], d, c["causal"], c["window"],
                               c["seed"])
         assert not torch.isnan(got.float()).any()
@@ -85,3 +96,100 @@ def test_noalloc_attention_rejects_calls_over_its_limits():
     st = lib.inl_cuda_attention_noalloc(None, None, None, 128, 128, 128, None, 128, 1, 1, 1, 128, 1.0, 0, -1,
                                         bad.ctypes.data, 2, None)
     assert st == 4 and "non-decreasing" in N_.last_error()
+
+
+@pytest.mark.gpu
+def test_noalloc_attention_in_a_fresh_process(gpu):
+    """The same calls in a child process whose first call into the library is
+    the no-allocation entry point (the array's device address is looked up
+    there)."""
+    code = (
+        "import sys, torch; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+        "import test_zz_no_alloc as t\n"
+        "from im_not_llm_b200 import _native as N_\n"
+        "for c in t.CALLS:\n"
+        "    got, want = t._run_both(torch, N_, 'bf16', c['lengths'], c['hq'], c['hkv'], 128, c['causal'],"
+        " c['window'], c['seed'])\n"
+        "    assert not torch.isnan(got.float()).any()\n"
+        "    assert (got.double() - want.double()).abs().max().item() < t.TOL['bf16']\n"
+        "print('fresh ok')\n" % (str(ROOT), str(ROOT / "tests")))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "fresh ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_noalloc_attention_refuses_a_capturing_stream(gpu):
+    """It waits for its stream before returning, so a stream in capture is
+    refused (INL_ERR_CONFIG) before anything is queued, and the capture stays
+    valid."""
+    import torch
+
+    from im_not_llm_b200 import _native as N_
+
+    cu = _cu([100, 28])
+    qkv = torch.zeros(128, 3 * 128, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(128, 128, device="cuda", dtype=torch.bfloat16)
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        st = N_.lib().inl_cuda_attention_noalloc(
+            qkv.data_ptr(), qkv.data_ptr() + 256, qkv.data_ptr() + 512, 384, 384, 384, out.data_ptr(), 128, 1, 1,
+            1, 128, 1.0, 1, -1, cu.ctypes.data, 2, ctypes.c_void_p(side.cuda_stream))
+        out.add_(1)  # the capture is still usable after the refusal
+    assert st == 1 and "capturing" in N_.last_error()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert out.float().eq(1).all()
+
+
+def _work_order(cu, qb, causal):
+    """The heaviest-first order of the allocating entry point: (text, block)
+    items, stably sorted by the key blocks a causal block attends to (b + 1)
+    or by the text's block count (csrc/model.cu attention_work)."""
+    items = []
+    for i in range(len(cu) - 1):
+        nb = -(-(cu[i + 1] - cu[i]) // qb)
+        items += [((b + 1) if causal else nb, i, b) for b in range(nb)]
+    return [(i, b) for _, i, b in sorted(items, key=lambda x: -x[0])]
+
+
+def _build_kernel_order(cu, qb, causal):
+    """The slot arithmetic of build_work_kernel (csrc/attention_noalloc.cu),
+    restated on the CPU: texts sorted by block count (ties in text order),
+    exclusive prefix of the sorted counts, then each slot found by search."""
+    n = len(cu) - 1
+    nb = [-(-(cu[i + 1] - cu[i]) // qb) for i in range(n)]
+    order = sorted(range(n), key=lambda i: (-nb[i], i))
+    snb = [nb[i] for i in order]
+    pre = np.concatenate([[0], np.cumsum(snb)]).astype(np.int64)
+    n_work = int(pre[-1])
+    out = []
+    for p in range(n_work):
+        if not causal:
+            r = max(r for r in range(n) if pre[r] <= p)
+            b = p - pre[r]
+        else:
+            def above(b):  # items on levels above b
+                c = sum(1 for x in snb if x > b + 1)
+                return pre[c] - (b + 1) * c
+            b = min(b for b in range(snb[0]) if above(b) <= p)
+            r = p - above(b)
+        out.append((order[r], int(b)))
+    return out
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_device_work_list_arithmetic_is_heaviest_first(causal):
+    """CPU check of the build kernel's slot arithmetic: every (text, block)
+    item exactly once, in non-increasing weight, the same weights slot by
+    slot as the allocating entry point's list."""
+    rng = np.random.default_rng(3)
+    for lengths in ([2048, 1537, 129, 5, 1, 300, 0, 700], [640, 129, 640, 0, 1, 257, 1000, 3],
+                    list(rng.integers(0, 3000, 200))):
+        cu = _cu(lengths)
+        got = _build_kernel_order(cu, 128, causal)
+        want = _work_order(cu, 128, causal)
+        assert sorted(got) == sorted(want) and len(set(got)) == len(got)
+        nbs = [-(-(cu[i + 1] - cu[i]) // 128) for i in range(len(lengths))]
+        weight = [(b + 1) if causal else nbs[i] for i, b in got]
+        assert weight == [(b + 1) if causal else nbs[i] for i, b in want]
