@@ -454,8 +454,6 @@ def run_kernel_case(name: str, reps: int = 3):
                                                status.data_ptr(), s), name)
         flops = 2.0 * M * Nn * K
     elif name in ("attention", "attention_cfg5"):
-        import numpy as np
-
         if name == "attention":
             lengths = [2048] * 4 + [512] * 8 + [256] * 16
         else:  # ~64k tokens of config 5's lognormal lengths, in corpus order (seeded)
@@ -477,6 +475,61 @@ def run_kernel_case(name: str, reps: int = 3):
                                                4096, 4096, 4096, o.data_ptr(), 2048, 1, 16, 8, 128, 128 ** -0.5, 1,
                                                -1, cu.ctypes.data, len(lengths), s), name)
         flops = sum(4.0 * 2048 * L * (L + 1) / 2 for L in lengths)
+    elif name in ("norm", "layer_norm", "qk_norm_rope_d256"):
+        # HBM-bound row kernels at config sizes larger than L2: RMSNorm / LayerNorm
+        # over 65536 x 1024 bf16 rows (Qwen3 width), and config 4's q / k / v norm
+        # + RoPE over 66k tokens x (3 + 1 + 1) heads of 256 (v weightless)
+        if name == "qk_norm_rope_d256":
+            T, hq, hkv, d = 66142, 3, 1, 256
+            ld = (hq + 2 * hkv) * d
+            qkv = torch.randn(T, ld, device="cuda").to(torch.bfloat16)
+            qw, kw = torch.ones(d, device="cuda"), torch.ones(d, device="cuda")
+            pos = (torch.arange(T, device="cuda", dtype=torch.int32) % 2048)
+            ang = torch.arange(2048, device="cuda", dtype=torch.float64)[:, None] / (1e6 ** (torch.arange(
+                0, d // 2, device="cuda", dtype=torch.float64) * 2 / d))[None, :]
+            cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+
+            def launch():
+                N.check(N.lib().inl_cuda_qk_norm_rope(qkv.data_ptr(), 1, ld, T, hq, hkv, d, qw.data_ptr(),
+                                                      kw.data_ptr(), 1, 1e-6, pos.data_ptr(), cos.data_ptr(),
+                                                      sin.data_ptr(), 2048, status.data_ptr(), s), name)
+            nbytes = 2.0 * T * ld * 2
+        else:
+            rows, H = 65536, 1024
+            x = torch.randn(rows, H, device="cuda").to(torch.bfloat16)
+            y = torch.empty_like(x)
+            wt = torch.rand(H, device="cuda") + 0.5
+            bias = torch.zeros(H, device="cuda")
+            ln = 1 if name == "layer_norm" else 0
+
+            def launch():
+                N.check(N.lib().inl_cuda_norm(x.data_ptr(), 1, H, wt.data_ptr(), bias.data_ptr() if ln else None,
+                                              1e-6, ln, rows, H, y.data_ptr(), 1, H, s), name)
+            nbytes = 2.0 * rows * H * 2
+        flops = 0.0
+    elif name == "attention_cfg4":
+        # config 4's attention: 128 texts of log-uniform lengths (seed 4), 3 query
+        # heads / 1 K/V head x 256, bidirectional, the 512-token window of 5 in 6 layers
+        import im_not_llm_b200 as inl
+
+        _, cu = inl.synthetic.cfg4_inputs()
+        cu = np.ascontiguousarray(cu, dtype=np.int32)
+        lengths = np.diff(cu)
+        T, hq, hkv, d, win = int(cu[-1]), 3, 1, 256, 512
+        ld = (hq + 2 * hkv) * d
+        qkv = torch.randn(T, ld, device="cuda").to(torch.bfloat16)
+        o = torch.empty(T, hq * d, device="cuda", dtype=torch.bfloat16)
+
+        def launch():
+            N.check(N.lib().inl_cuda_attention(qkv.data_ptr(), qkv.data_ptr() + hq * d * 2,
+                                               qkv.data_ptr() + (hq + hkv) * d * 2, ld, ld, ld, o.data_ptr(), hq * d,
+                                               1, hq, hkv, d, 1.0, 0, win, cu.ctypes.data, len(lengths), s), name)
+        # attended (query, key) pairs: |q - k| <= 512 inside each text
+        pairs = 0.0
+        for L in lengths:
+            i = np.arange(int(L))
+            pairs += float((np.minimum(i + win, L - 1) - np.maximum(i - win, 0) + 1).sum())
+        flops = 4.0 * hq * d * pairs
     else:
         raise SystemExit(f"unknown case {name}")
     launch()
@@ -489,9 +542,99 @@ def run_kernel_case(name: str, reps: int = 3):
     torch.cuda.synchronize()
     ms = st.elapsed_time(en) / reps
     code = int(status.item())
-    print(json.dumps({"case": name, "ms": ms, "tflops": flops / ms / 1e9, "device_status": code}), flush=True)
+    rec = {"case": name, "ms": ms, "device_status": code}
+    if flops:
+        rec["tflops"] = flops / ms / 1e9
+    else:  # HBM-bound: algorithmic bytes (each input read once, each output written once)
+        hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs") if (
+            ROOT / "MEASURED_PEAKS.json").exists() else None
+        rec["gb_per_s"] = nbytes / ms / 1e6
+        rec["hbm_frac"] = rec["gb_per_s"] / hbm if hbm else None
+    print(json.dumps(rec), flush=True)
     if code:
         raise SystemExit(f"{name}: a device wait ran past its limit (status {code})")
+
+
+# The other BASELINE configurations, one forward of each config's own input
+# per step: `python bench.py --case cfg2`. name: (architecture, dtype, output).
+MODEL_CASES = {
+    "cfg1": ("Qwen3-0.6B, 8 x 128 tokens, last-token pooling + L2", "f32", "dense"),
+    "cfg2": ("ModernBERT SPLADE, 32 texts U[16, 256], V = 36282 max-pooled", "f32", "sparse"),
+    "cfg3": ("Qwen3-0.6B bidirectional + 1024->128 per token, 64 x 512 tokens", "bf16", "late"),
+    "cfg4": ("EmbeddingGemma-style, 128 texts log-U[32, 2048], mean pool + dense chain", "bf16", "dense"),
+    "cfg2_bf16": ("ModernBERT SPLADE in bf16 (the decoder on the tcgen05 SEGMAX GEMM), config 2's texts", "bf16",
+                  "sparse"),
+    # the f32 configurations on the SIMT FFMA GEMMs instead of the 3xBF16 tensor-core GEMMs
+    "cfg1_ffma": ("Qwen3-0.6B, 8 x 128 tokens, SIMT f32 GEMMs", "f32", "dense"),
+    "cfg2_ffma": ("ModernBERT SPLADE, 32 texts, SIMT f32 GEMMs", "f32", "sparse"),
+}
+
+
+def run_model_case(name: str, reps: int = 10, warmup: int = 3):
+    """Tokens/s of one configuration's full forward through the C ABI, ids
+    and outputs resident on the device; GEMM and attention time from a
+    second, profiled pass."""
+    import torch
+
+    import im_not_llm_b200 as inl
+
+    S = inl.synthetic
+    desc, dtype, kind = MODEL_CASES[name]
+    ffma = name.endswith("_ffma")
+    label = name
+    name = name.removesuffix("_ffma").removesuffix("_bf16")
+    if name == "cfg1":
+        cfg, w = dict(S.QWEN3_0_6B), S.qwen3_weights(S.QWEN3_0_6B, seed=0)
+        ids, cu = S.cfg1_inputs()
+    elif name == "cfg2":
+        cfg, w = dict(S.MODERNBERT_SPLADE), S.modernbert_weights(S.MODERNBERT_SPLADE, seed=0)
+        ids, cu = S.cfg2_inputs()
+    elif name == "cfg3":
+        cfg, w = dict(S.QWEN3_0_6B, is_causal=False), S.qwen3_weights(S.QWEN3_0_6B, seed=0)
+        ids, cu = S.cfg3_inputs()
+    else:
+        cfg, w = dict(S.GEMMA_STYLE), S.gemma_weights(S.GEMMA_STYLE, seed=0)
+        ids, cu = S.cfg4_inputs()
+    m = inl.CudaModel(cfg, w, dtype=dtype)
+    if name == "cfg3":
+        m.set_dense_head(S.late_projection(cfg))
+    if ffma:
+        m.set_f32_gemm("ffma")
+    info = m.info()
+    T, n = int(cu[-1]), len(cu) - 1
+    dev_ids = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.uint32).view(np.int32)).cuda()
+    rows, cols = {"dense": (n, info["dense_dim"]), "sparse": (n, info["sparse_dim"]),
+                  "late": (T, info["multivector_dim"])}[kind]
+    out = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    fwd = {"dense": m.embed, "sparse": m.encode_sparse, "late": m.encode_multivector}[kind]
+
+    def step():
+        fwd(dev_ids.data_ptr(), cu, out=out.data_ptr())
+
+    for _ in range(warmup):
+        step()
+    stream = torch.cuda.ExternalStream(m.stream)
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record(stream)
+    for _ in range(reps):
+        step()
+    en.record(stream)
+    torch.cuda.synchronize()
+    ms = st.elapsed_time(en) / reps
+    m.set_profiling(True)
+    for _ in range(reps):
+        step()
+    torch.cuda.synchronize()
+    g, a = m.profile(-1), m.profile(100)
+    m.set_profiling(False)
+    m.close()
+    print(json.dumps({"case": label, "workload": desc, "dtype": dtype, "tokens": T, "texts": n, "ms": ms,
+                      "tokens_per_s": T / (ms / 1000.0),
+                      "gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] else None,
+                      "gemm_ms": g["ms"] / reps, "attention_ms": a["ms"] / reps,
+                      "note": "inputs and outputs resident on the device; GEMM / attention times from a "
+                              "second pass with per-launch events"}), flush=True)
 
 
 # The benchmark's stdout carries exactly one JSON line. main() keeps the real
@@ -507,8 +650,9 @@ def emit(line: dict) -> None:
 def main():
     global _JSON_OUT
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + ["attention", "attention_cfg5", "gemm_qkv_fused",
-                                                              "gemm_gateup_fused"],
+    ap.add_argument("--case", choices=sorted(KERNEL_CASES) + sorted(MODEL_CASES) +
+                    ["attention", "attention_cfg5", "attention_cfg4", "gemm_qkv_fused", "gemm_gateup_fused", "norm",
+                     "layer_norm", "qk_norm_rope_d256"],
                     default=None,
                     help="time one kernel on a small case instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
@@ -517,6 +661,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.case in MODEL_CASES:
+        run_model_case(args.case)
+        return
     if args.case:
         run_kernel_case(args.case)
         return

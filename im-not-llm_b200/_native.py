@@ -33,7 +33,8 @@ EXPORTED = (
     "inl_cuda_model_launch_count", "inl_cuda_model_stream", "inl_cuda_embed_gather", "inl_cuda_norm",
     "inl_cuda_qk_norm_rope", "inl_cuda_token_positions", "inl_cuda_last_token_norm_l2", "inl_cuda_gemm_bf16_ex",
     "inl_cuda_attention_noalloc", "inl_cuda_causal_conv_silu", "inl_cuda_gated_delta_rule",
-    "inl_cuda_model_set_dense_normalize", "inl_cuda_config_check",
+    "inl_cuda_model_set_dense_normalize", "inl_cuda_config_check", "inl_cuda_model_set_prune_last",
+    "inl_cuda_forward_sparse_compact", "inl_cuda_model_set_f32_gemm",
 )
 
 
@@ -78,6 +79,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "inl_cuda_forward_dense": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int]),
         "inl_cuda_forward_multivector": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),
         "inl_cuda_forward_sparse": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),
+        "inl_cuda_forward_sparse_compact": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                                    c_void_p, c_i64, c_int]),
         "inl_cuda_forward_hidden": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int]),
         "inl_cuda_model_info": (c_int, [c_void_p, P(ModelInfo)]),
         "inl_cuda_model_destroy": (None, [c_void_p]),
@@ -94,6 +97,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                                c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int,
                                                c_void_p]),
         "inl_cuda_model_set_profiling": (c_int, [c_void_p, c_int]),
+        "inl_cuda_model_set_prune_last": (c_int, [c_void_p, c_int]),
+        "inl_cuda_model_set_f32_gemm": (c_int, [c_void_p, c_int]),
         "inl_cuda_model_profile": (c_int, [c_void_p, c_int, P(c_int), P(c_double), P(c_double)]),
         "inl_cuda_model_launch_count": (ctypes.c_longlong, [c_void_p, c_int]),
         "inl_cuda_model_stream": (c_void_p, [c_void_p]),

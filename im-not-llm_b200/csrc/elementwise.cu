@@ -57,6 +57,44 @@ __device__ __forceinline__ void st8<float>(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// E = 2, 4 or 8 consecutive values in one vector access (E * sizeof(T) bytes,
+// aligned to that size).
+template <typename T, int E>
+__device__ __forceinline__ void ld_vec(const T* p, float (&v)[E]) {
+  if constexpr (E == 8) {
+    ld8<T>(p, v);
+  } else if constexpr (sizeof(T) == 2) {
+    if constexpr (E == 4) {
+      const uint2 w = *reinterpret_cast<const uint2*>(p);
+      const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y);
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p));
+      v[0] = a.x; v[1] = a.y;
+    }
+  } else {
+    if constexpr (E == 4) {
+      const float4 a = *reinterpret_cast<const float4*>(p);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    } else {
+      const float2 a = *reinterpret_cast<const float2*>(p);
+      v[0] = a.x; v[1] = a.y;
+    }
+  }
+}
+template <typename T, int E>
+__device__ __forceinline__ void st_vec(T* p, const float (&v)[E]) {
+  if constexpr (E == 8) {
+    st8<T>(p, v);
+  } else if constexpr (sizeof(T) == 2) {
+    if constexpr (E == 4) *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+    else *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(v[0], v[1]);
+  } else {
+    if constexpr (E == 4) *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    else *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  }
+}
+
 // ------------------------------------------------------------ embedding
 template <typename TT, typename TO>
 __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T, const TT* __restrict__ table,
@@ -172,6 +210,62 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, const 
   }
 }
 
+// The same norm with the row held in registers (H = 256 NC, NC <= 4): one read
+// of the row instead of one per pass, the same arithmetic in the same order
+// (bit-identical results), weight and bias read as float4.
+template <typename TI, typename TO, bool LN, bool ACT, int NC>
+__global__ void norm_rows_reg_kernel(const TI* __restrict__ x, long long ldx, const float* __restrict__ w,
+                                     const float* __restrict__ b, float eps, int rows, TO* __restrict__ out,
+                                     long long ldo) {
+  constexpr int H = 256 * NC;
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const TI* xr = x + row * ldx;
+  TO* orow = out + row * ldo;
+  float v[NC][8];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    ld8<TI>(xr + lane * 8 + 256 * k, v[k]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[k][j] = pre_act<ACT>(v[k][j]);
+  }
+  float mean = 0.f;
+  if (LN) {
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[k][j];
+    mean = warp_sum(sum) / static_cast<float>(H);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float t = v[k][j] - mean;
+      ss += t * t;
+    }
+  const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(H) + eps);
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int c = lane * 8 + 256 * k;
+    float wv[8], bv[8];
+    if (w) ld8<float>(w + c, wv);
+    if (b) ld8<float>(b + c, bv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = (v[k][j] - mean) * inv;
+      if (w) t *= wv[j];
+      if (b) t += bv[j];
+      v[k][j] = t;
+    }
+    st8<TO>(orow + c, v[k]);
+  }
+}
+
 // ------------------------------------------------------------ q/k norm + rope
 // One warp per (token, head). Lane l holds elements [E*l, E*l+E), E = d/32;
 // lanes 0..15 hold the first half of the head, lanes 16..31 the second, so the
@@ -227,6 +321,62 @@ __global__ void qk_norm_rope_kernel(QkRopeArgs a) {
   }
 #pragma unroll
   for (int e = 0; e < E; ++e) st_f<T>(row, lane * E + e, x[e]);
+}
+
+// Same arithmetic with one vector access per lane for the row (E elements)
+// and for its E cos / sin factors, for rows, leading dimension and tables
+// aligned to the access size (the host checks).
+template <typename T, int E>
+__global__ void qk_norm_rope_vec_kernel(QkRopeArgs a) {
+  const int warps = blockDim.x >> 5;
+  const long long item = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
+  if (item >= static_cast<long long>(a.T) * heads) return;
+  const int t = static_cast<int>(item / heads);
+  const int h = static_cast<int>(item - static_cast<long long>(t) * heads);
+  constexpr int d = E * 32;
+  constexpr int half = d / 2;
+  T* row = reinterpret_cast<T*>(a.qkv) + static_cast<long long>(t) * a.ld + static_cast<long long>(h) * d;
+  const bool is_q = h < a.hq;
+  const bool is_k = !is_q && h < a.hq + a.hkv;
+  const float* w = is_q ? a.qw : (is_k ? a.kw : nullptr);
+  const bool norm = is_q ? (a.qw != nullptr) : (is_k ? (a.kw != nullptr) : true);
+  const bool is_bf16 = sizeof(T) == 2;
+  float x[E];
+  ld_vec<T, E>(row + lane * E, x);
+  if (norm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(d) + a.eps);
+    float wv[E];
+    if (w) ld_vec<float, E>(w + lane * E, wv);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float v = x[e] * inv;
+      if (w) v *= wv[e];
+      x[e] = is_bf16 ? bf16_round(v) : v;
+    }
+  }
+  if (is_q || is_k) {
+    int p = a.pos[t];
+    if (p < 0 || p >= a.max_pos) {
+      if (lane == 0 && a.status) atomicCAS(a.status, 0, INL_DEV_BAD_INDEX);
+      p = 0;
+    }
+    const bool first = lane < 16;
+    const int i0 = lane * E - (first ? 0 : half);
+    float c[E], sn[E];
+    ld_vec<float, E>(a.cos + static_cast<long long>(p) * half + i0, c);
+    ld_vec<float, E>(a.sin + static_cast<long long>(p) * half + i0, sn);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      x[e] = first ? (x[e] * c[e] - other * sn[e]) : (x[e] * c[e] + other * sn[e]);
+    }
+  }
+  st_vec<T, E>(row + lane * E, x);
 }
 
 // Heads of d <= 32 features (8, 16, 32): one warp per (token, head), lane l < d
@@ -359,16 +509,59 @@ __global__ void bias_rows_l2_kernel(float* x, long long ldx, int rows, int D, co
     for (int c = lane; c < D; c += 32) xr[c] *= inv;
 }
 
+// Mean pooling in two passes, deterministic. Pass 1: one CTA of 8 warps per
+// (text, chunk of kSegChunk tokens, group of 256 columns); lane l of a warp
+// holds columns 8l .. 8l+7 of the group (one 16-byte load per row for bf16),
+// warp w sums the chunk's rows w, w + 8, ..., and the eight warp sums are
+// added in warp order into partial[text][chunk][:]. Pass 2 adds a text's
+// chunks in order and divides by its length. Long texts spread over
+// ceil(L / kSegChunk) CTAs instead of one.
+constexpr int kSegChunk = 256;
+
 template <typename T>
-__global__ void segment_mean_kernel(const T* __restrict__ x, long long ldx, const int* __restrict__ cu, int n,
-                                    int H, float* __restrict__ out) {
-  const int i = blockIdx.x;
-  const int c = blockIdx.y * blockDim.x + threadIdx.x;
-  if (i >= n || c >= H) return;
+__global__ void __launch_bounds__(256) segment_sum_chunks_kernel(const T* __restrict__ x, long long ldx,
+                                                                 const int* __restrict__ cu, int H, int chunks,
+                                                                 float* __restrict__ partial) {
+  const int i = blockIdx.x, j = blockIdx.y;
   const int s = cu[i], e = cu[i + 1];
-  float acc = 0.f;
-  for (int t = s; t < e; ++t) acc += ld_f<T>(x + static_cast<long long>(t) * ldx, c);
-  out[static_cast<long long>(i) * H + c] = e > s ? acc / static_cast<float>(e - s) : 0.f;
+  const int t0 = s + j * kSegChunk;
+  if (t0 >= e) return;
+  const int t1 = min(e, t0 + kSegChunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.z * 256 + lane * 8;
+  const bool on = c0 < H;  // H is a multiple of 8
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (on) {
+    for (int t = t0 + warp; t < t1; t += 8) {
+      float v[8];
+      ld8<T>(x + static_cast<long long>(t) * ldx + c0, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += v[k];
+    }
+  }
+  __shared__ float red[8][256];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[warp][lane * 8 + k] = acc[k];
+  __syncthreads();
+  const int c = blockIdx.z * 256 + threadIdx.x;
+  if (c < H) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sum += red[w][threadIdx.x];
+    partial[(static_cast<long long>(i) * chunks + j) * H + c] = sum;
+  }
+}
+
+__global__ void segment_mean_finish_kernel(const float* __restrict__ partial, const int* __restrict__ cu, int n,
+                                           int H, int chunks, float* __restrict__ out) {
+  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (idx >= static_cast<long long>(n) * H) return;
+  const int i = static_cast<int>(idx / H), c = static_cast<int>(idx - static_cast<long long>(i) * H);
+  const int L = cu[i + 1] - cu[i];
+  const int nch = (L + kSegChunk - 1) / kSegChunk;
+  float sum = 0.f;
+  for (int j = 0; j < nch; ++j) sum += partial[(static_cast<long long>(i) * chunks + j) * H + c];
+  out[idx] = L > 0 ? sum / static_cast<float>(L) : 0.f;
 }
 
 __global__ void truncate_normalize_kernel(const float* __restrict__ x, int n, int D, int dim,
@@ -567,10 +760,48 @@ int embed_gather(const uint32_t* ids, int T, const void* table, int table_bf16, 
   return ok(cudaGetLastError());
 }
 
+template <bool LN, bool ACT, int NC>
+static void norm_reg_launch(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps,
+                            int rows, void* out, int out_bf16, long long ldo, int grid, cudaStream_t s) {
+  if (x_bf16 && out_bf16)
+    norm_rows_reg_kernel<__nv_bfloat16, __nv_bfloat16, LN, ACT, NC><<<grid, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, w, b, eps, rows, static_cast<__nv_bfloat16*>(out), ldo);
+  else if (x_bf16)
+    norm_rows_reg_kernel<__nv_bfloat16, float, LN, ACT, NC><<<grid, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, w, b, eps, rows, static_cast<float*>(out), ldo);
+  else if (out_bf16)
+    norm_rows_reg_kernel<float, __nv_bfloat16, LN, ACT, NC><<<grid, 128, 0, s>>>(
+        static_cast<const float*>(x), ldx, w, b, eps, rows, static_cast<__nv_bfloat16*>(out), ldo);
+  else
+    norm_rows_reg_kernel<float, float, LN, ACT, NC><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, w, b,
+                                                                        eps, rows, static_cast<float*>(out), ldo);
+}
+
+// Register-resident norm when the rows allow it (H = 256, 512, 768 or 1024;
+// rows, strides and weights aligned for the vector accesses); false otherwise.
+template <bool LN, bool ACT>
+static bool norm_reg(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows,
+                     int H, void* out, int out_bf16, long long ldo, cudaStream_t s) {
+  const int ei = x_bf16 ? 2 : 4, eo = out_bf16 ? 2 : 4;
+  if ((H & 255) || H > 1024 || (ldx * ei) % (8 * ei) || (ldo * eo) % (8 * eo) ||
+      (reinterpret_cast<uintptr_t>(x) % (8 * ei)) || (reinterpret_cast<uintptr_t>(out) % (8 * eo)) ||
+      (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
+    return false;
+  const int grid = rows_grid(rows, 4);
+  switch (H / 256) {
+    case 1: norm_reg_launch<LN, ACT, 1>(x, x_bf16, ldx, w, b, eps, rows, out, out_bf16, ldo, grid, s); break;
+    case 2: norm_reg_launch<LN, ACT, 2>(x, x_bf16, ldx, w, b, eps, rows, out, out_bf16, ldo, grid, s); break;
+    case 3: norm_reg_launch<LN, ACT, 3>(x, x_bf16, ldx, w, b, eps, rows, out, out_bf16, ldo, grid, s); break;
+    default: norm_reg_launch<LN, ACT, 4>(x, x_bf16, ldx, w, b, eps, rows, out, out_bf16, ldo, grid, s); break;
+  }
+  return true;
+}
+
 template <bool LN>
 static int norm_dispatch(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps,
                          int rows, int H, void* out, int out_bf16, long long ldo, cudaStream_t s) {
   if (rows <= 0) return 0;
+  if (norm_reg<LN, false>(x, x_bf16, ldx, w, b, eps, rows, H, out, out_bf16, ldo, s)) return ok(cudaGetLastError());
   const int grid = rows_grid(rows, 4);
   if (x_bf16 && out_bf16)
     norm_rows_kernel<__nv_bfloat16, __nv_bfloat16, LN><<<grid, 128, 0, s>>>(
@@ -609,8 +840,17 @@ int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s) {
   }
   const int E = a.d / 32;
   if (a.d % 32 != 0) return -1;
-#define INL_QKR(EE)                                                              \
-  if (a.bf16) qk_norm_rope_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);   \
+  // One vector access per lane when the rows, the weights and the tables are
+  // aligned to it; element by element otherwise.
+  const size_t es = a.bf16 ? 2 : 4, vb = es * E;
+  const bool vec = (a.ld * es) % vb == 0 && (reinterpret_cast<uintptr_t>(a.qkv) % vb) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.cos) % (4 * E)) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.sin) % (4 * E)) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.qw) % (4 * E)) == 0 && (reinterpret_cast<uintptr_t>(a.kw) % (4 * E)) == 0;
+#define INL_QKR(EE)                                                                               \
+  if (vec && a.bf16) qk_norm_rope_vec_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);          \
+  else if (vec) qk_norm_rope_vec_kernel<float, EE><<<grid, 256, 0, s>>>(a);                       \
+  else if (a.bf16) qk_norm_rope_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);                \
   else qk_norm_rope_kernel<float, EE><<<grid, 256, 0, s>>>(a);
   switch (E) {
     case 2: INL_QKR(2) break;
@@ -639,6 +879,184 @@ int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, 
   return ok(cudaGetLastError());
 }
 
+// f32 rows split into three bf16 K-segments for the 3xBF16 tensor-core
+// product: x = hi + lo + O(2^-17 |x|) with hi = bf16(x), lo = bf16(x - hi).
+// Activation side (mode 0) [hi | hi | lo], weight side (mode 1) [hi | lo | hi]:
+// one bf16 GEMM over K' = 3K then sums hi.hi + hi.lo + lo.hi in f32.
+__global__ void split3_kernel(const float* __restrict__ x, long long ldx, int rows, int K, int mode,
+                              __nv_bfloat16* __restrict__ out, long long ldo) {
+  const int pairs = K / 2;
+  const long long total = static_cast<long long>(rows) * pairs;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / pairs);
+    const int k = 2 * static_cast<int>(i - static_cast<long long>(r) * pairs);
+    const float2 v = *reinterpret_cast<const float2*>(x + static_cast<long long>(r) * ldx + k);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(v.x, v.y);
+    const float2 h = __bfloat1622float2(hi);
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x - h.x, v.y - h.y);
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + static_cast<long long>(r) * ldo + k);
+    o[0] = hi;
+    o[K / 2] = mode ? lo : hi;
+    o[K] = mode ? hi : lo;
+  }
+}
+
+int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* out, long long ldo, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  if ((K & 1) || (ldx & 1) || (ldo & 1) || (reinterpret_cast<uintptr_t>(x) & 7) ||
+      (reinterpret_cast<uintptr_t>(out) & 3))
+    return -1;
+  const long long total = static_cast<long long>(rows) * (K / 2);
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  split3_kernel<<<blocks, 256, 0, s>>>(x, ldx, rows, K, mode, static_cast<__nv_bfloat16*>(out), ldo);
+  return ok(cudaGetLastError());
+}
+
+// out = a + b over rows x cols (f32; out may alias a or b).
+__global__ void add_rows_f32_kernel(float* out, long long ldo, const float* a, long long lda, const float* b,
+                                    long long ldb, int rows, int cols) {
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cols), c = static_cast<int>(i - static_cast<long long>(r) * cols);
+    out[static_cast<long long>(r) * ldo + c] = a[static_cast<long long>(r) * lda + c] + b[static_cast<long long>(r) * ldb + c];
+  }
+}
+
+int add_rows_f32(float* out, long long ldo, const float* a, long long lda, const float* b, long long ldb, int rows,
+                 int cols, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const long long total = static_cast<long long>(rows) * cols;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  add_rows_f32_kernel<<<blocks, 256, 0, s>>>(out, ldo, a, lda, b, ldb, rows, cols);
+  return ok(cudaGetLastError());
+}
+
+// Gated MLP from the full gate/up product x [rows, 2I] (f32) whose columns come in
+// blocks of `blk`: gate block j, then up block j. out[r, c] = act(gate) * up.
+template <int ACT>
+__global__ void act_mul_blocks_kernel(const float* __restrict__ x, long long ldx, int rows, int I, int blk,
+                                      float* __restrict__ out, long long ldo) {
+  const long long total = static_cast<long long>(rows) * I;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / I), c = static_cast<int>(i - static_cast<long long>(r) * I);
+    const int b = c / blk, o = c - b * blk;
+    const float* row = x + static_cast<long long>(r) * ldx + 2LL * b * blk + o;
+    float g = row[0];
+    if constexpr (ACT == INL_ACT_SILU) g = silu_f(g);
+    else if constexpr (ACT == INL_ACT_GELU_ERF) g = gelu_erf_f(g);
+    else g = gelu_tanh_f(g);
+    out[static_cast<long long>(r) * ldo + c] = g * row[blk];
+  }
+}
+
+int act_mul_blocks_f32(const float* x, long long ldx, int rows, int I, int blk, int act, float* out, long long ldo,
+                       cudaStream_t s) {
+  if (rows <= 0 || I <= 0) return 0;
+  if (blk <= 0) return -1;
+  const long long total = static_cast<long long>(rows) * I;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  switch (act) {
+    case INL_ACT_SILU: act_mul_blocks_kernel<INL_ACT_SILU><<<blocks, 256, 0, s>>>(x, ldx, rows, I, blk, out, ldo); break;
+    case INL_ACT_GELU_ERF:
+      act_mul_blocks_kernel<INL_ACT_GELU_ERF><<<blocks, 256, 0, s>>>(x, ldx, rows, I, blk, out, ldo);
+      break;
+    default: act_mul_blocks_kernel<INL_ACT_GELU_TANH><<<blocks, 256, 0, s>>>(x, ldx, rows, I, blk, out, ldo); break;
+  }
+  return ok(cudaGetLastError());
+}
+
+// One CTA per row. Counting: a block sum of the active entries.
+__global__ void sparse_count_kernel(const float* __restrict__ rows, int D, int* __restrict__ counts,
+                                    int* __restrict__ bad) {
+  const float* row = rows + static_cast<long long>(blockIdx.x) * D;
+  int c = 0;
+  bool finite = true;
+  for (int v = threadIdx.x; v < D; v += blockDim.x) {
+    const float w = row[v];
+    c += w > 0.f;
+    finite &= isfinite(w);
+  }
+  __shared__ int red[32];
+  c = __reduce_add_sync(0xffffffffu, c);
+  if (!__all_sync(0xffffffffu, finite) && (threadIdx.x & 31) == 0) atomicOr(bad, 1);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    counts[blockIdx.x] = t;
+  }
+}
+
+// Order-preserving compaction of one row per CTA: each pass takes blockDim.x
+// consecutive columns; a warp's active lanes find their slot from the ballot,
+// the warps' totals are scanned in shared memory, and the pass's total moves
+// the row's write position.
+__global__ void sparse_compact_kernel(const float* __restrict__ rows, int D, const long long* __restrict__ offsets,
+                                      int32_t* __restrict__ idx, float* __restrict__ val) {
+  const float* row = rows + static_cast<long long>(blockIdx.x) * D;
+  long long base = offsets[blockIdx.x];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __shared__ int wsum[32];
+  for (int v0 = 0; v0 < D; v0 += blockDim.x) {
+    const int v = v0 + threadIdx.x;
+    const float w = v < D ? row[v] : 0.f;
+    const bool on = w > 0.f;
+    const unsigned bal = __ballot_sync(0xffffffffu, on);
+    if (lane == 0) wsum[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int k = 0; k < nw; ++k) {
+      const int c = wsum[k];
+      before += k < warp ? c : 0;
+      total += c;
+    }
+    if (on) {
+      const long long at = base + before + __popc(bal & ((1u << lane) - 1u));
+      idx[at] = v;
+      val[at] = w;
+    }
+    base += total;
+    __syncthreads();  // wsum is rewritten by the next pass
+  }
+}
+
+int sparse_count(const float* rows, int n, int D, int* counts, int* bad, cudaStream_t s) {
+  if (n <= 0) return 0;
+  sparse_count_kernel<<<n, 256, 0, s>>>(rows, D, counts, bad);
+  return ok(cudaGetLastError());
+}
+
+int sparse_compact(const float* rows, int n, int D, const long long* offsets, int32_t* idx, float* val,
+                   cudaStream_t s) {
+  if (n <= 0) return 0;
+  sparse_compact_kernel<<<n, 256, 0, s>>>(rows, D, offsets, idx, val);
+  return ok(cudaGetLastError());
+}
+
+__global__ void gather_last_rows_kernel(const uint4* __restrict__ in, long long ld_in, const int* __restrict__ cu,
+                                        int n, int chunks, uint4* __restrict__ out, long long ld_out) {
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const uint4* src = in + static_cast<long long>(cu[i + 1] - 1) * ld_in;
+  uint4* dst = out + static_cast<long long>(i) * ld_out;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = src[c];
+}
+
+int gather_last_rows_bf16(const void* in, long long ld_in, const int* cu, int n, int cols, void* out,
+                          long long ld_out, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if ((cols % 8) || (ld_in % 8) || (ld_out % 8) || (reinterpret_cast<uintptr_t>(in) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
+    return -1;
+  gather_last_rows_kernel<<<n, 128, 0, s>>>(static_cast<const uint4*>(in), ld_in / 8, cu, n, cols / 8,
+                                             static_cast<uint4*>(out), ld_out / 8);
+  return ok(cudaGetLastError());
+}
+
 int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min, float* out, long long ldo,
                 cudaStream_t s) {
   if (rows <= 0) return 0;
@@ -646,14 +1064,24 @@ int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min,
   return ok(cudaGetLastError());
 }
 
-int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, float* out,
-                 cudaStream_t s) {
+size_t segment_mean_scratch_bytes(int n, int H, int max_len) {
+  const size_t chunks = static_cast<size_t>(std::max(1, (max_len + kSegChunk - 1) / kSegChunk));
+  return static_cast<size_t>(std::max(n, 1)) * chunks * H * 4;
+}
+
+int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, int max_len, float* scratch,
+                 float* out, cudaStream_t s) {
   if (n <= 0) return 0;
-  dim3 grid(n, (H + 127) / 128);
+  if ((H % 8) || (ldx % 8) || (reinterpret_cast<uintptr_t>(x) & 15)) return -1;
+  const int chunks = std::max(1, (max_len + kSegChunk - 1) / kSegChunk);
+  dim3 grid(n, chunks, (H + 255) / 256);
   if (x_bf16)
-    segment_mean_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, cu, n, H, out);
+    segment_sum_chunks_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, cu, H,
+                                                                    chunks, scratch);
   else
-    segment_mean_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float*>(x), ldx, cu, n, H, out);
+    segment_sum_chunks_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, cu, H, chunks, scratch);
+  const long long total = static_cast<long long>(n) * H;
+  segment_mean_finish_kernel<<<static_cast<int>((total + 255) / 256), 256, 0, s>>>(scratch, cu, n, H, chunks, out);
   return ok(cudaGetLastError());
 }
 
@@ -701,6 +1129,8 @@ int convert_bf16_rows(const __nv_bfloat16* src, int rows, int cols, void* dst, i
 int norm_act(const void* x, int x_bf16, long long ldx, const float* w, const float* b, float eps, int rows, int H,
              void* out, int out_bf16, long long ldo, cudaStream_t s) {
   if (rows <= 0) return 0;
+  if (x_bf16 == out_bf16 && norm_reg<true, true>(x, x_bf16, ldx, w, b, eps, rows, H, out, out_bf16, ldo, s))
+    return ok(cudaGetLastError());
   const int grid = rows_grid(rows, 4);
   if (x_bf16 && out_bf16)
     norm_rows_kernel<__nv_bfloat16, __nv_bfloat16, true, true><<<grid, 128, 0, s>>>(

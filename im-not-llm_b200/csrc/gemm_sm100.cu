@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int m_tiles = (M + kBM - 1) / kBM;
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 32 * kEpiWarps);
+      mbar_init(&tempty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -384,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();  // the previous kernel's outputs (A, residual, sums of squares) are complete
 
   if (warp == 0) {
     if (lane == 0) {
@@ -474,7 +476,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + quad * 32 + lane;
       epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e, st, lane);
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -532,6 +535,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leading CTA of the pair
@@ -563,6 +567,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -728,8 +733,8 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, to, M, N, K, e, status);
-  return cudaGetLastError();
+  cudaError_t err = launch_pdl(kern, dim3(grid), dim3(kThreads), C::SMEM_BYTES, stream, ta, tb, to, M, N, K, e, status);
+  return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 template <int EPI, int ACT>
@@ -744,8 +749,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   int pairs = num_sms() / 2;
   if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
   if (tiles < pairs) pairs = tiles;
-  kern<<<2 * pairs, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, to, M, N, K, e, status);
-  return cudaGetLastError();
+  cudaError_t err =
+      launch_pdl(kern, dim3(2 * pairs), dim3(kThreads), C::SMEM_BYTES, stream, ta, tb, to, M, N, K, e, status);
+  return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 template <int EPI>

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 // Every bf16 epilogue first multiplies the accumulator by the row scale
 // r = rsqrt(sum(ss_in[row, :]) / ss_dim + ss_eps) when ss_in is given (the
@@ -94,6 +95,25 @@ inline cudaError_t set_smem_limit_once(Kernel kern, int bytes, std::atomic<unsig
   return err;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// its predecessor in the stream finishes, and must call pdl_wait() before it
+// reads anything the predecessor wrote.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 struct GemmF32Args {
   const float* A = nullptr;
   long long lda = 0;
@@ -156,6 +176,28 @@ int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s);
 // Position of every packed token inside its text: pos[t] = t - cu[i] for cu[i] <= t < cu[i+1].
 int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s);
 
+// 3xBF16: f32 rows -> bf16 [rows, 3K] at row stride ldo, mode 0 [hi | hi | lo]
+// (activation side), mode 1 [hi | lo | hi] (weight side); K, ldx, ldo even.
+int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* out, long long ldo, cudaStream_t s);
+// out = a + b (f32 rows; out may alias a or b).
+int add_rows_f32(float* out, long long ldo, const float* a, long long lda, const float* b, long long ldb, int rows,
+                 int cols, cudaStream_t s);
+// out[r, c] = act(gate) * up from x [rows, 2I] f32 whose columns alternate gate / up blocks of blk.
+int act_mul_blocks_f32(const float* x, long long ldx, int rows, int I, int blk, int act, float* out, long long ldo,
+                       cudaStream_t s);
+
+// Sparse compaction of n dense f32 rows of width D: counts[i] = #{v : row_i[v] > 0};
+// *bad set to 1 when a row holds a non-finite value.
+int sparse_count(const float* rows, int n, int D, int* counts, int* bad, cudaStream_t s);
+// idx / val[offsets[i] ..) = the active entries of row i in ascending column order.
+int sparse_compact(const float* rows, int n, int D, const long long* offsets, int32_t* idx, float* val,
+                   cudaStream_t s);
+
+// out[i, :] = in[cu[i + 1] - 1, :] for the n texts (bf16 rows; cols, ld_in and
+// ld_out multiples of 8, rows 16-byte aligned).
+int gather_last_rows_bf16(const void* in, long long ld_in, const int* cu, int n, int cols, void* out,
+                          long long ld_out, cudaStream_t s);
+
 // Dense last-token head: out[i] = L2(RMSNorm(h[cu[i+1]-1])) in f32, L2 = x / sqrt(sum x^2 + 1e-12).
 int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, int n, const float* w, float eps,
                        int H, float* out, cudaStream_t s);
@@ -199,9 +241,13 @@ int rows_l2_f32(const float* x, long long ldx, int rows, int D, float clamp_min,
 int bias_rows_l2_f32(float* x, long long ldx, int rows, int D, const float* bias, int normalize, float clamp_min,
                      cudaStream_t s);
 
-// Segment mean over packed rows: out[i] = mean_{t in text i} x[t] (f32 out) .
-int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, float* out,
-                 cudaStream_t s);
+// Segment mean over packed rows: out[i] = mean_{t in text i} x[t] (f32 out),
+// the mean of each text's rows (f32 out [n, H]) through scratch of
+// segment_mean_scratch_bytes(n, H, max_len) bytes (per-chunk partial sums);
+// H and ldx multiples of 8, x 16-byte aligned.
+size_t segment_mean_scratch_bytes(int n, int H, int max_len);
+int segment_mean(const void* x, int x_bf16, long long ldx, const int* cu, int n, int H, int max_len, float* scratch,
+                 float* out, cudaStream_t s);
 
 // Truncate rows of [n, D] f32 to `dim` and renormalise (Matryoshka); out [n, dim].
 int truncate_normalize(const float* x, int n, int D, int dim, float* out, cudaStream_t s);

@@ -824,6 +824,12 @@ int create_common(const char* config_json, int device, int dtype, inl_model** ou
     delete m;
     return r;
   }
+  // f32 GEMMs on the tensor cores (3xBF16, relative error ~5e-6) except for
+  // the Qwen3.5 late tower: its gated delta rule carries a state from token to
+  // token, and the projections' error grows past the 1e-4 per component that
+  // the reference holds its f32 tower to (crates/inl-late/tests/tiny_golden.rs),
+  // so it keeps the SIMT FFMA GEMMs.
+  m->f32_split3 = m->c.arch != inl::ARCH_QWEN35;
   if (m->c.H % 8 != 0) {
     delete m;
     return fail(INL_ERR_CONFIG, "hidden_size must be a multiple of 8");
@@ -865,7 +871,13 @@ struct Batch {
   int n = 0;
   int T = 0;
   int max_len = 0;
+  int min_len = 0;
   const int32_t* cu_host = nullptr;
+  // Causal last-token pooling reads only each text's last row: the last
+  // layer then runs attention on the query tile holding that row and the o /
+  // MLP projections on the n last rows alone (the row's value does not depend
+  // on the other rows' outputs of that layer).
+  bool last_only = false;
 };
 
 int check_inputs(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b) {
@@ -876,9 +888,11 @@ int check_inputs(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* 
   b.cu_host = cu;
   if (n == 0) return INL_OK;
   if (cu[0] != 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens[0] must be 0");
+  b.min_len = cu[1] - cu[0];
   for (int i = 0; i < n; ++i) {
     const int len = cu[i + 1] - cu[i];
     if (len < 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");
+    b.min_len = std::min(b.min_len, len);
     if (len > m->c.max_pos)
       return fail(INL_ERR_INVALID_INPUT, "text " + std::to_string(i) + " has " + std::to_string(len) +
                                              " tokens; the model accepts at most " + std::to_string(m->c.max_pos));
@@ -948,7 +962,17 @@ int ensure_workspace(inl_model* m, const Batch& b, int n_work) {
   INL_CUDA_TRY(m->cu.ensure((text_cap(b.n) + 1) * 4), "workspace");
   INL_CUDA_TRY(m->work.ensure(static_cast<size_t>(std::max(n_work, 1)) * 8), "workspace");
   if (m->qb_alt) INL_CUDA_TRY(m->work_alt.ensure(static_cast<size_t>(std::max(m->n_work_alt, 1)) * 8), "workspace");
-  const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work + m->n_work_alt) * 8 + 64;
+  if (b.last_only) {
+    // last-row buffers: h [n, H], attention rows [n, hq d], MLP rows [n, I] (bf16),
+    // sums of squares [n, H / 64] (f32); the work list of last tiles and 0..n
+    const size_t n = text_cap(b.n);
+    const size_t parts_l = static_cast<size_t>((c.H + INL_SS_COLS - 1) / INL_SS_COLS);
+    INL_CUDA_TRY(m->lastbuf.ensure(n * (c.H + static_cast<size_t>(c.hq) * c.d + c.I) * 2 + n * parts_l * 4 + 1024),
+                 "workspace");
+    INL_CUDA_TRY(m->work_last.ensure(n * 8 + (n + 1) * 4), "workspace");
+  }
+  const size_t stage = static_cast<size_t>(b.n + 1) * 4 + static_cast<size_t>(n_work + m->n_work_alt) * 8 +
+                       (b.last_only ? static_cast<size_t>(b.n) * 8 + static_cast<size_t>(b.n + 1) * 4 : 0) + 64;
   if (stage > m->h_stage_bytes) {
     const size_t want = std::max({stage * 2, m->h_stage_bytes * 2, size_t(1) << 20});
     if (m->h_stage) {
@@ -991,6 +1015,17 @@ int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch&
   std::vector<std::pair<int, int2>> alt;
   if (m->qb_alt) alt = attention_work(b.cu_host, b.n, m->qb_alt, m->c.causal != 0);
   m->n_work_alt = static_cast<int>(alt.size());
+  // Pruned last layer: the query tile holding each text's last row, heaviest
+  // (most key blocks) first.
+  std::vector<std::pair<int, int2>> last;
+  if (b.last_only) {
+    for (int i = 0; i < b.n; ++i) {
+      const int q = (b.cu_host[i + 1] - b.cu_host[i] - 1) / qb;
+      last.push_back({q, make_int2(i, q)});
+    }
+    std::stable_sort(last.begin(), last.end(), [](const auto& a, const auto& c) { return a.first > c.first; });
+  }
+  m->n_work_last = static_cast<int>(last.size());
   int r = ensure_workspace(m, b, n_work);
   if (r) return r;
   int* cu_stage = m->h_stage;
@@ -998,6 +1033,16 @@ int plan_and_upload(inl_model* m, const uint32_t* ids, int ids_mem, const Batch&
   int2* work_stage = reinterpret_cast<int2*>(cu_stage + ((b.n + 1 + 3) & ~3));
   for (int i = 0; i < n_work; ++i) work_stage[i] = items[i].second;
   for (int i = 0; i < m->n_work_alt; ++i) work_stage[n_work + i] = alt[i].second;
+  if (m->n_work_last > 0) {
+    int2* last_stage = work_stage + n_work + m->n_work_alt;
+    for (int i = 0; i < m->n_work_last; ++i) last_stage[i] = last[i].second;
+    int* iota_stage = reinterpret_cast<int*>(last_stage + m->n_work_last);
+    for (int i = 0; i <= b.n; ++i) iota_stage[i] = i;
+    INL_CUDA_TRY(cudaMemcpyAsync(m->work_last.p, last_stage, static_cast<size_t>(m->n_work_last) * 8 +
+                                                                 static_cast<size_t>(b.n + 1) * 4,
+                                 cudaMemcpyHostToDevice, m->stream),
+                 "work list upload");
+  }
   if (m->n_work_alt > 0)
     INL_CUDA_TRY(cudaMemcpyAsync(m->work_alt.p, work_stage + n_work, static_cast<size_t>(m->n_work_alt) * 8,
                                  cudaMemcpyHostToDevice, m->stream),
@@ -1032,6 +1077,73 @@ cudaEvent_t take_event(inl_model* m) {
 }
 
 // y = x . W^T with the model dtype's GEMM and a fused epilogue.
+// The bf16 [rows, 3K] split of an f32 matrix (mode 1 [hi | lo | hi] for the
+// weight side of a product, mode 0 [hi | hi | lo] for the activation side),
+// made once on the model's stream and kept with the weights.
+const void* split_weight(inl_model* m, const void* w, int rows, int K, int mode) {
+  const uintptr_t key = reinterpret_cast<uintptr_t>(w) | static_cast<uintptr_t>(mode & 1);
+  auto it = m->split_w.find(key);
+  if (it != m->split_w.end()) return it->second;
+  void* p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(rows) * 3 * K * 2) != cudaSuccess) return nullptr;
+  m->allocs.push_back(p);
+  if (inl::split3_bf16(static_cast<const float*>(w), K, rows, K, mode, p, 3LL * K, m->stream) != 0) return nullptr;
+  m->launches++;
+  m->split_w[key] = p;
+  return p;
+}
+
+// An f32 GEMM on the tensor cores: the activations are split into bf16
+// [hi | hi | lo], the weight into [hi | lo | hi], and one bf16 GEMM over
+// K' = 3K accumulates hi.hi + hi.lo + lo.hi in f32 (relative error ~5e-6,
+// against ~2e-3 for a single bf16 product). The residual and gated epilogues
+// then run as f32 passes. Returns -1 where a shape does not fit (the SIMT
+// path runs instead).
+int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int M, int N, int K, int epi, int act,
+                  void* out, long long ldo, const void* resid, long long ldr) {
+  if ((K % 8) || (lda & 1) || (reinterpret_cast<uintptr_t>(A) & 7)) return -1;
+  const void* w3 = split_weight(m, W, N, K, 1);
+  if (!w3) return -3;
+  const long long K3 = 3LL * K;
+  if (m->split_a.ensure(token_cap(M) * K3 * 2) != cudaSuccess) return -3;
+  if (inl::split3_bf16(static_cast<const float*>(A), lda, M, K, 0, m->split_a.p, K3, m->stream)) return -3;
+  m->launches++;
+  const bool plain = epi == INL_EPI_F32 || epi == INL_EPI_BF16;
+  float* dst = static_cast<float*>(out);
+  long long ldd = ldo;
+  if (!plain || (reinterpret_cast<uintptr_t>(out) & 15) || (ldo % 8)) {
+    if (m->split_c.ensure(token_cap(M) * static_cast<size_t>(N) * 4) != cudaSuccess) return -3;
+    dst = m->split_c.as<float>();
+    ldd = N;
+  }
+  inl::GemmArgs g;
+  g.A = m->split_a.as<__nv_bfloat16>();
+  g.lda = K3;
+  g.W = static_cast<const __nv_bfloat16*>(w3);
+  g.ldw = K3;
+  g.M = M;
+  g.N = N;
+  g.K = static_cast<int>(K3);
+  g.epi = INL_EPI_F32;
+  g.out = dst;
+  g.ldo = ldd;
+  g.status = m->d_status;
+  int r = inl::gemm_bf16_tn(g, m->stream);
+  if (r) return r == -1 ? -1 : -3;
+  m->launches++;
+  if (epi == INL_EPI_RESID_BF16) {
+    r = inl::add_rows_f32(static_cast<float*>(out), ldo, static_cast<const float*>(resid), ldr, dst, ldd, M, N,
+                          m->stream);
+  } else if (epi == INL_EPI_GATED_BF16) {
+    r = inl::act_mul_blocks_f32(dst, ldd, M, N / 2, m->gate_block, act, static_cast<float*>(out), ldo, m->stream);
+  } else if (dst != out) {
+    r = cudaMemcpy2DAsync(out, ldo * 4, dst, ldd * 4, static_cast<size_t>(N) * 4, M, cudaMemcpyDeviceToDevice,
+                          m->stream) == cudaSuccess ? 0 : -3;
+  }
+  if (!plain || dst != out) m->launches++;
+  return r;
+}
+
 int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int N, int K, int epi, int act,
            void* out, long long ldo, const void* resid, long long ldr, int kind) {
   ProfileRec rec{};
@@ -1062,6 +1174,9 @@ int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int
     g.status = m->d_status;
     r = inl::gemm_bf16_tn(g, m->stream);
   } else {
+    r = m->f32_split3 ? linear_split3(m, A, lda, W, M, N, K, epi, act, out, ldo, resid, ldr) : -1;
+  }
+  if (r == -1 && m->dtype != INL_DTYPE_BF16) {
     inl::GemmF32Args g;
     g.A = static_cast<const float*>(A);
     g.lda = lda;
@@ -1129,6 +1244,75 @@ int gemm(inl_model* m, inl::GemmArgs g, int kind) {
   return r;
 }
 
+// The pruned last layer after its attention: the n last rows of the
+// attention output and of h are gathered, then the o projection (residual,
+// sums of squares for the folded norm), gate/up and down run on those rows
+// alone. The result is h's last rows, [n, H] at the start of lastbuf.
+int qwen3_last_rows(inl_model* m, const Batch& b, const inl::LayerWeights& w) {
+  const ModelConfig& c = m->c;
+  const size_t ncap = text_cap(b.n);
+  const int q_out = c.hq * c.d;
+  const int parts = (c.H + INL_SS_COLS - 1) / INL_SS_COLS;
+  cudaStream_t s = m->stream;
+  auto* base = static_cast<uint8_t*>(m->lastbuf.p);
+  auto* h_last = reinterpret_cast<__nv_bfloat16*>(base);
+  auto* a_last = reinterpret_cast<__nv_bfloat16*>(base + ncap * c.H * 2);
+  auto* inter = reinterpret_cast<__nv_bfloat16*>(base + ncap * (c.H + q_out) * 2);
+  auto* ss_last = reinterpret_cast<float*>(base + ncap * (c.H + q_out + c.I) * 2);
+  INL_K_TRY(inl::gather_last_rows_bf16(m->attn.p, q_out, m->cu.as<int>(), b.n, q_out, a_last, q_out, s),
+            "gather attention rows");
+  INL_K_TRY(inl::gather_last_rows_bf16(m->h.p, c.H, m->cu.as<int>(), b.n, c.H, h_last, c.H, s), "gather rows");
+  m->launches += 2;
+
+  inl::GemmArgs o;
+  o.A = a_last;
+  o.lda = q_out;
+  o.W = static_cast<const __nv_bfloat16*>(w.wo);
+  o.M = b.n;
+  o.N = c.H;
+  o.K = q_out;
+  o.epi = INL_EPI_RESID_BF16;
+  o.out = h_last;
+  o.ldo = c.H;
+  o.resid = h_last;
+  o.ldr = c.H;
+  o.ss_out = ss_last;
+  INL_K_TRY(gemm(m, o, 1), "o projection");
+
+  inl::GemmArgs gu;
+  gu.A = h_last;
+  gu.lda = c.H;
+  gu.W = static_cast<const __nv_bfloat16*>(w.wgu);
+  gu.M = b.n;
+  gu.N = 2 * c.I;
+  gu.K = c.H;
+  gu.epi = INL_EPI_GATED_BF16;
+  gu.act = INL_ACT_SILU;
+  gu.out = inter;
+  gu.ldo = c.I;
+  gu.ss_in = ss_last;
+  gu.ss_in_parts = parts;
+  gu.ss_dim = c.H;
+  gu.ss_eps = c.eps;
+  INL_K_TRY(gemm(m, gu, 2), "gate/up projection");
+
+  inl::GemmArgs dn;
+  dn.A = inter;
+  dn.lda = c.I;
+  dn.W = static_cast<const __nv_bfloat16*>(w.wd);
+  dn.M = b.n;
+  dn.N = c.H;
+  dn.K = c.I;
+  dn.epi = INL_EPI_RESID_BF16;
+  dn.out = h_last;
+  dn.ldo = c.H;
+  dn.resid = h_last;
+  dn.ldr = c.H;
+  dn.ss_out = ss_last;
+  INL_K_TRY(gemm(m, dn, 3), "down projection");
+  return INL_OK;
+}
+
 // Fused bf16 layer stack: 4 GEMMs + attention per layer. The input RMSNorms
 // are folded (weights scaled by the norm weight at load, row scale from the
 // sums of squares the previous residual epilogue wrote); q/k RMSNorm + RoPE
@@ -1146,6 +1330,7 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
   const __nv_bfloat16* h = m->h.as<__nv_bfloat16>();
   for (int l = 0; l < c.layers; ++l) {
     const inl::LayerWeights& w = m->layers[l];
+    const bool pruned = b.last_only && l == c.layers - 1;
     inl::GemmArgs g;
     g.A = h;
     g.lda = c.H;
@@ -1188,13 +1373,17 @@ int qwen3_tower_fused(inl_model* m, const Batch& b, int n_work) {
     aa.window = -1;
     aa.cu = m->cu.as<int>();
     aa.n = b.n;
-    aa.work = m->work.as<int2>();
-    aa.n_work = n_work;
+    aa.work = pruned ? m->work_last.as<int2>() : m->work.as<int2>();
+    aa.n_work = pruned ? m->n_work_last : n_work;
     aa.q_block = inl::attention_q_block(1, c.d);
     aa.total_rows = T;
     aa.status = m->d_status;
     INL_K_TRY(run_attention(m, aa, s), "attention");
     m->launches++;
+    if (pruned) {
+      INL_K_TRY(qwen3_last_rows(m, b, w), "last-row projections");
+      break;
+    }
 
     inl::GemmArgs o;
     o.A = m->attn.as<__nv_bfloat16>();
@@ -1618,9 +1807,12 @@ int qwen35_tower(inl_model* m, const Batch& b, int n_work) {
   return INL_OK;
 }
 
-int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b) {
+int run_tower(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu, int n, Batch& b,
+              bool last_token_pooling = false) {
   int r = check_inputs(m, ids, ids_mem, cu, n, b);
   if (r) return r;
+  b.last_only = last_token_pooling && m->prune_last && m->fused && m->c.arch == inl::ARCH_QWEN3 && m->c.causal &&
+                b.n > 0 && b.min_len > 0;
   INL_CUDA_TRY(cudaSetDevice(m->device), "cudaSetDevice");
   int n_work = 0;
   if ((r = plan_and_upload(m, ids, ids_mem, b, &n_work))) return r;
@@ -1795,7 +1987,7 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
   if (c.arch == inl::ARCH_QWEN35)
     return fail(INL_ERR_CONFIG, "a Qwen3.5 late tower has no pooled dense head (use forward_multivector)");
   Batch b;
-  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b, c.arch == inl::ARCH_QWEN3);
   if (r) return r;
   if (b.n == 0) return INL_OK;
   if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
@@ -1812,26 +2004,36 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
     INL_CUDA_TRY(m->head_buf.ensure(text_cap(b.n) * widest * 4), "pooling buffer");
     INL_K_TRY(inl::rms_norm(m->h.p, bf, c.H, m->final_norm, c.eps, b.T, c.H, m->xn.p, bf, c.H, m->stream),
               "final norm");
-    INL_K_TRY(inl::segment_mean(m->xn.p, bf, c.H, m->cu.as<int>(), b.n, c.H, m->pooled.as<float>(), m->stream),
+    INL_CUDA_TRY(m->seg_scratch.ensure(inl::segment_mean_scratch_bytes(b.n, c.H, b.max_len)), "pooling buffer");
+    INL_K_TRY(inl::segment_mean(m->xn.p, bf, c.H, m->cu.as<int>(), b.n, c.H, b.max_len, m->seg_scratch.as<float>(),
+                                m->pooled.as<float>(), m->stream),
               "mean pooling");
-    m->launches += 2;
+    m->launches += 3;
     float* cur = m->pooled.as<float>();
     float* nxt = m->head_buf.as<float>();
     int in = c.H;
     for (size_t j = 0; j < m->dense_chain.size(); ++j) {
-      inl::GemmF32Args g;
-      g.A = cur;
-      g.lda = in;
-      g.W = m->dense_chain[j];
-      g.ldw = in;
-      g.M = b.n;
-      g.N = c.dense_dims[j];
-      g.K = in;
-      g.epi = INL_EPI_F32;
-      g.out = nxt;
-      g.ldo = c.dense_dims[j];
-      INL_K_TRY(inl::gemm_f32_tn(g, m->stream), "dense head");
-      m->launches++;
+      // f32 pooled rows through the f32 dense chain: 3xBF16 on the tensor
+      // cores where it applies, the SIMT f32 GEMM otherwise
+      int dr = m->f32_split3 ? linear_split3(m, cur, in, m->dense_chain[j], b.n, c.dense_dims[j], in, INL_EPI_F32, 0,
+                                             nxt, c.dense_dims[j], nullptr, 0)
+                             : -1;
+      if (dr == -1) {
+        inl::GemmF32Args g;
+        g.A = cur;
+        g.lda = in;
+        g.W = m->dense_chain[j];
+        g.ldw = in;
+        g.M = b.n;
+        g.N = c.dense_dims[j];
+        g.K = in;
+        g.epi = INL_EPI_F32;
+        g.out = nxt;
+        g.ldo = c.dense_dims[j];
+        dr = inl::gemm_f32_tn(g, m->stream);
+        m->launches++;
+      }
+      INL_K_TRY(dr, "dense head");
       std::swap(cur, nxt);
       in = c.dense_dims[j];
     }
@@ -1850,9 +2052,17 @@ int inl_cuda_forward_dense(inl_model* m, const uint32_t* ids, int ids_mem, const
   }
   const size_t bytes = static_cast<size_t>(b.n) * c.H * 4;
   INL_CUDA_TRY(m->out.ensure(text_cap(b.n) * c.H * 4), "output buffer");
-  INL_K_TRY(inl::last_token_norm_l2(m->h.p, bf, c.H, m->cu.as<int>(), b.n, m->final_norm, c.eps, c.H,
-                                    m->out.as<float>(), m->stream),
-            "last-token pooling");
+  if (b.last_only) {
+    // the pruned last layer left each text's last row at row i of lastbuf
+    const int* iota = reinterpret_cast<const int*>(m->work_last.as<int2>() + m->n_work_last);
+    INL_K_TRY(inl::last_token_norm_l2(m->lastbuf.p, bf, c.H, iota, b.n, m->final_norm, c.eps, c.H,
+                                      m->out.as<float>(), m->stream),
+              "last-token pooling");
+  } else {
+    INL_K_TRY(inl::last_token_norm_l2(m->h.p, bf, c.H, m->cu.as<int>(), b.n, m->final_norm, c.eps, c.H,
+                                      m->out.as<float>(), m->stream),
+              "last-token pooling");
+  }
   m->launches++;
   return finish(m, m->out.p, bytes, out, out_mem);
 }
@@ -1892,16 +2102,18 @@ int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int ids_mem,
   return finish(m, m->out.p, bytes, out, out_mem);
 }
 
-int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
-                            float* out, int out_mem) {
-  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+}  // extern "C"
+
+namespace {
+
+// The SPLADE forward up to the dense term-weight rows [n, sparse_dim] f32 in
+// m->out (device); b describes the batch.
+int sparse_rows(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts, Batch& b) {
   const ModelConfig& c = m->c;
   if (c.arch != inl::ARCH_MODERNBERT) return fail(INL_ERR_CONFIG, "this model has no SPLADE head");
-  Batch b;
   int r = run_tower(m, ids, ids_mem, cu_seqlens, n_texts, b);
   if (r) return r;
   if (b.n == 0) return INL_OK;
-  if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
   const int bf = m->dtype == INL_DTYPE_BF16;
   const int H = c.H, V = c.V, n = b.n;
   cudaStream_t s = m->stream;
@@ -1965,19 +2177,117 @@ int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, cons
       g.ldp = V;
       INL_K_TRY(gemm(m, g, 6), "decoder");
     } else {
-      INL_K_TRY(inl::gemm_f32_segmax(m->xn.as<float>(), H, static_cast<const float*>(m->embed), H, Ts, V, H,
-                                     m->speak_seg.as<int>(), m->pooled_i.as<int>(), V, s),
-                "decoder");
-      m->launches++;
+      // f32: the tied table split as the activation side [hi | hi | lo] (rows =
+      // vocabulary), the speaking rows as the weight side [hi | lo | hi], one
+      // bf16 SEGMAX GEMM over K' = 3H; or the SIMT f32 SEGMAX GEMM.
+      const void* t3 = m->f32_split3 && (H % 8) == 0 ? split_weight(m, m->embed, V, H, 0) : nullptr;
+      if (t3) {
+        INL_CUDA_TRY(m->split_a.ensure(token_cap(Ts) * 3 * static_cast<size_t>(H) * 2), "split buffer");
+        INL_K_TRY(inl::split3_bf16(m->xn.as<float>(), H, Ts, H, 1, m->split_a.p, 3LL * H, s), "split");
+        m->launches++;
+        inl::GemmArgs g;
+        g.A = static_cast<const __nv_bfloat16*>(t3);
+        g.lda = 3LL * H;
+        g.W = m->split_a.as<__nv_bfloat16>();
+        g.ldw = 3LL * H;
+        g.M = V;
+        g.N = Ts;
+        g.K = 3 * H;
+        g.epi = INL_EPI_SEGMAX;
+        g.seg = m->speak_seg.as<int>();
+        g.pooled = m->pooled_i.as<int>();
+        g.ldp = V;
+        INL_K_TRY(gemm(m, g, 6), "decoder");
+      } else {
+        INL_K_TRY(inl::gemm_f32_segmax(m->xn.as<float>(), H, static_cast<const float*>(m->embed), H, Ts, V, H,
+                                       m->speak_seg.as<int>(), m->pooled_i.as<int>(), V, s),
+                  "decoder");
+        m->launches++;
+      }
     }
   }
-  const size_t bytes = static_cast<size_t>(n) * m->sparse_dim * 4;
   INL_CUDA_TRY(m->out.ensure(text_cap(n) * m->sparse_dim * 4), "output buffer");
   INL_K_TRY(inl::splade_finish(m->pooled_i.as<int>(), n, V, m->decoder_bias, c.logit_shift, m->open_mask, m->canon,
                                m->sparse_dim, m->out.as<float>(), s),
             "splade finish");
   m->launches++;
-  return finish(m, m->out.p, bytes, out, out_mem);
+  return INL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
+                            float* out, int out_mem) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  Batch b;
+  int r = sparse_rows(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.n == 0) return INL_OK;
+  if (!out) return fail(INL_ERR_INVALID_INPUT, "out is NULL");
+  return finish(m, m->out.p, static_cast<size_t>(b.n) * m->sparse_dim * 4, out, out_mem);
+}
+
+int inl_cuda_forward_sparse_compact(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens,
+                                    int n_texts, int64_t* offsets, int32_t* indices, float* values, int64_t capacity,
+                                    int out_mem) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  if (out_mem != INL_MEM_HOST && out_mem != INL_MEM_DEVICE) return fail(INL_ERR_INVALID_INPUT, "bad out_mem");
+  if (n_texts > 0 && !offsets) return fail(INL_ERR_INVALID_INPUT, "offsets is NULL");
+  Batch b;
+  int r = sparse_rows(m, ids, ids_mem, cu_seqlens, n_texts, b);
+  if (r) return r;
+  if (b.n == 0) {
+    if (offsets) offsets[0] = 0;
+    return INL_OK;
+  }
+  const int n = b.n, D = m->sparse_dim;
+  cudaStream_t s = m->stream;
+  // pass 1: active terms per row (and a flag for non-finite weights)
+  INL_CUDA_TRY(m->compact_meta.ensure((text_cap(n) + 1) * 8 + 64), "compaction buffer");
+  int* d_counts = m->compact_meta.as<int>();
+  int* d_bad = d_counts + n;  // read back with the counts
+  INL_CUDA_TRY(cudaMemsetAsync(d_bad, 0, sizeof(int), s), "compaction");
+  INL_K_TRY(inl::sparse_count(m->out.as<float>(), n, D, d_counts, d_bad, s), "sparse count");
+  m->launches++;
+  std::vector<int> counts(n + 1);
+  INL_CUDA_TRY(cudaMemcpyAsync(counts.data(), d_counts, static_cast<size_t>(n + 1) * 4, cudaMemcpyDeviceToHost, s),
+               "count read");
+  r = finish(m, nullptr, 0, nullptr, INL_MEM_HOST);  // drains the stream, checks the device status word
+  if (r) return r;
+  if (counts[n] != 0)  // crates/inl-sparse/src/native.rs:536-540
+    return fail(INL_ERR_INFERENCE, "non-finite SPLADE term weight");
+  offsets[0] = 0;
+  for (int i = 0; i < n; ++i) offsets[i + 1] = offsets[i] + counts[i];
+  const int64_t total = offsets[n];
+  if (total > capacity)
+    return fail(INL_ERR_INVALID_INPUT, "the batch has " + std::to_string(total) + " active terms; capacity is " +
+                                           std::to_string(capacity) + " (offsets[n_texts] holds the size needed)");
+  if (total == 0) return INL_OK;
+  if (!indices || !values) return fail(INL_ERR_INVALID_INPUT, "indices / values is NULL");
+  // pass 2: every row's active terms in ascending term order at its offset
+  INL_CUDA_TRY(m->compact_off.ensure((text_cap(n) + 1) * 8), "compaction buffer");
+  INL_CUDA_TRY(cudaMemcpyAsync(m->compact_off.p, offsets, static_cast<size_t>(n + 1) * 8, cudaMemcpyHostToDevice, s),
+               "offsets upload");
+  int32_t* d_idx = indices;
+  float* d_val = values;
+  if (out_mem == INL_MEM_HOST) {
+    INL_CUDA_TRY(m->compact_idx.ensure(static_cast<size_t>(total) * 4), "compaction buffer");
+    INL_CUDA_TRY(m->compact_val.ensure(static_cast<size_t>(total) * 4), "compaction buffer");
+    d_idx = m->compact_idx.as<int32_t>();
+    d_val = m->compact_val.as<float>();
+  }
+  INL_K_TRY(inl::sparse_compact(m->out.as<float>(), n, D, m->compact_off.as<long long>(), d_idx, d_val, s),
+            "sparse compaction");
+  m->launches++;
+  if (out_mem == INL_MEM_HOST) {
+    INL_CUDA_TRY(cudaMemcpyAsync(indices, d_idx, static_cast<size_t>(total) * 4, cudaMemcpyDeviceToHost, s),
+                 "result copy");
+    INL_CUDA_TRY(cudaMemcpyAsync(values, d_val, static_cast<size_t>(total) * 4, cudaMemcpyDeviceToHost, s),
+                 "result copy");
+  }
+  return finish(m, nullptr, 0, nullptr, INL_MEM_HOST);
 }
 
 int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
@@ -2060,6 +2370,19 @@ int inl_cuda_device_count(void) {
 const char* inl_cuda_version(void) { return "inl_cuda 0.1.0 (sm_100a)"; }
 
 // ---------------------------------------------------------------- profiling
+int inl_cuda_model_set_f32_gemm(inl_model* m, int mode) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  if (mode != 0 && mode != 1) return fail(INL_ERR_CONFIG, "f32 GEMM mode is 0 (SIMT FFMA) or 1 (3xBF16)");
+  m->f32_split3 = mode == 1;
+  return INL_OK;
+}
+
+int inl_cuda_model_set_prune_last(inl_model* m, int enable) {
+  if (!m) return fail(INL_ERR_CONFIG, "NULL model");
+  m->prune_last = enable != 0;
+  return INL_OK;
+}
+
 int inl_cuda_model_set_profiling(inl_model* m, int enable) {
   if (!m) return fail(INL_ERR_CONFIG, "NULL model");
   cudaStreamSynchronize(m->stream);
@@ -2267,6 +2590,8 @@ int inl_cuda_attention(const void* q, const void* k, const void* v, int64_t ldq,
   if (n_texts <= 0) return INL_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int qb = inl::attention_q_block(dtype == INL_DTYPE_BF16, d);
+  if (!cu_seqlens_host) return fail(INL_ERR_CONFIG, "NULL cu_seqlens");
+  if (cu_seqlens_host[0] != 0) return fail(INL_ERR_INVALID_INPUT, "cu_seqlens[0] must be 0");
   for (int i = 0; i < n_texts; ++i)
     if (cu_seqlens_host[i + 1] < cu_seqlens_host[i])
       return fail(INL_ERR_INVALID_INPUT, "cu_seqlens must be non-decreasing");

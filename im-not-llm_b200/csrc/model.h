@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <map>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/inl_cuda.h"
@@ -179,6 +180,18 @@ struct inl_model {
   // workspaces
   inl::DevBuf h, xn, qkv, attn, ids, cu, pos, work, out, pooled, tmp;
   inl::DevBuf ple_in;  // [T, layers * ple] per-layer inputs of the batch
+  // Pruned last layer of causal last-token pooling: the last rows' buffers,
+  // the work list of the query tiles holding them, then 0..n.
+  inl::DevBuf compact_meta, compact_off, compact_idx, compact_val;  // sparse compaction
+  // f32 models: GEMMs as one bf16 tensor-core GEMM over K' = 3K (3xBF16) when
+  // on; the split [hi | lo | hi] copy of each f32 weight is made on first use.
+  bool f32_split3 = true;
+  std::unordered_map<uintptr_t, void*> split_w;
+  inl::DevBuf split_a, split_c;
+  inl::DevBuf seg_scratch;  // mean pooling's per-chunk partial sums
+  inl::DevBuf lastbuf, work_last;
+  int n_work_last = 0;
+  bool prune_last = true;  // off: every layer runs on every row (tests compare the two)
   // Attention work list for layers whose head_dim takes another query block
   // than c.d's (per-layer head shapes); n_work_alt = 0 when every layer shares one.
   inl::DevBuf work_alt;

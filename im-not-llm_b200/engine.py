@@ -28,6 +28,7 @@ import dataclasses
 import json
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Callable, Sequence
@@ -547,6 +548,20 @@ class SparseVector:
         return len(self.indices)
 
 
+def _sparse_forward(model, ids, cu) -> list[SparseVector]:
+    """One batch of SPLADE vectors: the active terms are compacted on the
+    device (ascending term ids, weights > 0) and only they cross to the host.
+    A non-finite weight is an inference error, as in the reference
+    (crates/inl-sparse/src/native.rs:536-540)."""
+    try:
+        pairs = model.encode_sparse_compact(ids, cu)
+    except InlError as e:
+        if "non-finite" in str(e):
+            raise InlError.inference("native sparse encoder produced non-finite weights") from e
+        raise
+    return [SparseVector(idx, val) for idx, val in pairs]
+
+
 class SparseEncoder(_EngineBase):
     """SparseEngine over a ModernBERT + SPLADE CudaModel."""
 
@@ -603,13 +618,7 @@ class SparseEncoder(_EngineBase):
         return out[0]
 
     def _encode(self, texts: list[np.ndarray]) -> list[SparseVector]:
-        def forward(model: CudaModel, ids, cu):
-            dense = model.encode_sparse(ids, cu)
-            if not np.all(np.isfinite(dense)):  # crates/inl-sparse/src/native.rs:536-540
-                raise InlError.inference("native sparse encoder produced non-finite weights")
-            return [SparseVector.from_dense(row) for row in dense]
-
-        return self._run_batches("native sparse", texts, forward)
+        return self._run_batches("native sparse", texts, _sparse_forward)
 
 
 class DataParallelEmbedder:
@@ -655,14 +664,21 @@ class DataParallelEmbedder:
         errors: list = []
 
         def worker(w: int):
+            # The next batch is packed on a helper thread while this one runs:
+            # the forward call releases the GIL for its whole duration.
             try:
-                for b in plan[w]:
-                    ids, cu = pack(texts, batches[b])
-                    out = forward(self.models[w], ids, cu)
-                    if len(out) != len(batches[b]):  # crates/inl-text/src/native.rs:674-679
-                        raise InlError.inference(f"{what} returned {len(out)} results for {len(batches[b])} inputs")
-                    for i, v in zip(batches[b], out):
-                        results[i] = v
+                mine = plan[w]
+                with ThreadPoolExecutor(max_workers=1) as packer:
+                    nxt = packer.submit(pack, texts, batches[mine[0]]) if mine else None
+                    for k, b in enumerate(mine):
+                        ids, cu = nxt.result()
+                        if k + 1 < len(mine):
+                            nxt = packer.submit(pack, texts, batches[mine[k + 1]])
+                        out = forward(self.models[w], ids, cu)
+                        if len(out) != len(batches[b]):  # crates/inl-text/src/native.rs:674-679
+                            raise InlError.inference(f"{what} returned {len(out)} results for {len(batches[b])} inputs")
+                        for i, v in zip(batches[b], out):
+                            results[i] = v
             except BaseException as e:
                 errors.append(e)
 
@@ -686,13 +702,7 @@ class DataParallelEmbedder:
         (crates/inl-sparse/src/native.rs:536-540)."""
         texts = self._texts(inputs, self.passage_prefix, self.max_length)
 
-        def forward(m, ids, cu):
-            dense = m.encode_sparse(ids, cu)
-            if not np.all(np.isfinite(dense)):
-                raise InlError.inference("native sparse encoder produced non-finite weights")
-            return [SparseVector.from_dense(row) for row in dense]
-
-        return self._run("native sparse", texts, forward)
+        return self._run("native sparse", texts, _sparse_forward)
 
     def encode_late(self, inputs: Sequence, task: LateTask | None = None) -> list[np.ndarray]:
         """Per-token vectors for one late task: its prompt in front, the ids

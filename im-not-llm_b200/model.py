@@ -128,6 +128,23 @@ class CudaModel:
                 "sparse forward")
         return out
 
+    def encode_sparse_compact(self, ids, cu_seqlens) -> list[tuple[np.ndarray, np.ndarray]]:
+        """SPLADE terms compacted on the device: per text, (indices uint32
+        ascending, weights f32) of its active terms (weight > 0). Only the
+        active terms are copied to the host."""
+        ids, ids_mem, cu = self._inputs(ids, cu_seqlens)
+        n = len(cu) - 1
+        offsets = np.zeros(n + 1, dtype=np.int64)
+        cap = max(n * self.info()["sparse_dim"], 1)  # upper bound: every term of every text
+        idx = np.empty(cap, dtype=np.int32)
+        val = np.empty(cap, dtype=np.float32)
+        iptr = ids if isinstance(ids, int) else ids.ctypes.data
+        N.check(N.lib().inl_cuda_forward_sparse_compact(self.handle, iptr, ids_mem, cu.ctypes.data, n,
+                                                        offsets.ctypes.data, idx.ctypes.data, val.ctypes.data, cap,
+                                                        N.INL_MEM_HOST), "sparse forward")
+        return [(idx[offsets[i]:offsets[i + 1]].astype(np.uint32), val[offsets[i]:offsets[i + 1]].copy())
+                for i in range(n)]
+
     def encode_multivector(self, ids, cu_seqlens, out=None) -> np.ndarray | int:
         """Per-token late-interaction vectors [T, out_features] f32."""
         ids, ids_mem, cu = self._inputs(ids, cu_seqlens)
@@ -151,6 +168,17 @@ class CudaModel:
         N.check(N.lib().inl_cuda_forward_hidden(self.handle, iptr, ids_mem, cu.ctypes.data, n,
                                                 1 if normalize_final else 0, optr, omem), "hidden forward")
         return out
+
+    def set_f32_gemm(self, mode: str) -> None:
+        """f32 models: "3xbf16" (default) runs the contractions on the tensor
+        cores over split bf16 operands; "ffma" on the SIMT f32 kernels."""
+        N.check(N.lib().inl_cuda_model_set_f32_gemm(self.handle, {"ffma": 0, "3xbf16": 1}[mode]), "f32 GEMM mode")
+
+    def set_prune_last(self, enable: bool) -> None:
+        """Causal last-token pooling runs the last layer's attention, o and
+        MLP only where the pooled row needs them (default on); off runs that
+        layer on every row."""
+        N.check(N.lib().inl_cuda_model_set_prune_last(self.handle, 1 if enable else 0), "prune_last")
 
     # ----------------------------------------------------------- measurement
     def set_profiling(self, enable: bool) -> None:

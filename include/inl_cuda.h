@@ -134,6 +134,21 @@ INL_API int inl_cuda_forward_multivector(inl_model* m, const uint32_t* ids, int 
 INL_API int inl_cuda_forward_sparse(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens, int n_texts,
                             float* out, int out_mem);
 
+/* SPLADE term weights as sparse vectors, compacted on the device: text i's
+ * active terms (weight > 0) are indices[offsets[i] .. offsets[i + 1]) in
+ * ascending term order with their weights in values[...], the pairs of the
+ * reference's SparseVector (crates/inl-sparse/src/lib.rs:51-62), which its
+ * encoder builds from the dense rows (crates/inl-sparse/src/native.rs:516-545).
+ * offsets (n_texts + 1 entries, host memory) are always written; when
+ * offsets[n_texts] exceeds capacity nothing else is written and the call
+ * returns INL_ERR_INVALID_INPUT (call again with a capacity of at least
+ * offsets[n_texts]). A non-finite weight is INL_ERR_INFERENCE, as the
+ * reference's encoder refuses one (native.rs:536-540). indices and values are
+ * host or device memory (out_mem); only the active terms cross to the host. */
+INL_API int inl_cuda_forward_sparse_compact(inl_model* m, const uint32_t* ids, int ids_mem, const int32_t* cu_seqlens,
+                                    int n_texts, int64_t* offsets, int32_t* indices, float* values,
+                                    int64_t capacity, int out_mem);
+
 /* Final hidden states [total_tokens, hidden] f32 before any pooling head
  * (after the tower's final norm when normalize_final != 0). For tests and
  * custom heads; the reference exposes the same tensor inside forward_last /

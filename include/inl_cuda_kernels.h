@@ -182,6 +182,25 @@ INL_API int inl_cuda_gated_delta_rule(const float* mixed, int64_t ld_mixed, cons
 INL_API int inl_cuda_model_set_profiling(inl_model* m, int enable);
 INL_API int inl_cuda_model_profile(inl_model* m, int kind, int* launches, double* total_ms, double* flops);
 
+/* f32 models' contractions: mode 1 (default) runs each as one bf16 tcgen05
+ * GEMM over K' = 3K on split operands, [hi | hi | lo] . [hi | lo | hi] with
+ * hi = bf16(x), lo = bf16(x - hi), accumulated in f32 (3xBF16: relative error
+ * ~5e-6 per product sum); mode 0 runs them on the SIMT FFMA kernels, the
+ * default for the Qwen3.5 late tower (its gated delta rule carries a state
+ * from token to token, which grows that error past the reference's 1e-4
+ * per component for this tower). The
+ * reference runs f32 on cuBLAS SGEMM and found single-pass TF32 too coarse
+ * for its sparse golden (docs/DEVICES.md:371-379). */
+INL_API int inl_cuda_model_set_f32_gemm(inl_model* m, int mode);
+
+/* Causal last-token pooling (Qwen3 dense, bf16): by default the last layer
+ * runs attention on the query tile holding each text's last row and the o /
+ * MLP projections on the n last rows only, as the pooled vector needs
+ * nothing else. enable = 0 runs that layer on every row (the embeddings are
+ * the same function; tests compare the two). The reference computes every
+ * row (crates/inl-text/src/qwen3/mod.rs:339-358 narrows after the stack). */
+INL_API int inl_cuda_model_set_prune_last(inl_model* m, int enable);
+
 /* Kernel launches issued by the model since the last reset. */
 INL_API long long inl_cuda_model_launch_count(inl_model* m, int reset);
 

@@ -303,17 +303,19 @@ def test_gemm_qkv_epilogue(gpu, d, hq, hkv):
         assert err < 1e-2, (name, err)
 
 
-@pytest.mark.parametrize("causal,window", [(1, -1), (0, -1), (0, 300)])
-def test_attention_long_texts(gpu, causal, window):
-    """Several 128-key blocks per query tile, GQA 16/8, head_dim 128 (the
-    Qwen3-0.6B shape), texts up to 2048 tokens."""
+@pytest.mark.parametrize("d,hq,hkv,causal,window", [(128, 16, 8, 1, -1), (128, 16, 8, 0, -1), (128, 16, 8, 0, 300),
+                                                    (256, 3, 1, 0, 512), (256, 3, 1, 0, -1), (64, 12, 12, 1, -1)])
+def test_attention_long_texts(gpu, d, hq, hkv, causal, window):
+    """Several 128-key blocks per query tile, texts up to 2048 tokens: GQA
+    16/8 x 128 (Qwen3-0.6B), 3/1 x 256 with and without the 512 window
+    (the EmbeddingGemma-style config), 12 x 64 causal."""
     import torch
 
     N_ = _lib()
     lengths = [2048, 1537, 129, 5]
     cu = np.zeros(len(lengths) + 1, dtype=np.int32)
     np.cumsum(lengths, out=cu[1:])
-    T, hq, hkv, d = int(cu[-1]), 16, 8, 128
+    T = int(cu[-1])
     g = torch.Generator(device="cuda").manual_seed(7)
     qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", generator=g).to(torch.bfloat16)
     q, k, v = qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:]

@@ -1,8 +1,10 @@
 """Model-level parity of the Qwen3 tower through the C ABI against the CPU
-oracle (oracle/qwen3.py), on the same seeded weights and inputs.
+oracle (oracle/qwen3.py, and its torch-CPU restatement oracle/qwen3_torch.py
+for the full-size cases), on the same seeded weights and inputs.
 
 Tolerances: f32 cosine >= 0.99999 per vector;
-bf16 cosine >= 0.999 per vector; late-interaction bf16 per-token cosine >= 0.999.
+bf16 cosine >= 0.999 per vector; late-interaction per-token cosine >= 0.9999
+in f32 and >= 0.999 in bf16.
 """
 import numpy as np
 import pytest
@@ -15,6 +17,7 @@ pytestmark = pytest.mark.gpu
 
 F32_COS = 0.99999
 BF16_COS = 0.999
+LATE_F32_COS = 0.9999
 
 
 def _tiny(cfg, scale=5.0):
@@ -135,45 +138,148 @@ def test_config1_full_size(gpu, qwen3_full, dtype, floor):
     assert cos.min() >= floor, cos
 
 
+@pytest.fixture(scope="module")
+def qwen3_cpu(qwen3_full):
+    from oracle import qwen3_torch as QT
+
+    cfg, w = qwen3_full
+    return QT.Qwen3Cpu(w, cfg)
+
+
 @pytest.mark.slow
-def test_config3_late_full_size_subset(gpu, qwen3_full):
-    """Config 3 tower + head (bidirectional, 1024->128, per-token L2) on the first
-    8 of its 64 x 512 texts (the oracle's cost bound); bf16 per-token cosine."""
+def test_config3_late_full_size_all_texts_bf16(gpu, qwen3_full, qwen3_cpu):
+    """Config 3 tower + head (bidirectional, 1024->128, per-token L2) on all
+    64 of its 512-token texts in one packed forward (32768 token vectors);
+    bf16 per-token cosine."""
     cfg, w = qwen3_full
     cfg = dict(cfg, is_causal=False)
     ids, cu = inl.synthetic.cfg3_inputs()
-    ids, cu = ids[: cu[8]], cu[:9]
     proj = inl.synthetic.late_projection(cfg)
-    ref = Q.encode_late(w, cfg, proj, ids, cu)
+    ref = qwen3_cpu.encode_late(proj, ids, cu)
     m = inl.CudaModel(cfg, w, dtype="bf16")
     m.set_dense_head(proj)
     got = m.encode_multivector(ids, cu)
     m.close()
+    assert got.shape == ref.shape == (64 * 512, 128)
     cos = cosine_rows(got, ref)
     assert cos.min() >= BF16_COS, cos.min()
 
 
 @pytest.mark.slow
-def test_config5_batch_properties(gpu, qwen3_full):
-    """A full ~64k-token packed batch of the config-5 corpus: finite unit
-    vectors, short texts match the oracle computed alone, and embedding a text
-    alone equals embedding it inside the packed batch."""
+def test_config3_late_full_size_f32(gpu, qwen3_full, qwen3_cpu):
+    """Config 3 in f32 at the full architecture on 8 of its texts: every
+    token vector at the late-interaction f32 floor (cosine >= 0.9999)."""
     cfg, w = qwen3_full
-    lengths, ids = inl.synthetic.cfg5_corpus(n_texts=2048)
-    order = inl.planner.longest_first(lengths)
-    texts_all = np.split(ids, np.cumsum(lengths)[:-1])
-    batch = [order[k] for k in inl.planner.plan_packed([lengths[i] for i in order], 65536)[0]]
-    pids, pcu = inl.planner.pack(texts_all, batch)
+    cfg = dict(cfg, is_causal=False)
+    ids, cu = inl.synthetic.cfg3_inputs()
+    ids, cu = ids[: cu[8]], cu[:9]
+    proj = inl.synthetic.late_projection(cfg)
+    ref = qwen3_cpu.encode_late(proj, ids, cu)
+    m = inl.CudaModel(cfg, w, dtype="f32")
+    m.set_dense_head(proj)
+    got = m.encode_multivector(ids, cu)
+    m.close()
+    cos = cosine_rows(got, ref)
+    assert cos.min() >= LATE_F32_COS, cos.min()
+
+
+def _cfg5_mixed_batch(budget=65536):
+    """A ~64k-token packed batch of config-5 texts whose lengths span the
+    corpus: its longest text (2048, the clip), the rest drawn in corpus order
+    (lognormal, median 256) until the budget is full."""
+    lengths, ids = inl.synthetic.cfg5_corpus(n_texts=16384)  # holds three texts at the 2048 clip
+    texts = np.split(ids, np.cumsum(lengths)[:-1])
+    first = int(np.argmax(lengths))
+    batch, total = [first], int(lengths[first])
+    for i in range(len(lengths)):
+        if i != first and total + int(lengths[i]) <= budget:
+            batch.append(i)
+            total += int(lengths[i])
+    return inl.planner.pack(texts, batch)
+
+
+@pytest.mark.slow
+def test_config5_packed_batch_across_lengths(gpu, qwen3_full, qwen3_cpu):
+    """A full ~64k-token packed batch of the config-5 corpus in bf16: finite
+    unit vectors; the longest text (2048 tokens: multi-tile causal attention
+    and the far rows of the RoPE table), two texts at the median length and
+    the shortest text against the oracle; and the longest and shortest
+    embedded alone equal to their vectors in the packed batch."""
+    cfg, w = qwen3_full
+    pids, pcu = _cfg5_mixed_batch()
+    L = np.diff(pcu)
+    assert L.max() == 2048 and pcu[-1] > 60000
     m = inl.CudaModel(cfg, w, dtype="bf16")
     got = m.embed(pids, pcu)
     assert np.isfinite(got).all()
     assert np.allclose(np.linalg.norm(got, axis=-1), 1.0, atol=1e-4)
-    # the shortest texts of the batch against the oracle, and alone vs packed
-    short = np.argsort(np.diff(pcu))[:3]
-    for j in short:
+    order = np.argsort(L, kind="stable")
+    median = order[len(order) // 2: len(order) // 2 + 2]
+    picks = [int(np.argmax(L)), int(median[0]), int(median[1]), int(order[0])]
+    rows = [pids[pcu[j]:pcu[j + 1]] for j in picks]
+    sub_cu = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    ref = qwen3_cpu.embed_last(np.concatenate(rows), sub_cu)
+    cos = cosine_rows(got[picks], ref)
+    assert cos.min() >= BF16_COS, dict(zip([int(L[j]) for j in picks], cos))
+    for j in (picks[0], picks[-1]):
         t = pids[pcu[j]:pcu[j + 1]]
-        ref = Q.embed_last(w, cfg, t, np.array([0, len(t)]))
         alone = m.embed(t, np.array([0, len(t)]))
-        assert cosine_rows(got[j:j + 1], ref)[0] >= BF16_COS
         assert cosine_rows(got[j:j + 1], alone)[0] > 0.99999
     m.close()
+
+
+@pytest.mark.slow
+def test_config5_longest_texts_f32(gpu, qwen3_full, qwen3_cpu):
+    """The same long and median texts through the f32 tower: the f32 floor
+    (cosine >= 0.99999) at 2048 tokens."""
+    cfg, w = qwen3_full
+    pids, pcu = _cfg5_mixed_batch()
+    L = np.diff(pcu)
+    order = np.argsort(L, kind="stable")
+    picks = [int(np.argmax(L)), int(order[len(order) // 2]), int(order[0])]
+    rows = [pids[pcu[j]:pcu[j + 1]] for j in picks]
+    sub_cu = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    sub_ids = np.concatenate(rows)
+    ref = qwen3_cpu.embed_last(sub_ids, sub_cu)
+    m = inl.CudaModel(cfg, w, dtype="f32")
+    got = m.embed(sub_ids, sub_cu)
+    m.close()
+    cos = cosine_rows(got, ref)
+    assert cos.min() >= F32_COS, cos
+
+
+@pytest.mark.parametrize("cfg_name", ["QWEN3_TINY", "QWEN3_TINY_D64"])
+def test_pruned_last_layer_equals_the_full_layer(gpu, cfg_name):
+    """Causal last-token pooling prunes the last layer to the rows the pooled
+    vector reads (the query tile of each text's last row for attention, the
+    last rows for o / gate-up / down). The embeddings equal those of the
+    unpruned layer: every row's arithmetic is the same, only other rows are
+    skipped."""
+    cfg = dict(getattr(inl.synthetic, cfg_name))
+    w = _tiny(cfg)
+    ids, cu = inl.synthetic.random_texts(37, 1, 700, cfg["vocab_size"], seed=17)
+    m = inl.CudaModel(cfg, w, dtype="bf16")
+    pruned = m.embed(ids, cu)
+    m.set_prune_last(False)
+    full = m.embed(ids, cu)
+    m.set_prune_last(True)
+    again = m.embed(ids, cu)
+    m.close()
+    assert np.abs(pruned - full).max() < 1e-6, np.abs(pruned - full).max()
+    assert np.array_equal(pruned, again)
+    assert cosine_rows(pruned, Q.embed_last(w, cfg, ids, cu)).min() >= BF16_COS
+
+
+@pytest.mark.slow
+def test_pruned_last_layer_full_size_batch(gpu, qwen3_full):
+    """The same on a full ~64k-token config-5 batch (about 200 last rows: the
+    pruned projections run on partial M tiles)."""
+    cfg, w = qwen3_full
+    pids, pcu = _cfg5_mixed_batch()
+    m = inl.CudaModel(cfg, w, dtype="bf16")
+    pruned = m.embed(pids, pcu)
+    m.set_prune_last(False)
+    full = m.embed(pids, pcu)
+    m.close()
+    assert cosine_rows(pruned, full).min() > 0.999999
+    assert np.abs(pruned - full).max() < 1e-5, np.abs(pruned - full).max()

@@ -2,12 +2,9 @@
 towers through the C ABI against the CPU oracles (oracle/modernbert.py,
 oracle/gemma.py), on the same seeded weights and inputs.
 
-Tolerances. SPLADE f32: weights within 1e-4 and identical term sets, where a
-term counts as present when its weight exceeds 1e-5 (a term whose max logit
-sits within f32 rounding of the shift, weight ~1e-7, may land on either side
-of zero; the reference's own golden test compares SparseVectors whose values
-come from the same arithmetic). SPLADE bf16: cosine >= 0.999 of the dense
-term-weight rows. Dense f32: cosine >= 0.99999; bf16: >= 0.999.
+Tolerances. SPLADE f32: weights within 1e-4 and identical active term sets
+(weight > 0), the assertion of the reference's golden test. SPLADE bf16:
+cosine >= 0.999 of the dense term-weight rows. Dense f32: cosine >= 0.99999; bf16: >= 0.999.
 """
 import numpy as np
 import pytest
@@ -25,11 +22,17 @@ def _scaled(weights, scale):
     return {k: (v * np.float32(scale) if v.ndim == 2 and "embed" not in k else v) for k, v in weights.items()}
 
 
-def assert_splade_f32(got, ref, tol=1e-4, present=1e-5):
+def assert_splade_f32(got, ref, tol=1e-4):
+    """Weights within ``tol`` and identical active term sets (weight > 0, the
+    SparseVector rule, crates/inl-sparse/src/lib.rs:51-62), as the
+    reference's golden test asserts them (modernbert.rs:1014-1057); a flip
+    reports its two weights."""
     assert got.shape == ref.shape
     assert np.abs(got - ref).max() <= tol, np.abs(got - ref).max()
     for i in range(len(ref)):
-        assert np.array_equal(np.nonzero(got[i] > present)[0], np.nonzero(ref[i] > present)[0]), i
+        a, b = got[i] > 0, ref[i] > 0
+        flips = np.nonzero(a != b)[0]
+        assert len(flips) == 0, (i, [(int(v), float(got[i, v]), float(ref[i, v])) for v in flips[:8]])
 
 
 @pytest.fixture(scope="module")
@@ -42,6 +45,38 @@ def mb_tiny():
 
 def _pooling(cfg):
     return cfg.get("splade", {})
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_sparse_compaction_equals_the_dense_rows(gpu, mb_tiny, dtype):
+    """inl_cuda_forward_sparse_compact: per text the ascending term ids with
+    weight > 0 and their weights, bit for bit the nonzeros of the dense rows;
+    a prefix-only text is an empty vector; a capacity below the batch's term
+    count is refused with the size needed in offsets[n]."""
+    import ctypes
+
+    from im_not_llm_b200 import _native as N_
+
+    cfg, w = mb_tiny
+    ids, cu = inl.synthetic.random_texts(9, 1, 200, cfg["vocab_size"], seed=23)
+    ids[cu[3]:cu[4]] = 5  # prefix tokens only
+    m = inl.CudaModel(cfg, w, dtype=dtype)
+    dense = m.encode_sparse(ids, cu)
+    pairs = m.encode_sparse_compact(ids, cu)
+    assert len(pairs) == len(dense)
+    for row, (idx, val) in zip(dense, pairs):
+        nz = np.nonzero(row > 0)[0]
+        assert np.array_equal(idx, nz) and np.array_equal(val, row[nz])
+    assert len(pairs[3][0]) == 0
+    total = sum(len(p[0]) for p in pairs)
+    offsets = np.zeros(len(cu), dtype=np.int64)
+    small = np.empty(max(total - 1, 1), dtype=np.int32)
+    smallv = np.empty(max(total - 1, 1), dtype=np.float32)
+    st = N_.lib().inl_cuda_forward_sparse_compact(m.handle, ids.ctypes.data, N_.INL_MEM_HOST, cu.ctypes.data,
+                                                  len(cu) - 1, offsets.ctypes.data, small.ctypes.data,
+                                                  smallv.ctypes.data, total - 1, N_.INL_MEM_HOST)
+    assert st == 4 and offsets[-1] == total and "capacity" in N_.last_error()
+    m.close()
 
 
 def test_modernbert_tiny_f32_matches_oracle(gpu, mb_tiny):
@@ -198,3 +233,63 @@ def test_config4_gemma_full_size_subset(gpu, config4_case, dtype, floor):
     got = m.embed(ids, cu, out_dim=256)
     m.close()
     assert cosine_rows(got, truncate_and_normalize(ref, 256)).min() >= floor
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("mode,eps", [("ffma", 1e-6), ("3xbf16", 5e-6)])
+def test_config4_unscaled_weights_f32_within_the_oracles_own_f32_spread(gpu, mode, eps):
+    """Config 4 with its BASELINE weights as drawn (unit q/k norm weights, no
+    scaling) in f32, on its four shortest texts (33 to 43 tokens).
+
+    Unscaled attention over RMS-normed q / k (crates/inl-text/src/gemma2.rs:14-16)
+    at this depth is ill-conditioned: perturbing every weight matrix by one
+    f32 rounding step (relative 1e-7) already moves the f32 oracle's own
+    embeddings to cosine ~0.9994, below the 0.99999 floor. A GPU evaluation
+    rounds differently, so the check is the oracle's own spread under
+    perturbations of the size of the GPU's arithmetic error: the GPU's
+    deviation 1 - cosine is at most the largest deviation of three oracle runs
+    with every weight matrix perturbed by relative noise eps. For the SIMT
+    FFMA GEMMs eps = 1e-6, the typical difference between two summation orders
+    of a dot product of K ~ 10^3 terms (sqrt(K) u, u = 2^-24); for the 3xBF16
+    tensor-core GEMMs eps = 5e-6, the size of their operand splitting error
+    (|x - hi - lo| <= 2^-17 |x|). Measured on a B200 (FFMA): deviations 6e-4 to
+    3.1e-3 against spreads of 2.2e-3 to 7.7e-3."""
+    cfg = dict(inl.synthetic.GEMMA_STYLE)
+    w, dense = _gemma_weights(cfg)
+    ids, cu = inl.synthetic.cfg4_inputs()
+    L = np.diff(cu)
+    pick = np.argsort(L, kind="stable")[:4]
+    rows = [ids[cu[i]:cu[i + 1]] for i in pick]
+    pid = np.concatenate(rows).astype(np.uint32)
+    pcu = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    ref = G.embed_dense_head(w, cfg, dense, pid, pcu, prefix="")
+    spread = np.zeros(len(rows))
+    rng = np.random.default_rng(9)
+    for _ in range(3):
+        wp = {k: (v * (1 + eps * rng.standard_normal(v.shape))).astype(np.float32) if v.ndim == 2 else v
+              for k, v in w.items()}
+        dp = [wp[f"dense_head.{j}.weight"] for j in range(len(cfg["dense_dims"]))]
+        spread = np.maximum(spread, 1 - cosine_rows(G.embed_dense_head(wp, cfg, dp, pid, pcu, prefix=""), ref))
+    m = inl.CudaModel(cfg, w, dtype="f32")
+    m.set_f32_gemm(mode)
+    got = m.embed(pid, pcu)
+    m.close()
+    dev = 1 - cosine_rows(got, ref)
+    assert (dev <= np.maximum(spread, 1e-5)).all(), {"gpu_deviation": dev.tolist(), "oracle_spread": spread.tolist()}
+
+
+@pytest.mark.slow
+def test_config2_splade_f32_both_gemm_modes_agree(gpu):
+    """Config 2 in f32 through the SIMT FFMA GEMMs and through the 3xBF16
+    tensor-core GEMMs: identical active term sets and weights within 1e-4
+    of each other (each is also held to the oracle by
+    test_config2_splade_full_size_f32 in the default mode)."""
+    cfg = dict(inl.synthetic.MODERNBERT_SPLADE)
+    w = inl.synthetic.modernbert_weights(cfg, seed=0)
+    ids, cu = inl.synthetic.cfg2_inputs()
+    m = inl.CudaModel(cfg, w, dtype="f32")
+    split = m.encode_sparse(ids, cu)
+    m.set_f32_gemm("ffma")
+    ffma = m.encode_sparse(ids, cu)
+    m.close()
+    assert_splade_f32(split, ffma)

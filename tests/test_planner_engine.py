@@ -282,6 +282,12 @@ class _EchoReplica:
             out[i, (cu[i + 1] - cu[i]) % 4] = np.nan if self.nan else 1.0 + i * 0
         return out
 
+    def encode_sparse_compact(self, ids, cu):
+        dense = self.encode_sparse(ids, cu)
+        if not np.all(np.isfinite(dense)):
+            raise inl.InferenceError("non-finite SPLADE term weight")
+        return [(np.nonzero(r > 0)[0].astype(np.uint32), r[r > 0]) for r in dense]
+
     def encode_multivector(self, ids, cu):
         self.calls += 1
         out = np.zeros((len(ids), 2), dtype=np.float32)
