@@ -1,5 +1,6 @@
 // Backend of the C++ host layer over the C ABI of libinl_cuda
 // (include/inl_cuda.h): one model handle, host buffers in and out.
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -53,11 +54,21 @@ class CudaBackend : public Backend {
     return out;
   }
 
-  std::vector<float> sparse(const Packed& b) override {
+  std::vector<SparseVector> sparse(const Packed& b) override {
+    // compacted on the device; only the active terms are copied back
     const int n = static_cast<int>(b.cu.size()) - 1;
-    std::vector<float> out(static_cast<size_t>(n) * info().sparse_dim);
-    check(inl_cuda_forward_sparse(m_, b.ids.data(), INL_MEM_HOST, b.cu.data(), n, out.data(), INL_MEM_HOST),
+    const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(n) * info().sparse_dim);
+    std::vector<int64_t> offsets(static_cast<size_t>(n) + 1);
+    std::vector<int32_t> idx(static_cast<size_t>(cap));
+    std::vector<float> val(static_cast<size_t>(cap));
+    check(inl_cuda_forward_sparse_compact(m_, b.ids.data(), INL_MEM_HOST, b.cu.data(), n, offsets.data(), idx.data(),
+                                          val.data(), cap, INL_MEM_HOST),
           "sparse forward");
+    std::vector<SparseVector> out(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) {
+      out[i].indices.assign(idx.begin() + offsets[i], idx.begin() + offsets[i + 1]);
+      out[i].values.assign(val.begin() + offsets[i], val.begin() + offsets[i + 1]);
+    }
     return out;
   }
 

@@ -297,16 +297,10 @@ EngineInfo SparseEncoder::load() {
 std::vector<SparseVector> SparseEncoder::encode(const Tokens& texts) {
   const Tokens t = truncate(texts, options_.max_length);
   if (t.empty()) return {};
-  const size_t V = static_cast<size_t>(model()->backend->info().sparse_dim);
-  return run_batches<SparseVector>("native sparse", t, [V](Backend& b, const Packed& p) {
-    const std::vector<float> dense = b.sparse(p);
-    for (float v : dense)  // crates/inl-sparse/src/native.rs:536-540
-      if (!std::isfinite(v)) throw InferenceError("native sparse encoder produced non-finite weights");
-    const size_t n = p.cu.size() - 1;
-    std::vector<SparseVector> out;
-    for (size_t i = 0; i < n && (i + 1) * V <= dense.size(); ++i) out.push_back(SparseVector::from_dense(&dense[i * V], V));
-    return out;
-  });
+  // The backend returns the compacted vectors (the library compacts them on
+  // the device); a non-finite weight is an inference error there, as in
+  // crates/inl-sparse/src/native.rs:536-540.
+  return run_batches<SparseVector>("native sparse", t, [](Backend& b, const Packed& p) { return b.sparse(p); });
 }
 
 LateEncoder::LateEncoder(Loader loader, Options options, LateTask query, LateTask document)

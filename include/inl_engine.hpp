@@ -108,6 +108,12 @@ struct ModelInfo {
   int device = 0;
 };
 
+struct SparseVector {  // crates/inl-sparse/src/lib.rs:51-62: sorted term ids, positive weights
+  std::vector<uint32_t> indices;
+  std::vector<float> values;
+  static SparseVector from_dense(const float* row, size_t n);
+};
+
 // What the engines need from a loaded model. Outputs are row-major f32.
 class Backend {
  public:
@@ -115,8 +121,9 @@ class Backend {
   virtual ModelInfo info() = 0;
   // [n, dense_dim or out_dim] unit vectors
   virtual std::vector<float> dense(const Packed& batch, int out_dim) = 0;
-  // [n, sparse_dim] SPLADE weights
-  virtual std::vector<float> sparse(const Packed& batch) = 0;
+  // one SPLADE vector per text: active terms (weight > 0) in ascending term
+  // order; a non-finite weight is an InferenceError
+  virtual std::vector<SparseVector> sparse(const Packed& batch) = 0;
   // [total tokens, multivector_dim] per-token vectors in packed order
   virtual std::vector<float> multivector(const Packed& batch) = 0;
 };
@@ -154,12 +161,6 @@ struct Options {  // the subset of TextOptions (crates/inl-text/src/native.rs:17
   std::optional<double> per_batch_timeout_seconds;
   std::optional<int> output_dim;
   double batch_timeout() const;  // crates/inl-text/src/native.rs:739-752
-};
-
-struct SparseVector {  // crates/inl-sparse/src/lib.rs:51-62: sorted term ids, positive weights
-  std::vector<uint32_t> indices;
-  std::vector<float> values;
-  static SparseVector from_dense(const float* row, size_t n);
 };
 
 using Tokens = std::vector<std::vector<uint32_t>>;

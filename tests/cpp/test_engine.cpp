@@ -62,15 +62,20 @@ struct Fake : Backend {
     }
     return out;
   }
-  std::vector<float> sparse(const Packed& p) override {
+  std::vector<SparseVector> sparse(const Packed& p) override {
     ++*calls;
     const size_t n = p.cu.size() - 1;
-    std::vector<float> out(n * 5, 0.f);
+    std::vector<float> rows(n * 5, 0.f);
     for (size_t i = 0; i < n; ++i) {
-      out[i * 5] = -1.f;
-      out[i * 5 + (p.cu[i + 1] - p.cu[i]) % 5] += 2.f;
-      if (nan) out[i * 5 + 3] = std::numeric_limits<float>::quiet_NaN();
+      rows[i * 5] = -1.f;
+      rows[i * 5 + (p.cu[i + 1] - p.cu[i]) % 5] += 2.f;
+      if (nan) rows[i * 5 + 3] = std::numeric_limits<float>::quiet_NaN();
     }
+    // the library's compaction: a non-finite weight is an inference error
+    for (float v : rows)
+      if (!std::isfinite(v)) throw InferenceError("non-finite SPLADE term weight");
+    std::vector<SparseVector> out;
+    for (size_t i = 0; i < n; ++i) out.push_back(SparseVector::from_dense(&rows[i * 5], 5));
     return out;
   }
   std::vector<float> multivector(const Packed& p) override {
