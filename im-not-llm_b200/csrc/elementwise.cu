@@ -379,6 +379,76 @@ __global__ void qk_norm_rope_vec_kernel(QkRopeArgs a) {
   st_vec<T, E>(row + lane * E, x);
 }
 
+// One warp per token, for heads of 64 or 128 features, where a warp per
+// (token, head) has too little to do (a 128- or 256-byte row): the token's
+// RoPE factors are read once (E cos and E sin per lane) and its heads are
+// processed in groups of four, the group's rows loaded before any is computed.
+// Same arithmetic as the per-(token, head) kernels; rows, weights and tables
+// aligned to the vector access (the host checks).
+template <typename T, int E>
+__global__ void qk_norm_rope_tok_kernel(QkRopeArgs a) {
+  const int warps = blockDim.x >> 5;
+  const long long t = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= a.T) return;
+  constexpr int d = E * 32;
+  constexpr int half = d / 2;
+  constexpr int G = 4;
+  const int heads = a.hq + a.hkv + (a.v_norm ? a.hkv : 0);
+  const bool is_bf16 = sizeof(T) == 2;
+  T* base = reinterpret_cast<T*>(a.qkv) + t * a.ld + lane * E;
+  const bool first = lane < 16;
+  float c[E], sn[E];
+  {
+    int p = a.pos[t];
+    if (p < 0 || p >= a.max_pos) {
+      if (lane == 0 && a.status) atomicCAS(a.status, 0, INL_DEV_BAD_INDEX);
+      p = 0;
+    }
+    const int i0 = lane * E - (first ? 0 : half);
+    ld_vec<float, E>(a.cos + static_cast<long long>(p) * half + i0, c);
+    ld_vec<float, E>(a.sin + static_cast<long long>(p) * half + i0, sn);
+  }
+  float qw[E], kw[E];
+  if (a.qw) ld_vec<float, E>(a.qw + lane * E, qw);
+  if (a.kw) ld_vec<float, E>(a.kw + lane * E, kw);
+  for (int h0 = 0; h0 < heads; h0 += G) {
+    float x[G][E];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      if (h0 + g < heads) ld_vec<T, E>(base + static_cast<long long>(h0 + g) * d, x[g]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int h = h0 + g;
+      if (h >= heads) break;  // warp-uniform
+      const bool is_q = h < a.hq;
+      const bool is_k = !is_q && h < a.hq + a.hkv;
+      const bool has_w = is_q ? (a.qw != nullptr) : (is_k ? (a.kw != nullptr) : false);
+      const bool norm = is_q ? (a.qw != nullptr) : (is_k ? (a.kw != nullptr) : true);
+      if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss += x[g][e] * x[g][e];
+        const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(d) + a.eps);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          float v = x[g][e] * inv;
+          if (has_w) v *= is_q ? qw[e] : kw[e];
+          x[g][e] = is_bf16 ? bf16_round(v) : v;
+        }
+      }
+      if (is_q || is_k) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float other = __shfl_xor_sync(0xffffffffu, x[g][e], 16);
+          x[g][e] = first ? (x[g][e] * c[e] - other * sn[e]) : (x[g][e] * c[e] + other * sn[e]);
+        }
+      }
+      st_vec<T, E>(base + static_cast<long long>(h) * d, x[g]);
+    }
+  }
+}
+
 // Heads of d <= 32 features (8, 16, 32): one warp per (token, head), lane l < d
 // holds element l and its RoPE partner sits in lane l ^ (d / 2).
 template <typename T>
@@ -847,8 +917,14 @@ int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s) {
                    (reinterpret_cast<uintptr_t>(a.cos) % (4 * E)) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.sin) % (4 * E)) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.qw) % (4 * E)) == 0 && (reinterpret_cast<uintptr_t>(a.kw) % (4 * E)) == 0;
+  // Aligned rows: one warp per token for head_dim 64 / 128 (19.1 -> 9.0 us on
+  // config 2's bf16 layers), one warp per (token, head) for 256 (0.124
+  // against 0.138 ms on config 4's).
+  const int tok_grid = rows_grid(a.T, 8);
 #define INL_QKR(EE)                                                                               \
-  if (vec && a.bf16) qk_norm_rope_vec_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);          \
+  if (vec && EE < 8 && a.bf16) qk_norm_rope_tok_kernel<__nv_bfloat16, EE><<<tok_grid, 256, 0, s>>>(a); \
+  else if (vec && EE < 8) qk_norm_rope_tok_kernel<float, EE><<<tok_grid, 256, 0, s>>>(a);         \
+  else if (vec && a.bf16) qk_norm_rope_vec_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);     \
   else if (vec) qk_norm_rope_vec_kernel<float, EE><<<grid, 256, 0, s>>>(a);                       \
   else if (a.bf16) qk_norm_rope_kernel<__nv_bfloat16, EE><<<grid, 256, 0, s>>>(a);                \
   else qk_norm_rope_kernel<float, EE><<<grid, 256, 0, s>>>(a);
@@ -883,6 +959,8 @@ int last_token_norm_l2(const void* h, int h_bf16, long long ldh, const int* cu, 
 // product: x = hi + lo + O(2^-17 |x|) with hi = bf16(x), lo = bf16(x - hi).
 // Activation side (mode 0) [hi | hi | lo], weight side (mode 1) [hi | lo | hi]:
 // one bf16 GEMM over K' = 3K then sums hi.hi + hi.lo + lo.hi in f32.
+// Mode 2 writes the hi segment alone: the bf16-rounded operand of a plain
+// bf16 product over K.
 __global__ void split3_kernel(const float* __restrict__ x, long long ldx, int rows, int K, int mode,
                               __nv_bfloat16* __restrict__ out, long long ldo) {
   const int pairs = K / 2;
@@ -897,6 +975,7 @@ __global__ void split3_kernel(const float* __restrict__ x, long long ldx, int ro
     const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x - h.x, v.y - h.y);
     __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + static_cast<long long>(r) * ldo + k);
     o[0] = hi;
+    if (mode == 2) continue;
     o[K / 2] = mode ? lo : hi;
     o[K] = mode ? hi : lo;
   }

@@ -240,17 +240,21 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
     // Rows are vocabulary entries, columns are packed tokens of segment seg[col]:
     // a running max per segment run, flushed with one atomicMax per run.
     // seg[col] is the same for every lane, so the branches stay warp-uniform.
+    // The 32 columns' segments arrive with one coalesced load per chunk,
+    // requested before the TMEM read so the two latencies overlap; each
+    // column's segment is then shuffled from the lane that loaded it. The
+    // inner loop is unrolled in full so that r[] stays in registers.
     int cur = -1;
     float mx = -INFINITY;
 #pragma unroll 1
     for (int c = 0; c < HW; c += 32) {
+      const int c0 = n0 + half * HW + c;
+      const int my_seg = c0 + lane < e.N ? __ldg(e.seg + c0 + lane) : -1;
       tmem_ld32(t_row + half * HW + c, r);
       tmem_ld_wait();
-      const int c0 = n0 + half * HW + c;
-#pragma unroll 4
+#pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int col = c0 + j;
-        const int sg = col < e.N ? __ldg(e.seg + col) : -1;
+        const int sg = __shfl_sync(0xffffffffu, my_seg, j);
         const float v = __uint_as_float(r[j]);
         if (sg != cur) {
           if (cur >= 0 && row_ok) atomicMax(e.pooled + static_cast<long long>(cur) * e.ldp + row, encode_ordered(mx));
@@ -316,7 +320,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
           for (int j = 0; j < 8; ++j)
             reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
-          for (int j = 0; j < left; ++j) dst[j] = v[j];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)  // static indices keep v[] in registers
+            if (j < left) dst[j] = v[j];
         }
       } else {
         if constexpr (EPI == INL_EPI_RESID_BF16) {
@@ -842,11 +848,15 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
     bn = 256;
   }
-  // CTA pairs (cta_group::2) take 256-wide tiles of the plain, residual and gated
-  // bf16 epilogues; each CTA of a pair loads 128 rows of W. The QKV epilogue
-  // (q/k norm + RoPE) measured faster on single CTAs, so it stays there.
+  // CTA pairs (cta_group::2) take 256-wide tiles of the plain, residual,
+  // gated and f32 epilogues; each CTA of a pair loads 128 rows of W, so a K
+  // step moves 32 KB per CTA instead of 48 KB (the 3xBF16 f32 products: 3%
+  // faster on config 1). The QKV epilogue (q/k norm + RoPE) measured faster on
+  // single CTAs, and the segment-max decoder the same on both, so those stay
+  // on single CTAs.
   const bool pair = g.cta_pair && bn == 256 &&
-                    (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16);
+                    (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16 ||
+                     g.epi == INL_EPI_F32);
   CUtensorMap ta, tb, to;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, pair ? 128 : bn)) return -2;
@@ -865,6 +875,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     switch (g.epi) {
       case INL_EPI_BF16: err = launch_gemm_pair<INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm_pair<INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_F32: err = launch_gemm_pair<INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: err = dispatch_act_pair<INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
     }
   } else if (bn == 256) {

@@ -177,7 +177,8 @@ int qk_norm_rope(const QkRopeArgs& a, cudaStream_t s);
 int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s);
 
 // 3xBF16: f32 rows -> bf16 [rows, 3K] at row stride ldo, mode 0 [hi | hi | lo]
-// (activation side), mode 1 [hi | lo | hi] (weight side); K, ldx, ldo even.
+// (activation side), mode 1 [hi | lo | hi] (weight side); mode 2 writes [hi]
+// alone ([rows, K], a bf16 product); K, ldx, ldo even.
 int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* out, long long ldo, cudaStream_t s);
 // out = a + b (f32 rows; out may alias a or b).
 int add_rows_f32(float* out, long long ldo, const float* a, long long lda, const float* b, long long ldb, int rows,

@@ -487,7 +487,6 @@ bool head_dim_supported(int d, int bf16) {
 
 int shape_support(const ModelConfig& c, int dtype) {
   const int bf = dtype == INL_DTYPE_BF16;
-  if (c.arch == inl::ARCH_QWEN35 && bf) return fail(INL_ERR_CONFIG, "the Qwen3.5 tower runs in f32");
   if (c.arch == inl::ARCH_MODERNBERT && !head_dim_supported(c.d, bf))
     return fail(INL_ERR_CONFIG, "head_dim " + std::to_string(c.d) + " is not supported by the CUDA tower in " +
                                     (bf ? "bf16" : "f32"));
@@ -817,12 +816,21 @@ int create_common(const char* config_json, int device, int dtype, inl_model** ou
   INL_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
   inl_model* m = new inl_model();
   m->dtype = dtype;
+  m->api_dtype = dtype;
   m->device = device;
   m->gate_block = dtype == INL_DTYPE_BF16 ? 128 : 64;
   int r = parse_config(config_json, m->c);
   if (r) {
     delete m;
     return r;
+  }
+  if (m->c.arch == inl::ARCH_QWEN35 && dtype == INL_DTYPE_BF16) {
+    // bf16 Qwen3.5 (accepted by the reference, crates/inl-late/src/native.rs:232):
+    // the tower keeps f32 activations, norms and the gated delta rule, and runs
+    // its GEMMs on bf16-rounded operands with f32 accumulation.
+    m->dtype = INL_DTYPE_F32;
+    m->gate_block = 64;
+    m->f32_bf16_operands = true;
   }
   // f32 GEMMs on the tensor cores (3xBF16, relative error ~5e-6) except for
   // the Qwen3.5 late tower: its gated delta rule carries a state from token to
@@ -1081,13 +1089,16 @@ cudaEvent_t take_event(inl_model* m) {
 // weight side of a product, mode 0 [hi | hi | lo] for the activation side),
 // made once on the model's stream and kept with the weights.
 const void* split_weight(inl_model* m, const void* w, int rows, int K, int mode) {
-  const uintptr_t key = reinterpret_cast<uintptr_t>(w) | static_cast<uintptr_t>(mode & 1);
+  const uintptr_t key = reinterpret_cast<uintptr_t>(w) | static_cast<uintptr_t>(mode & 3);
   auto it = m->split_w.find(key);
   if (it != m->split_w.end()) return it->second;
+  const int segs = mode == 2 ? 1 : 3;
   void* p = nullptr;
-  if (cudaMalloc(&p, static_cast<size_t>(rows) * 3 * K * 2) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(rows) * segs * K * 2) != cudaSuccess) return nullptr;
   m->allocs.push_back(p);
-  if (inl::split3_bf16(static_cast<const float*>(w), K, rows, K, mode, p, 3LL * K, m->stream) != 0) return nullptr;
+  if (inl::split3_bf16(static_cast<const float*>(w), K, rows, K, mode, p, static_cast<long long>(segs) * K,
+                       m->stream) != 0)
+    return nullptr;
   m->launches++;
   m->split_w[key] = p;
   return p;
@@ -1102,11 +1113,13 @@ const void* split_weight(inl_model* m, const void* w, int rows, int K, int mode)
 int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int M, int N, int K, int epi, int act,
                   void* out, long long ldo, const void* resid, long long ldr) {
   if ((K % 8) || (lda & 1) || (reinterpret_cast<uintptr_t>(A) & 7)) return -1;
-  const void* w3 = split_weight(m, W, N, K, 1);
+  // one segment (a bf16 product) for a Qwen3.5 tower requested in bf16
+  const bool one = m->f32_bf16_operands;
+  const void* w3 = split_weight(m, W, N, K, one ? 2 : 1);
   if (!w3) return -3;
-  const long long K3 = 3LL * K;
+  const long long K3 = (one ? 1LL : 3LL) * K;
   if (m->split_a.ensure(token_cap(M) * K3 * 2) != cudaSuccess) return -3;
-  if (inl::split3_bf16(static_cast<const float*>(A), lda, M, K, 0, m->split_a.p, K3, m->stream)) return -3;
+  if (inl::split3_bf16(static_cast<const float*>(A), lda, M, K, one ? 2 : 0, m->split_a.p, K3, m->stream)) return -3;
   m->launches++;
   const bool plain = epi == INL_EPI_F32 || epi == INL_EPI_BF16;
   float* dst = static_cast<float*>(out);
@@ -1174,7 +1187,8 @@ int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int
     g.status = m->d_status;
     r = inl::gemm_bf16_tn(g, m->stream);
   } else {
-    r = m->f32_split3 ? linear_split3(m, A, lda, W, M, N, K, epi, act, out, ldo, resid, ldr) : -1;
+    r = (m->f32_split3 || m->f32_bf16_operands) ? linear_split3(m, A, lda, W, M, N, K, epi, act, out, ldo, resid, ldr)
+                                                : -1;
   }
   if (r == -1 && m->dtype != INL_DTYPE_BF16) {
     inl::GemmF32Args g;
@@ -2293,7 +2307,7 @@ int inl_cuda_forward_sparse_compact(inl_model* m, const uint32_t* ids, int ids_m
 int inl_cuda_model_info(const inl_model* m, inl_model_info* out) {
   if (!m || !out) return fail(INL_ERR_CONFIG, "NULL argument");
   out->arch = m->c.arch;
-  out->dtype = m->dtype;
+  out->dtype = m->api_dtype;
   out->device = m->device;
   out->hidden_size = m->c.H;
   out->num_layers = m->c.layers;

@@ -186,6 +186,10 @@ struct inl_model {
   // f32 models: GEMMs as one bf16 tensor-core GEMM over K' = 3K (3xBF16) when
   // on; the split [hi | lo | hi] copy of each f32 weight is made on first use.
   bool f32_split3 = true;
+  // Qwen3.5 tower requested in bf16: f32 activations and recurrence, the
+  // GEMMs on bf16-rounded operands (one segment of the split path)
+  bool f32_bf16_operands = false;
+  int api_dtype = 0;  // the dtype the model was created with, as reported
   std::unordered_map<uintptr_t, void*> split_w;
   inl::DevBuf split_a, split_c;
   inl::DevBuf seg_scratch;  // mean pooling's per-chunk partial sums

@@ -37,6 +37,23 @@ def _w(weights: dict, name: str) -> np.ndarray:
     return np.asarray(weights[name], dtype=np.float32)
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """x rounded to the nearest bf16 (ties to even), as f32."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return (((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+def linear(x: np.ndarray, w: np.ndarray, operands: str = "f32") -> np.ndarray:
+    """``x @ w^T`` in f32. ``operands="bf16"`` rounds both factors to bf16
+    first and keeps the f32 sum: the CUDA tower's bf16 mode (bf16 products on
+    the tensor cores, f32 activations, norms and recurrence). The reference's
+    own bf16 tower has no golden vectors; this mode is what the CUDA bf16 path
+    is checked against."""
+    if operands == "bf16":
+        return bf16_round(x) @ bf16_round(w).T
+    return x @ w.T
+
+
 def root_prefix(weights: dict) -> str:
     """The text model's root, as crates/inl-late/src/native.rs:519-531 finds it."""
     for p in ("language_model", "model.language_model", "model", ""):
@@ -148,16 +165,16 @@ def gated_delta_rule_chunked(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.
     return out.astype(np.float32)
 
 
-def gated_deltanet(weights: dict, cfg: dict, p: str, x: np.ndarray) -> np.ndarray:
+def gated_deltanet(weights: dict, cfg: dict, p: str, x: np.ndarray, operands: str = "f32") -> np.ndarray:
     """GatedDeltaNet::forward (qwen3_5.rs:481-545) for one text; x: [T, H] normed."""
     T = x.shape[0]
     nk, nv = int(cfg["linear_num_key_heads"]), int(cfg["linear_num_value_heads"])
     dk, dv = int(cfg["linear_key_head_dim"]), int(cfg["linear_value_head_dim"])
     eps = float(cfg["rms_norm_eps"])
     conv_w = _w(weights, p + "conv1d.weight").reshape(2 * nk * dk + nv * dv, -1)
-    mixed = causal_conv_silu(x @ _w(weights, p + "in_proj_qkv.weight").T, conv_w)
-    beta = sigmoid(x @ _w(weights, p + "in_proj_b.weight").T)
-    a = x @ _w(weights, p + "in_proj_a.weight").T + _w(weights, p + "dt_bias")
+    mixed = causal_conv_silu(linear(x, _w(weights, p + "in_proj_qkv.weight"), operands), conv_w)
+    beta = sigmoid(linear(x, _w(weights, p + "in_proj_b.weight"), operands))
+    a = linear(x, _w(weights, p + "in_proj_a.weight"), operands) + _w(weights, p + "dt_bias")
     g = softplus(a) * -np.exp(_w(weights, p + "A_log"))
     q = mixed[:, :nk * dk].reshape(T, nk, dk)
     k = mixed[:, nk * dk:2 * nk * dk].reshape(T, nk, dk)
@@ -167,11 +184,11 @@ def gated_deltanet(weights: dict, cfg: dict, p: str, x: np.ndarray) -> np.ndarra
         k = np.repeat(k, nv // nk, axis=1)
     core = gated_delta_rule(q, k, v, g, beta)
     # gated RMSNorm per value head with the plain weight, then silu(z)
-    z = (x @ _w(weights, p + "in_proj_z.weight").T).reshape(T, nv, dv)
+    z = linear(x, _w(weights, p + "in_proj_z.weight"), operands).reshape(T, nv, dv)
     var = np.mean(core * core, axis=-1, keepdims=True, dtype=np.float32)
     normed = core / np.sqrt(var + np.float32(eps)) * _w(weights, p + "norm.weight")
     out = (normed * silu(z)).reshape(T, nv * dv)
-    return (out @ _w(weights, p + "out_proj.weight").T).astype(np.float32)
+    return linear(out, _w(weights, p + "out_proj.weight"), operands).astype(np.float32)
 
 
 def rotary(cfg: dict, positions: int) -> tuple[np.ndarray, np.ndarray, int]:
@@ -195,16 +212,18 @@ def rope_partial(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, dim: int) -> n
     return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s, x[..., dim:]], axis=-1).astype(np.float32)
 
 
-def full_attention(weights: dict, cfg: dict, p: str, x: np.ndarray, cos, sin, rdim: int) -> np.ndarray:
+def full_attention(weights: dict, cfg: dict, p: str, x: np.ndarray, cos, sin, rdim: int,
+                   operands: str = "f32") -> np.ndarray:
     """FullAttention::forward (qwen3_5.rs:302-350) for one text, no padding."""
     T = x.shape[0]
     hq, hkv, hd = int(cfg["num_attention_heads"]), int(cfg["num_key_value_heads"]), int(cfg["head_dim"])
     eps = float(cfg["rms_norm_eps"])
-    qg = (x @ _w(weights, p + "q_proj.weight").T).reshape(T, hq, 2 * hd)
+    qg = linear(x, _w(weights, p + "q_proj.weight"), operands).reshape(T, hq, 2 * hd)
     q = zc_rms_norm(qg[..., :hd], _w(weights, p + "q_norm.weight"), eps)
     gate = qg[..., hd:].reshape(T, hq * hd)
-    k = zc_rms_norm((x @ _w(weights, p + "k_proj.weight").T).reshape(T, hkv, hd), _w(weights, p + "k_norm.weight"), eps)
-    v = (x @ _w(weights, p + "v_proj.weight").T).reshape(T, hkv, hd)
+    k = zc_rms_norm(linear(x, _w(weights, p + "k_proj.weight"), operands).reshape(T, hkv, hd),
+                    _w(weights, p + "k_norm.weight"), eps)
+    v = linear(x, _w(weights, p + "v_proj.weight"), operands).reshape(T, hkv, hd)
     q = rope_partial(q, cos[:T], sin[:T], rdim)
     k = rope_partial(k, cos[:T], sin[:T], rdim)
     rep = hq // hkv
@@ -213,11 +232,12 @@ def full_attention(weights: dict, cfg: dict, p: str, x: np.ndarray, cos, sin, rd
     if cfg.get("is_causal", True):  # additive -1e4 on future keys (qwen3_5.rs:16, 917-938)
         s = s + np.where(np.arange(T)[None, :] > np.arange(T)[:, None], np.float32(-1e4), np.float32(0))[None]
     o = np.einsum("hqk,khd->qhd", softmax(s, axis=-1), vv, dtype=np.float32).reshape(T, hq * hd)
-    return ((o * sigmoid(gate)) @ _w(weights, p + "o_proj.weight").T).astype(np.float32)
+    return linear(o * sigmoid(gate), _w(weights, p + "o_proj.weight"), operands).astype(np.float32)
 
 
-def hidden(weights: dict, config: dict, ids: np.ndarray) -> np.ndarray:
-    """``last_hidden_state`` of one text (Qwen35Text::forward, qwen3_5.rs:893-915)."""
+def hidden(weights: dict, config: dict, ids: np.ndarray, operands: str = "f32") -> np.ndarray:
+    """``last_hidden_state`` of one text (Qwen35Text::forward, qwen3_5.rs:893-915);
+    ``operands`` as in :func:`linear`."""
     cfg = text_config(config)
     root = root_prefix(weights)
     eps = float(cfg["rms_norm_eps"])
@@ -227,20 +247,22 @@ def hidden(weights: dict, config: dict, ids: np.ndarray) -> np.ndarray:
         p = f"{root}layers.{i}."
         x = zc_rms_norm(h, _w(weights, p + "input_layernorm.weight"), eps)
         if kind == "linear_attention":
-            h = h + gated_deltanet(weights, cfg, p + "linear_attn.", x)
+            h = h + gated_deltanet(weights, cfg, p + "linear_attn.", x, operands)
         else:
-            h = h + full_attention(weights, cfg, p + "self_attn.", x, cos, sin, rdim)
+            h = h + full_attention(weights, cfg, p + "self_attn.", x, cos, sin, rdim, operands)
         x = zc_rms_norm(h, _w(weights, p + "post_attention_layernorm.weight"), eps)
-        m = silu(x @ _w(weights, p + "mlp.gate_proj.weight").T) * (x @ _w(weights, p + "mlp.up_proj.weight").T)
-        h = h + m @ _w(weights, p + "mlp.down_proj.weight").T
+        m = silu(linear(x, _w(weights, p + "mlp.gate_proj.weight"), operands)) * linear(
+            x, _w(weights, p + "mlp.up_proj.weight"), operands)
+        h = h + linear(m, _w(weights, p + "mlp.down_proj.weight"), operands)
     return zc_rms_norm(h, _w(weights, root + "norm.weight"), eps)
 
 
 def late_vectors(weights: dict, config: dict, projection: np.ndarray, bias: np.ndarray | None,
-                 ids: np.ndarray, skip=frozenset(), normalize: bool = True) -> np.ndarray:
+                 ids: np.ndarray, skip=frozenset(), normalize: bool = True, operands: str = "f32") -> np.ndarray:
     """One text's kept token vectors (encode_batch, crates/inl-late/src/native.rs:631-683):
-    ``hidden @ W^T (+ b)``, ``x / max(|x|, 1e-12)``, skiplist tokens dropped."""
-    y = hidden(weights, config, ids) @ projection.astype(np.float32).T
+    ``hidden @ W^T (+ b)``, ``x / max(|x|, 1e-12)``, skiplist tokens dropped;
+    ``operands`` as in :func:`linear`."""
+    y = linear(hidden(weights, config, ids, operands), projection.astype(np.float32), operands)
     if bias is not None:
         y = y + bias
     if normalize:

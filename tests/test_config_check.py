@@ -117,9 +117,14 @@ def test_qwen35_config_refusals(path, value):
         inl.config_check(_edit(cfg, path, value), "f32")
 
 
-def test_qwen35_runs_in_f32_only():
-    with pytest.raises(inl.ConfigError, match="f32"):
-        inl.config_check(_qwen35(), "bf16")
+def test_qwen35_accepts_bf16_as_the_reference_does():
+    """The reference's late engine takes f32 (default) or bf16
+    (crates/inl-late/src/native.rs:232); the tower reports the dtype it was
+    asked for."""
+    from im_not_llm_b200 import _native as N
+
+    assert inl.config_check(_qwen35(), "bf16")["dtype"] == N.INL_DTYPE_BF16
+    assert inl.config_check(_qwen35(), "f32")["dtype"] == N.INL_DTYPE_F32
 
 
 def test_malformed_configs():

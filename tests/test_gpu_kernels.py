@@ -65,13 +65,19 @@ def test_gemm_bf16_plain(gpu, M, N, K, bn):
     assert err < 8e-3, err
 
 
-def test_gemm_bf16_f32_epilogue(gpu):
+@pytest.mark.parametrize("M,N,K,bn", [
+    (333, 128, 1024, 0),   # one CTA, 128-wide tiles
+    (333, 200, 1024, 0),   # a last chunk of 8 columns (the ragged store)
+    (700, 768, 2304, 0),   # 256-wide tiles on CTA pairs, K as in a 3xBF16 product
+    (700, 768, 2304, 128),  # the same on single CTAs
+])
+def test_gemm_bf16_f32_epilogue(gpu, M, N, K, bn):
     import torch
 
-    A = torch.randn(333, 1024, device="cuda").to(torch.bfloat16)
-    W = (torch.randn(128, 1024, device="cuda") * 0.05).to(torch.bfloat16)
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
     ref = A.float() @ W.float().T
-    out = _gemm(torch, A, W, epi=EPI_F32)
+    out = _gemm(torch, A, W, epi=EPI_F32, bn=bn)
     err = (out - ref).abs().max().item() / ref.abs().max().item()
     assert err < 1e-4, err
 

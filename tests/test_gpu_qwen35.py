@@ -14,11 +14,12 @@ import im_not_llm_b200 as inl
 
 LATE = Path(__file__).resolve().parent / "golden" / "tiny_qwen3_5_late"
 TOLERANCE = 1e-4  # crates/inl-late/tests/tiny_golden.rs:24-26
+BF16_COS = 0.999  # per-token cosine against the oracle in the same bf16 operand mode
 
 pytestmark = pytest.mark.gpu
 
 
-def _encoder(batch_size):
+def _encoder(batch_size, dtype="f32"):
     from safetensors.numpy import load_file
 
     cfg = json.loads((LATE / "config.json").read_text())
@@ -26,7 +27,7 @@ def _encoder(batch_size):
     tok = inl.TextTokenizer.from_file(LATE / "tokenizer.json")
 
     def load():
-        m = inl.CudaModel(cfg, str(LATE / "model.safetensors"), dtype="f32")
+        m = inl.CudaModel(cfg, str(LATE / "model.safetensors"), dtype=dtype)
         m.set_dense_head(dense)
         return m
 
@@ -89,3 +90,44 @@ def test_tiny_late_tower_from_the_model_dir(gpu):
             if got.size:
                 assert np.abs(got - want).max() < TOLERANCE, (case["task"], i)
     enc.unload()
+
+
+def test_tiny_late_tower_in_bf16(gpu):
+    """The tower requested in bf16 (the reference accepts it,
+    crates/inl-late/src/native.rs:232): GEMMs on bf16-rounded operands with
+    f32 sums, f32 activations, norms and recurrence. Every token vector of the
+    golden's texts (query and document prompts, batched) against the oracle in
+    the same operand mode (oracle/qwen3_5.py ``operands="bf16"``), and the
+    model reports bf16. Against the f32 golden itself this random tiny tower
+    loses up to half its cosine on a few tokens in both implementations alike
+    (the oracle's bf16 mode shows the same worst token), so the f32 vectors
+    are not the bound here."""
+    from safetensors.numpy import load_file
+
+    from oracle import qwen3_5 as Q35
+
+    cfg = json.loads((LATE / "config.json").read_text())
+    weights = load_file(str(LATE / "model.safetensors"))
+    dense = load_file(str(LATE / "1_Dense" / "model.safetensors"))["linear.weight"]
+    golden = json.loads((LATE / "golden.json").read_text())
+    tok = inl.TextTokenizer.from_file(LATE / "tokenizer.json")
+    tasks = inl.LateTask.from_model_dir(LATE, tok)
+    m = inl.CudaModel(cfg, str(LATE / "model.safetensors"), dtype="bf16")
+    try:
+        assert m.info()["dtype"] == 1  # INL_DTYPE_BF16, as created
+        m.set_dense_head(dense)
+        worst = 1.0
+        for task in ("query", "document"):
+            setup = tasks[task]
+            rows = [r[:setup.length] for r in tok.encode_untruncated([setup.prompt + t for t in golden["texts"]])]
+            rows = [np.asarray(r, dtype=np.uint32) for r in rows if len(r)]
+            ids = np.concatenate(rows)
+            cu = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+            got = m.encode_multivector(ids, cu)
+            want = np.concatenate([Q35.late_vectors(weights, cfg, dense, None, r, operands="bf16") for r in rows])
+            assert got.shape == want.shape
+            cos = (got * want).sum(-1) / (np.linalg.norm(got, axis=-1) * np.linalg.norm(want, axis=-1))
+            worst = min(worst, float(cos.min()))
+        assert worst >= BF16_COS, worst
+    finally:
+        m.close()

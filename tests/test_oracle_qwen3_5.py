@@ -77,3 +77,22 @@ def test_chunked_form_equals_the_recurrence():
         want = Q35.gated_delta_rule(q, k, v, g, beta)
         got = Q35.gated_delta_rule_chunked(q, k, v, g, beta, chunk=chunk)
         assert np.abs(got - want).max() < 1e-5, (T, chunk)
+
+
+def test_bf16_operand_mode_rounds_like_torch():
+    """oracle/qwen3_5.py's bf16 operand mode: round to nearest, ties to even
+    (torch's float -> bfloat16 conversion), f32 sums."""
+    import torch
+
+    from oracle import qwen3_5 as Q35
+
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal(4096) * np.exp(rng.uniform(-20, 20, 4096))).astype(np.float32)
+    ties = np.array([1 + 2 ** -8, 1 + 3 * 2 ** -8, -(1 + 2 ** -8), 1 + 2 ** -9], dtype=np.float32)
+    for v in (x, ties):
+        want = torch.from_numpy(v).to(torch.bfloat16).float().numpy()
+        assert np.array_equal(Q35.bf16_round(v), want)
+    a = rng.standard_normal((5, 24)).astype(np.float32)
+    w = rng.standard_normal((7, 24)).astype(np.float32)
+    assert np.array_equal(Q35.linear(a, w, "bf16"), Q35.bf16_round(a) @ Q35.bf16_round(w).T)
+    assert np.array_equal(Q35.linear(a, w), a @ w.T)
