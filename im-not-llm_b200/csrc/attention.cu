@@ -3,9 +3,11 @@
 // h / (hq / hkv)), masks computed from positions instead of materialised.
 //
 // bf16 runs on the tcgen05 kernel of attention_sm100.cu (head_dim 64, 128,
-// 256). f32: SIMT kernel for the f32-accurate configurations: 32 queries per CTA,
-// 32-key tiles in shared memory, one lane per key for the scores and one lane
-// per head dimension slice for the output.
+// 256). f32 (the f32-accurate configurations): head_dim 64 / 128 on a
+// register-tiled SIMT kernel (64 queries per CTA, 8 x 8 output tiles per
+// thread); other head dims, and rows not 16-byte aligned, on a plain SIMT
+// kernel (32 queries per CTA, 32-key tiles in shared memory, one lane per key
+// for the scores and one lane per head dimension slice for the output).
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,7 +36,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(AttnArgs a) {
   const int kvh = head / (a.hq / a.hkv);
   const int s0 = a.cu[text];
   const int L = a.cu[text + 1] - s0;
-  const int q0 = qb * kFQ;
+  const int q0 = qb * a.q_block + blockIdx.z * kFQ;  // a work item of q_block rows is gridDim.z CTAs
   if (q0 >= L) return;
   int k_lo = 0, k_hi = L;
   if (a.causal) k_hi = min(L, q0 + kFQ);
@@ -116,16 +118,222 @@ int launch_f32(const AttnArgs& a, cudaStream_t s) {
   constexpr int bytes = (kFQ * D + kFK * (D + 1) + kFK * D) * 4;
   static std::atomic<unsigned long long> attr{0};  // one bit per device
   if (set_smem_limit_once(kern, bytes, attr) != cudaSuccess) return -3;
-  dim3 grid(a.n_work, a.hq);
+  dim3 grid(a.n_work, a.hq, a.q_block / kFQ);
   kern<<<grid, 128, bytes, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// f32 attention for head_dim 64 / 128, register-tiled: a CTA takes 64 queries
+// of one head and walks 32-key tiles. Thread t of the 64 R threads (R = D / 64)
+// owns the 8 queries of group qg = t / (8 R) and, within the group's 8 R
+// threads, slot g = t % (8 R): the scores of keys [g * 4 / R, +4 / R) of each
+// tile and the output columns [8 g, 8 g + 8). The 8 R threads of a group sit
+// in one warp, so a query row's max and sum combine with shuffles, and every
+// thread holds its rows' running max and sum for the output rescale. Q, K, V
+// and P live in shared memory row-major with rows padded by 4 floats: the
+// 16-byte loads of a warp touch distinct banks, and the lanes of one group
+// read the same Q / P addresses (broadcast). Per 4 columns of the scores a
+// thread issues 8 + 4 / R loads for 128 / R FMAs, per 4 keys of the output
+// 16 loads for 256 FMAs. expf and the masks as in attn_f32_kernel.
+constexpr int kTQ = 64;  // queries per CTA
+constexpr int kTK = 32;  // keys per tile
+
+template <int D>
+struct F32Tiled {
+  static constexpr int R = D / 64;
+  static constexpr int THREADS = 64 * R;
+  static constexpr int G = 8 * R;       // threads per query group
+  static constexpr int KPT = 4 / R;     // keys per thread per tile
+  static constexpr int LD = D + 4;      // padded row of Q, K, V
+  static constexpr int LDP = kTK + 4;   // padded row of P
+  static constexpr int SMEM = (kTQ * LD + 2 * kTK * LD + kTQ * LDP) * 4;
+};
+
+template <int D>
+__global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(AttnArgs a) {
+  using C = F32Tiled<D>;
+  constexpr int KPT = C::KPT, LD = C::LD, LDP = C::LDP;
+  extern __shared__ __align__(16) float fsm[];
+  float* sQ = fsm;                 // [kTQ][LD]
+  float* sK = sQ + kTQ * LD;       // [kTK][LD]
+  float* sV = sK + kTK * LD;       // [kTK][LD]
+  float* sP = sV + kTK * LD;       // [kTQ][LDP]
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int qg = tid / C::G, g = tid % C::G;
+  const int2 wk = a.work[blockIdx.x];
+  const int head = blockIdx.y;
+  const int kvh = head / (a.hq / a.hkv);
+  const int s0 = a.cu[wk.x];
+  const int L = a.cu[wk.x + 1] - s0;
+  const int q0 = wk.y * kTQ;
+  if (q0 >= L) return;
+  int k_lo = 0, k_hi = L;
+  if (a.causal) k_hi = min(L, q0 + kTQ);
+  if (a.window >= 0) {
+    k_lo = max(0, q0 - a.window);
+    k_hi = min(k_hi, q0 + kTQ + a.window);
+  }
+  const float* qbase = static_cast<const float*>(a.q) + static_cast<long long>(s0) * a.ldq + head * D;
+  const float* kbase = static_cast<const float*>(a.k) + static_cast<long long>(s0) * a.ldk + kvh * D;
+  const float* vbase = static_cast<const float*>(a.v) + static_cast<long long>(s0) * a.ldv + kvh * D;
+
+  constexpr int C4 = D / 4;  // float4 per row
+  for (int i = tid; i < kTQ * C4; i += C::THREADS) {
+    const int r = i / C4, c = (i - r * C4) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < L) v = *reinterpret_cast<const float4*>(qbase + static_cast<long long>(q0 + r) * a.ldq + c);
+    *reinterpret_cast<float4*>(sQ + r * LD + c) = v;
+  }
+  float o[8][8];
+  float m_r[8], l_r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m_r[i] = -INFINITY;
+    l_r[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[i][j] = 0.f;
+  }
+  const int qrow0 = qg * 8;       // first of this thread's query rows in the tile
+  const int kc0 = g * KPT;        // first of this thread's keys in a key tile
+  const int dc0 = g * 8;          // first of this thread's output columns
+
+  for (int kt = (k_lo / kTK) * kTK; kt < k_hi; kt += kTK) {
+    __syncthreads();  // the previous tile's K, V and P are consumed
+    for (int i = tid; i < kTK * C4; i += C::THREADS) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (kt + r < L) {
+        kv = *reinterpret_cast<const float4*>(kbase + static_cast<long long>(kt + r) * a.ldk + c);
+        vv = *reinterpret_cast<const float4*>(vbase + static_cast<long long>(kt + r) * a.ldv + c);
+      }
+      *reinterpret_cast<float4*>(sK + r * LD + c) = kv;
+      *reinterpret_cast<float4*>(sV + r * LD + c) = vv;
+    }
+    __syncthreads();
+    // Scores of this thread's 8 queries x KPT keys.
+    float sc[8][KPT];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < KPT; ++j) sc[i][j] = 0.f;
+#pragma unroll 2
+    for (int c = 0; c < D; c += 4) {
+      float4 kf[KPT];
+#pragma unroll
+      for (int j = 0; j < KPT; ++j) kf[j] = *reinterpret_cast<const float4*>(sK + (kc0 + j) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 qf = *reinterpret_cast<const float4*>(sQ + (qrow0 + i) * LD + c);
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+          sc[i][j] = fmaf(qf.x, kf[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qf.y, kf[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qf.z, kf[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qf.w, kf[j].w, sc[i][j]);
+        }
+      }
+    }
+    // Online softmax per query row; the row's G threads combine by shuffles.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int qr = q0 + qrow0 + i;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KPT; ++j) {
+        const int key = kt + kc0 + j;
+        bool valid = key < L && key >= k_lo;
+        if (a.causal) valid = valid && key <= qr;
+        if (a.window >= 0) valid = valid && abs(qr - key) <= a.window;
+        sc[i][j] = valid ? sc[i][j] * a.scale : -INFINITY;
+        mt = fmaxf(mt, sc[i][j]);
+      }
+#pragma unroll
+      for (int off = C::G / 2; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float m_new = fmaxf(m_r[i], mt);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = expf(m_r[i] - m_use);
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < KPT; ++j) {
+        sc[i][j] = expf(sc[i][j] - m_use);
+        ps += sc[i][j];
+      }
+#pragma unroll
+      for (int off = C::G / 2; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l_r[i] = l_r[i] * alpha + ps;
+      m_r[i] = m_new;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[i][j] *= alpha;
+      float* prow = sP + (qrow0 + i) * LDP + kc0;
+      if constexpr (KPT == 4) *reinterpret_cast<float4*>(prow) = make_float4(sc[i][0], sc[i][1], sc[i][2], sc[i][3]);
+      else *reinterpret_cast<float2*>(prow) = make_float2(sc[i][0], sc[i][1]);
+    }
+    __syncthreads();  // P complete
+    // O[8 queries][8 columns] += P[8][kTK] . V[kTK][8], four keys at a time.
+#pragma unroll 1
+    for (int j = 0; j < kTK; j += 4) {
+      float4 vf[4][2];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        vf[u][0] = *reinterpret_cast<const float4*>(sV + (j + u) * LD + dc0);
+        vf[u][1] = *reinterpret_cast<const float4*>(sV + (j + u) * LD + dc0 + 4);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 pf = *reinterpret_cast<const float4*>(sP + (qrow0 + i) * LDP + j);
+        const float p4[4] = {pf.x, pf.y, pf.z, pf.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          o[i][0] = fmaf(p4[u], vf[u][0].x, o[i][0]);
+          o[i][1] = fmaf(p4[u], vf[u][0].y, o[i][1]);
+          o[i][2] = fmaf(p4[u], vf[u][0].z, o[i][2]);
+          o[i][3] = fmaf(p4[u], vf[u][0].w, o[i][3]);
+          o[i][4] = fmaf(p4[u], vf[u][1].x, o[i][4]);
+          o[i][5] = fmaf(p4[u], vf[u][1].y, o[i][5]);
+          o[i][6] = fmaf(p4[u], vf[u][1].z, o[i][6]);
+          o[i][7] = fmaf(p4[u], vf[u][1].w, o[i][7]);
+        }
+      }
+    }
+  }
+  (void)lane;
+  float* obase = static_cast<float*>(a.out) + static_cast<long long>(s0) * a.ldo + head * D + dc0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int qr = q0 + qrow0 + i;
+    if (qr >= L) continue;
+    const float inv = l_r[i] > 0.f ? 1.0f / l_r[i] : 0.f;
+    float* dst = obase + static_cast<long long>(qr) * a.ldo;
+    *reinterpret_cast<float4*>(dst) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+  }
+}
+
+template <int D>
+int launch_f32_tiled(const AttnArgs& a, cudaStream_t s) {
+  using C = F32Tiled<D>;
+  auto kern = attn_f32_tiled_kernel<D>;
+  static std::atomic<unsigned long long> attr{0};  // one bit per device
+  if (set_smem_limit_once(kern, C::SMEM, attr) != cudaSuccess) return -3;
+  dim3 grid(a.n_work, a.hq);
+  kern<<<grid, C::THREADS, C::SMEM, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// The tiled kernel's 16-byte accesses need every row start of q, k, v and
+// out 16-byte aligned.
+bool f32_tiled_ok(const AttnArgs& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return al(a.q) && al(a.k) && al(a.v) && al(a.out) && (a.ldq % 4) == 0 && (a.ldk % 4) == 0 && (a.ldv % 4) == 0 &&
+         (a.ldo % 4) == 0;
 }
 
 }  // namespace
 
 int attention_q_block(int bf16, int d) {
   if (bf16) return 128;  // the tcgen05 kernel's query tile
-  return kFQ;
+  return (d == 64 || d == 128) ? kTQ : kFQ;  // the tiled f32 kernel's, else the SIMT kernel's
 }
 
 bool attention_supported(int bf16, int d) {
@@ -137,13 +345,14 @@ int attention(const AttnArgs& a, cudaStream_t s) {
   if (a.n_work <= 0) return 0;
   if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv != 0) return -1;
   if (a.bf16) return attention_tc(a, a.total_rows, s);  // head_dim 64, 128, 256 (others: -1)
-  if (a.q_block != kFQ) return -1;
+  if (a.q_block != attention_q_block(0, a.d)) return -1;
+  const bool tiled = f32_tiled_ok(a);
   switch (a.d) {
     case 8:
     case 16: return attention_small(a, s);  // tiny checkpoints
     case 32: return launch_f32<32>(a, s);
-    case 64: return launch_f32<64>(a, s);
-    case 128: return launch_f32<128>(a, s);
+    case 64: return tiled ? launch_f32_tiled<64>(a, s) : launch_f32<64>(a, s);
+    case 128: return tiled ? launch_f32_tiled<128>(a, s) : launch_f32<128>(a, s);
     case 256: return launch_f32<256>(a, s);
     default: return -1;
   }
