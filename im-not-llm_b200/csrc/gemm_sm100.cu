@@ -219,7 +219,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
   }
   uint32_t r[32];
   float v[32];
-  if constexpr (EPI == INL_EPI_GATED_BF16) {
+  if constexpr (EPI == INL_EPI_GATED_BF16 || EPI == INL_EPI_GATED_F32) {
     // Tile columns [0, BN/2) are gate, [BN/2, BN) up (weights interleaved in
     // BN/2-row blocks at load time); this warp makes output columns
     // [half * BN/4, (half + 1) * BN/4) of the tile's BN/2.
@@ -234,7 +234,17 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = gate_act<ACT>(__uint_as_float(r[j]) * rs) * (__uint_as_float(u[j]) * rs);
-      if (o0 + c < out_n) stage_store32(st, v, o0 + c, row0, lane);  // uniform; rows past M are clipped
+      if (o0 + c >= out_n) continue;  // uniform
+      if constexpr (EPI == INL_EPI_GATED_F32) {
+        // gate blocks are multiples of 32 columns, so a chunk is whole
+        if (row_ok) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(e.out) + static_cast<long long>(row) * e.ldo + o0 + c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+      } else {
+        stage_store32(st, v, o0 + c, row0, lane);  // rows past M are clipped
+      }
     }
   } else if constexpr (EPI == INL_EPI_SEGMAX) {
     // Rows are vocabulary entries, columns are packed tokens of segment seg[col]:
@@ -312,9 +322,27 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       if (left <= 0) continue;  // warp-uniform
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
-      if constexpr (EPI == INL_EPI_F32) {
+      if constexpr (EPI == INL_EPI_F32 || EPI == INL_EPI_RESID_F32) {
         if (!row_ok) continue;
         float* dst = reinterpret_cast<float*>(e.out) + static_cast<long long>(row) * e.ldo + col;
+        if constexpr (EPI == INL_EPI_RESID_F32) {
+          // read before the store: out may alias the residual
+          const float* src = reinterpret_cast<const float*>(e.resid) + static_cast<long long>(row) * e.ldr + col;
+          if (left >= 32) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 q4 = reinterpret_cast<const float4*>(src)[j];
+              v[4 * j] += q4.x;
+              v[4 * j + 1] += q4.y;
+              v[4 * j + 2] += q4.z;
+              v[4 * j + 3] += q4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < left) v[j] += src[j];
+          }
+        }
         if (left >= 32) {
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -825,8 +853,10 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.W) & 15)) return -1;
   if (g.epi != INL_EPI_SEGMAX && ((reinterpret_cast<uintptr_t>(g.out) & 15) || (g.ldo % 8) != 0)) return -1;
   if (g.epi == INL_EPI_RESID_BF16 && ((reinterpret_cast<uintptr_t>(g.resid) & 15) || (g.ldr % 8) != 0)) return -1;
+  if (g.epi == INL_EPI_RESID_F32 && (!g.resid || (reinterpret_cast<uintptr_t>(g.resid) & 15) || (g.ldr % 4) != 0))
+    return -1;
   int bn = (g.N <= 128 || (g.N % 256) != 0) ? 128 : 256;
-  if (g.epi == INL_EPI_GATED_BF16) {
+  if (g.epi == INL_EPI_GATED_BF16 || g.epi == INL_EPI_GATED_F32) {
     // Gate/up interleaved in blocks of bn/2 rows; the caller picks the block.
     bn = g.gate_block * 2;
     if ((bn != 128 && bn != 256) || (g.N % bn) != 0) return -1;
@@ -840,7 +870,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       return -1;
   }
   if (g.force_bn == 128 || g.force_bn == 256) {
-    if ((g.epi == INL_EPI_GATED_BF16 || g.epi == INL_EPI_QKV) && g.force_bn != bn) return -1;
+    if ((g.epi == INL_EPI_GATED_BF16 || g.epi == INL_EPI_GATED_F32 || g.epi == INL_EPI_QKV) && g.force_bn != bn)
+      return -1;
     bn = g.force_bn;
   }
   if (g.ss_in && (g.ss_in_parts <= 0 || g.ss_dim <= 0)) return -1;
@@ -856,7 +887,7 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
   // on single CTAs.
   const bool pair = g.cta_pair && bn == 256 &&
                     (g.epi == INL_EPI_BF16 || g.epi == INL_EPI_RESID_BF16 || g.epi == INL_EPI_GATED_BF16 ||
-                     g.epi == INL_EPI_F32);
+                     g.epi == INL_EPI_F32 || g.epi == INL_EPI_RESID_F32 || g.epi == INL_EPI_GATED_F32);
   CUtensorMap ta, tb, to;
   if (!make_kmajor_map(&ta, g.A, g.M, g.K, g.lda, kBM)) return -2;
   if (!make_kmajor_map(&tb, g.W, g.N, g.K, g.ldw, pair ? 128 : bn)) return -2;
@@ -876,6 +907,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       case INL_EPI_BF16: err = launch_gemm_pair<INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm_pair<INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_F32: err = launch_gemm_pair<INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_F32: err = launch_gemm_pair<INL_EPI_RESID_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_F32: err = dispatch_act_pair<INL_EPI_GATED_F32>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: err = dispatch_act_pair<INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
     }
   } else if (bn == 256) {
@@ -883,6 +916,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       case INL_EPI_BF16: err = launch_gemm<256, INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm<256, INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_F32: err = launch_gemm<256, INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_F32: err = launch_gemm<256, INL_EPI_RESID_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_F32: err = dispatch_act<256, INL_EPI_GATED_F32>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_GATED_BF16: err = dispatch_act<256, INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_QKV: err = launch_gemm<256, INL_EPI_QKV, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_SEGMAX: err = launch_gemm<256, INL_EPI_SEGMAX, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
@@ -893,6 +928,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
       case INL_EPI_BF16: err = launch_gemm<128, INL_EPI_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_RESID_BF16: err = launch_gemm<128, INL_EPI_RESID_BF16, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_F32: err = launch_gemm<128, INL_EPI_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_RESID_F32: err = launch_gemm<128, INL_EPI_RESID_F32, 0>(ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
+      case INL_EPI_GATED_F32: err = dispatch_act<128, INL_EPI_GATED_F32>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       case INL_EPI_GATED_BF16: err = dispatch_act<128, INL_EPI_GATED_BF16>(g.act, ta, tb, to, g.M, g.N, g.K, e, g.status, g.max_ctas, stream); break;
       default: return -1;
     }

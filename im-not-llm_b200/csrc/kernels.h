@@ -21,6 +21,8 @@ enum InlEpilogue : int {
   INL_EPI_F32 = 3,         // out = r * acc (f32)
   INL_EPI_QKV = 4,         // q|k|v heads: per-head RMSNorm of q/k (qn/kn) + half-split RoPE at pos[row]
   INL_EPI_SEGMAX = 5,      // pooled[seg[col]][row] = max over columns of the segment (order-encoded atomicMax)
+  INL_EPI_RESID_F32 = 6,   // out = r * acc + resid, f32 (resid read as f32; out may alias resid)
+  INL_EPI_GATED_F32 = 7,   // as INL_EPI_GATED_BF16 with an f32 output
 };
 
 // Columns per partial sum of squares written by the residual epilogue.

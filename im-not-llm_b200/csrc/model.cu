@@ -1122,6 +1122,35 @@ int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int
   if (inl::split3_bf16(static_cast<const float*>(A), lda, M, K, one ? 2 : 0, m->split_a.p, K3, m->stream)) return -3;
   m->launches++;
   const bool plain = epi == INL_EPI_F32 || epi == INL_EPI_BF16;
+  // The residual add and the gated activation run in the GEMM's epilogue when
+  // the f32 rows are 16-byte aligned (and, gated, the gate blocks match a tile
+  // width); otherwise the product goes through scratch and a second kernel.
+  const bool out_al = !(reinterpret_cast<uintptr_t>(out) & 15) && (ldo % 8) == 0;
+  const bool fuse_resid = epi == INL_EPI_RESID_BF16 && out_al && resid &&
+                          !(reinterpret_cast<uintptr_t>(resid) & 15) && (ldr % 4) == 0;
+  const bool fuse_gated = epi == INL_EPI_GATED_BF16 && out_al && (m->gate_block == 64 || m->gate_block == 128) &&
+                          (N % (2 * m->gate_block)) == 0;
+  if (fuse_resid || fuse_gated) {
+    inl::GemmArgs g;
+    g.A = m->split_a.as<__nv_bfloat16>();
+    g.lda = K3;
+    g.W = static_cast<const __nv_bfloat16*>(w3);
+    g.ldw = K3;
+    g.M = M;
+    g.N = N;
+    g.K = static_cast<int>(K3);
+    g.epi = fuse_resid ? INL_EPI_RESID_F32 : INL_EPI_GATED_F32;
+    g.act = act;
+    g.gate_block = m->gate_block;
+    g.out = out;
+    g.ldo = ldo;
+    g.resid = static_cast<const __nv_bfloat16*>(resid);  // read as f32 by this epilogue
+    g.ldr = ldr;
+    g.status = m->d_status;
+    const int r = inl::gemm_bf16_tn(g, m->stream);
+    if (r == 0) m->launches++;
+    return r == 0 ? 0 : (r == -1 ? -1 : -3);
+  }
   float* dst = static_cast<float*>(out);
   long long ldd = ldo;
   if (!plain || (reinterpret_cast<uintptr_t>(out) & 15) || (ldo % 8)) {

@@ -24,6 +24,8 @@ extern "C" {
 #define INL_GEMM_EPI_RESID 1      /* out = bf16(acc + resid), out may alias resid */
 #define INL_GEMM_EPI_GATED 2      /* out[:, n/2] = act(gate) * up, gate/up interleaved in gate_block rows */
 #define INL_GEMM_EPI_F32 3        /* out = acc (f32) */
+#define INL_GEMM_EPI_RESID_F32 6  /* out = acc + resid, f32 rows 16-byte aligned; out may alias resid */
+#define INL_GEMM_EPI_GATED_F32 7  /* as INL_GEMM_EPI_GATED with an f32 output */
 
 #define INL_ACT_SILU_ 0
 #define INL_ACT_GELU_ERF_ 1

@@ -15,6 +15,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 EPI_BF16, EPI_RESID, EPI_GATED, EPI_F32 = 0, 1, 2, 3
+EPI_RESID_F32, EPI_GATED_F32 = 6, 7
 
 
 def _lib():
@@ -33,6 +34,8 @@ def _gemm(torch, A, W, epi=EPI_BF16, act=0, gate_block=128, resid=None, out_dtyp
     N = W.shape[0]
     if epi == EPI_GATED:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
+    elif epi == EPI_GATED_F32:
+        out = torch.empty(M, N // 2, dtype=torch.float32, device="cuda")
     elif epi == EPI_F32:
         out = torch.empty(M, N, dtype=torch.float32, device="cuda")
     else:
@@ -97,6 +100,52 @@ def test_gemm_bf16_residual_in_place(gpu):
     torch.cuda.synchronize()
     err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
     assert err < 8e-3, err
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(700, 1024, 2048, 0), (700, 1024, 2048, 128), (129, 200, 512, 0)])
+def test_gemm_bf16_resid_f32_in_place(gpu, M, N, K, bn):
+    """The 3xBF16 residual epilogue: f32 out = acc + f32 resid, in place
+    (CTA pairs at N = 1024, single CTAs at 128, a ragged last chunk at 200)."""
+    import torch
+
+    N_ = _lib()
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    h = torch.randn(M, N, device="cuda")
+    ref = (A.float() @ W.float().T) + h
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = N_.lib().inl_cuda_gemm_bf16(A.data_ptr(), K, W.data_ptr(), K, M, N, K, EPI_RESID_F32, 0, 128,
+                                     h.data_ptr(), N, h.data_ptr(), N, bn, status.data_ptr(), _stream(torch))
+    N_.check(st, "gemm")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    err = (h - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, err
+
+
+@pytest.mark.parametrize("act,gb", [(0, 64), (1, 64), (2, 128), (0, 128)])
+def test_gemm_bf16_gated_f32(gpu, act, gb):
+    """The gated epilogue with an f32 output (gate/up blocks of 64 on
+    128-wide tiles, of 128 on CTA pairs)."""
+    import torch
+    import torch.nn.functional as F
+
+    M, K, I = 517, 1024, 768
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    gate = (torch.randn(I, K, device="cuda") * 0.03).to(torch.bfloat16)
+    up = (torch.randn(I, K, device="cuda") * 0.03).to(torch.bfloat16)
+    W = torch.empty(2 * I, K, device="cuda", dtype=torch.bfloat16)
+    for b in range(I // gb):
+        W[2 * b * gb:(2 * b + 1) * gb] = gate[b * gb:(b + 1) * gb]
+        W[(2 * b + 1) * gb:(2 * b + 2) * gb] = up[b * gb:(b + 1) * gb]
+    g = A.float() @ gate.float().T
+    u = A.float() @ up.float().T
+    fn = {0: F.silu, 1: lambda x: F.gelu(x), 2: lambda x: F.gelu(x, approximate="tanh")}[act]
+    ref = fn(g) * u
+    out = _gemm(torch, A, W, epi=EPI_GATED_F32, act=act, gate_block=gb)
+    assert out.dtype == torch.float32
+    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-4, err
 
 
 @pytest.mark.parametrize("act", [0, 1, 2])
