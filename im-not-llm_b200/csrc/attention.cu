@@ -123,41 +123,66 @@ int launch_f32(const AttnArgs& a, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// f32 attention for head_dim 64 / 128, register-tiled: a CTA takes 64 queries
-// of one head and walks 32-key tiles. Thread t of the 64 R threads (R = D / 64)
-// owns the 8 queries of group qg = t / (8 R) and, within the group's 8 R
-// threads, slot g = t % (8 R): the scores of keys [g * 4 / R, +4 / R) of each
-// tile and the output columns [8 g, 8 g + 8). The 8 R threads of a group sit
+// f32 attention for head_dim 64 / 128, register-tiled: a CTA of 64 R threads
+// (R = D / 64) takes 64 queries of one head and walks 32-key tiles. Thread t
+// owns the QPT = 8 queries of group qg = t / (8 R) and, within the group's
+// 8 R threads, slot g = t % (8 R): the scores of keys [g * 4 / R, +4 / R) of
+// each tile and the output columns [8 g, 8 g + 8). The 8 R threads of a group sit
 // in one warp, so a query row's max and sum combine with shuffles, and every
 // thread holds its rows' running max and sum for the output rescale. Q, K, V
 // and P live in shared memory row-major with rows padded by 4 floats: the
 // 16-byte loads of a warp touch distinct banks, and the lanes of one group
 // read the same Q / P addresses (broadcast). Per 4 columns of the scores a
-// thread issues 8 + 4 / R loads for 128 / R FMAs, per 4 keys of the output
-// 16 loads for 256 FMAs. expf and the masks as in attn_f32_kernel.
+// thread issues QPT + 4 / R loads for 16 QPT / R FMAs, per 4 keys of the
+// output 8 + QPT loads for 32 QPT FMAs. For head_dim 128 the K / V tiles
+// are double-buffered and copied with cp.async, so the next tile's rows
+// arrive while this one is computed. expf and the masks as in
+// attn_f32_kernel.
 constexpr int kTQ = 64;  // queries per CTA
 constexpr int kTK = 32;  // keys per tile
+
+// 16-byte global -> shared copies that bypass registers (cp.async): the
+// bytes past src_bytes (0 or 16) are zero-filled.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, int src_bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 template <int D>
 struct F32Tiled {
   static constexpr int R = D / 64;
-  static constexpr int THREADS = 64 * R;
-  static constexpr int G = 8 * R;       // threads per query group
+  static constexpr int QPT = 8;                     // queries per thread
+  static constexpr int G = 8 * R;                   // threads per query group
+  static constexpr int THREADS = (kTQ / QPT) * G;   // 64 R
   static constexpr int KPT = 4 / R;     // keys per thread per tile
   static constexpr int LD = D + 4;      // padded row of Q, K, V
   static constexpr int LDP = kTK + 4;   // padded row of P
-  static constexpr int SMEM = (kTQ * LD + 2 * kTK * LD + kTQ * LDP) * 4;
+  // Head_dim 128: tiles copied with cp.async into two K / V buffers, the next
+  // tile streaming in during this one (2 CTAs per SM either way; 1.56 -> 1.44
+  // ms of config 1's attention). Head_dim 64: one buffer filled by plain
+  // loads, which keeps 5 CTAs per SM; the asynchronous forms measured 4-9%
+  // slower there (fewer resident CTAs, or 128-thread CTAs at 4 queries per
+  // thread).
+  static constexpr bool ASYNC = D == 128;
+  static constexpr int NBUF = ASYNC ? 2 : 1;
+  static constexpr int SMEM = (kTQ * LD + 2 * NBUF * kTK * LD + kTQ * LDP) * 4;  // Q, K / V buffers, P
 };
 
 template <int D>
 __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(AttnArgs a) {
   using C = F32Tiled<D>;
-  constexpr int KPT = C::KPT, LD = C::LD, LDP = C::LDP;
+  constexpr int KPT = C::KPT, LD = C::LD, LDP = C::LDP, QPT = C::QPT;
   extern __shared__ __align__(16) float fsm[];
-  float* sQ = fsm;                 // [kTQ][LD]
-  float* sK = sQ + kTQ * LD;       // [kTK][LD]
-  float* sV = sK + kTK * LD;       // [kTK][LD]
-  float* sP = sV + kTK * LD;       // [kTQ][LDP]
+  float* sQ = fsm;                  // [kTQ][LD]
+  constexpr int NB = C::NBUF;
+  float* sK0 = sQ + kTQ * LD;        // [NB][kTK][LD]
+  float* sV0 = sK0 + NB * kTK * LD;  // [NB][kTK][LD]
+  float* sP = sV0 + NB * kTK * LD;   // [kTQ][LDP]
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int qg = tid / C::G, g = tid % C::G;
@@ -178,28 +203,26 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
   const float* kbase = static_cast<const float*>(a.k) + static_cast<long long>(s0) * a.ldk + kvh * D;
   const float* vbase = static_cast<const float*>(a.v) + static_cast<long long>(s0) * a.ldv + kvh * D;
 
+  // Every copy is in flight at once (cp.async); K / V tiles are double
+  // buffered, tile t + 1 streaming in while tile t is computed. Rows past the
+  // text are zero-filled.
   constexpr int C4 = D / 4;  // float4 per row
-  for (int i = tid; i < kTQ * C4; i += C::THREADS) {
-    const int r = i / C4, c = (i - r * C4) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + r < L) v = *reinterpret_cast<const float4*>(qbase + static_cast<long long>(q0 + r) * a.ldq + c);
-    *reinterpret_cast<float4*>(sQ + r * LD + c) = v;
+  if constexpr (C::ASYNC) {
+#pragma unroll 4
+    for (int i = tid; i < kTQ * C4; i += C::THREADS) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      const bool ok = q0 + r < L;
+      cp_async16(sQ + r * LD + c, ok ? qbase + static_cast<long long>(q0 + r) * a.ldq + c : qbase, ok ? 16 : 0);
+    }
+  } else {
+    for (int i = tid; i < kTQ * C4; i += C::THREADS) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q0 + r < L) v = *reinterpret_cast<const float4*>(qbase + static_cast<long long>(q0 + r) * a.ldq + c);
+      *reinterpret_cast<float4*>(sQ + r * LD + c) = v;
+    }
   }
-  float o[8][8];
-  float m_r[8], l_r[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    m_r[i] = -INFINITY;
-    l_r[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[i][j] = 0.f;
-  }
-  const int qrow0 = qg * 8;       // first of this thread's query rows in the tile
-  const int kc0 = g * KPT;        // first of this thread's keys in a key tile
-  const int dc0 = g * 8;          // first of this thread's output columns
-
-  for (int kt = (k_lo / kTK) * kTK; kt < k_hi; kt += kTK) {
-    __syncthreads();  // the previous tile's K, V and P are consumed
+  auto load_kv_sync = [&](int kt) {
     for (int i = tid; i < kTK * C4; i += C::THREADS) {
       const int r = i / C4, c = (i - r * C4) * 4;
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
@@ -207,14 +230,57 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
         kv = *reinterpret_cast<const float4*>(kbase + static_cast<long long>(kt + r) * a.ldk + c);
         vv = *reinterpret_cast<const float4*>(vbase + static_cast<long long>(kt + r) * a.ldv + c);
       }
-      *reinterpret_cast<float4*>(sK + r * LD + c) = kv;
-      *reinterpret_cast<float4*>(sV + r * LD + c) = vv;
+      *reinterpret_cast<float4*>(sK0 + r * LD + c) = kv;
+      *reinterpret_cast<float4*>(sV0 + r * LD + c) = vv;
     }
-    __syncthreads();
-    // Scores of this thread's 8 queries x KPT keys.
-    float sc[8][KPT];
+  };
+  auto load_kv = [&](int kt, int buf) {
+    float* dk = sK0 + buf * kTK * LD;
+    float* dv = sV0 + buf * kTK * LD;
+#pragma unroll 4
+    for (int i = tid; i < kTK * C4; i += C::THREADS) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      const bool ok = kt + r < L;
+      cp_async16(dk + r * LD + c, ok ? kbase + static_cast<long long>(kt + r) * a.ldk + c : kbase, ok ? 16 : 0);
+      cp_async16(dv + r * LD + c, ok ? vbase + static_cast<long long>(kt + r) * a.ldv + c : vbase, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  const int kt0 = (k_lo / kTK) * kTK;
+  if constexpr (C::ASYNC) load_kv(kt0, 0);  // committed with the Q copies
+  float o[QPT][8];
+  float m_r[QPT], l_r[QPT];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < QPT; ++i) {
+    m_r[i] = -INFINITY;
+    l_r[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[i][j] = 0.f;
+  }
+  const int qrow0 = qg * QPT;     // first of this thread's query rows in the tile
+  const int kc0 = g * KPT;        // first of this thread's keys in a key tile
+  const int dc0 = g * 8;          // first of this thread's output columns
+
+  int buf = 0;
+  for (int kt = kt0; kt < k_hi; kt += kTK, buf = NB == 2 ? buf ^ 1 : 0) {
+    if constexpr (C::ASYNC) {
+      // The other buffer was released by the barrier that ended the last tile.
+      if (kt + kTK < k_hi) {
+        load_kv(kt + kTK, buf ^ 1);
+        cp_async_wait<1>();  // this tile's copies (and Q) have landed
+      } else {
+        cp_async_wait<0>();
+      }
+    } else {
+      load_kv_sync(kt);  // the buffer was released by the last tile's closing barrier
+    }
+    __syncthreads();  // ... every thread's copies are visible
+    const float* sK = sK0 + buf * kTK * LD;
+    const float* sV = sV0 + buf * kTK * LD;
+    // Scores of this thread's QPT queries x KPT keys.
+    float sc[QPT][KPT];
+#pragma unroll
+    for (int i = 0; i < QPT; ++i)
 #pragma unroll
       for (int j = 0; j < KPT; ++j) sc[i][j] = 0.f;
 #pragma unroll 2
@@ -223,7 +289,7 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
 #pragma unroll
       for (int j = 0; j < KPT; ++j) kf[j] = *reinterpret_cast<const float4*>(sK + (kc0 + j) * LD + c);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < QPT; ++i) {
         const float4 qf = *reinterpret_cast<const float4*>(sQ + (qrow0 + i) * LD + c);
 #pragma unroll
         for (int j = 0; j < KPT; ++j) {
@@ -236,7 +302,7 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
     }
     // Online softmax per query row; the row's G threads combine by shuffles.
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < QPT; ++i) {
       const int qr = q0 + qrow0 + i;
       float mt = -INFINITY;
 #pragma unroll
@@ -270,7 +336,7 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
       else *reinterpret_cast<float2*>(prow) = make_float2(sc[i][0], sc[i][1]);
     }
     __syncthreads();  // P complete
-    // O[8 queries][8 columns] += P[8][kTK] . V[kTK][8], four keys at a time.
+    // O[QPT queries][8 columns] += P[QPT][kTK] . V[kTK][8], four keys at a time.
 #pragma unroll 1
     for (int j = 0; j < kTK; j += 4) {
       float4 vf[4][2];
@@ -280,7 +346,7 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
         vf[u][1] = *reinterpret_cast<const float4*>(sV + (j + u) * LD + dc0 + 4);
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < QPT; ++i) {
         const float4 pf = *reinterpret_cast<const float4*>(sP + (qrow0 + i) * LDP + j);
         const float p4[4] = {pf.x, pf.y, pf.z, pf.w};
 #pragma unroll
@@ -296,11 +362,12 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
         }
       }
     }
+    __syncthreads();  // this tile's K, V and P are consumed
   }
   (void)lane;
   float* obase = static_cast<float*>(a.out) + static_cast<long long>(s0) * a.ldo + head * D + dc0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < QPT; ++i) {
     const int qr = q0 + qrow0 + i;
     if (qr >= L) continue;
     const float inv = l_r[i] > 0.f ? 1.0f / l_r[i] : 0.f;

@@ -838,6 +838,10 @@ int create_common(const char* config_json, int device, int dtype, inl_model** ou
   // the reference holds its f32 tower to (crates/inl-late/tests/tiny_golden.rs),
   // so it keeps the SIMT FFMA GEMMs.
   m->f32_split3 = m->c.arch != inl::ARCH_QWEN35;
+  // f32 towers on the 3xBF16 path interleave gate / up in 128-row blocks, the
+  // block of the 256-wide CTA-pair tiles (64 would keep them on 128-wide
+  // single-CTA tiles).
+  if (m->dtype == INL_DTYPE_F32 && m->f32_split3) m->gate_block = 128;
   if (m->c.H % 8 != 0) {
     delete m;
     return fail(INL_ERR_CONFIG, "hidden_size must be a multiple of 8");
@@ -1219,7 +1223,28 @@ int linear(inl_model* m, const void* A, long long lda, const void* W, int M, int
     r = (m->f32_split3 || m->f32_bf16_operands) ? linear_split3(m, A, lda, W, M, N, K, epi, act, out, ldo, resid, ldr)
                                                 : -1;
   }
-  if (r == -1 && m->dtype != INL_DTYPE_BF16) {
+  if (r == -1 && m->dtype != INL_DTYPE_BF16 && epi == INL_EPI_GATED_BF16 && m->gate_block != 64) {
+    // The SIMT GEMM fuses the gated activation for 64-row gate blocks only:
+    // other blocks take the f32 product into scratch, then the activation.
+    if (m->split_c.ensure(token_cap(M) * static_cast<size_t>(N) * 4) != cudaSuccess) return -3;
+    inl::GemmF32Args g;
+    g.A = static_cast<const float*>(A);
+    g.lda = lda;
+    g.W = static_cast<const float*>(W);
+    g.ldw = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.epi = INL_EPI_F32;
+    g.out = m->split_c.as<float>();
+    g.ldo = N;
+    r = inl::gemm_f32_tn(g, m->stream);
+    if (r == 0) {
+      m->launches++;
+      r = inl::act_mul_blocks_f32(m->split_c.as<float>(), N, M, N / 2, m->gate_block, act, static_cast<float*>(out),
+                                  ldo, m->stream);
+    }
+  } else if (r == -1 && m->dtype != INL_DTYPE_BF16) {
     inl::GemmF32Args g;
     g.A = static_cast<const float*>(A);
     g.lda = lda;
