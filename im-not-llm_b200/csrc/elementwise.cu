@@ -981,11 +981,45 @@ __global__ void split3_kernel(const float* __restrict__ x, long long ldx, int ro
   }
 }
 
+// The same split four columns at a time (one 16-byte load, 8-byte stores)
+// with 32-bit indexing, for rows aligned to it; identical results.
+__global__ void split3_vec4_kernel(const float* __restrict__ x, long long ldx, int rows, int K, int mode,
+                                   __nv_bfloat16* __restrict__ out, long long ldo) {
+  const int q4 = K >> 2;
+  const int total = rows * q4;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / q4;
+    const int k = (i - r * q4) << 2;
+    const float4 v = *reinterpret_cast<const float4*>(x + static_cast<long long>(r) * ldx + k);
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+    const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+    const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+    const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+    uint2 hi, lo;
+    hi.x = *reinterpret_cast<const uint32_t*>(&h0);
+    hi.y = *reinterpret_cast<const uint32_t*>(&h1);
+    lo.x = *reinterpret_cast<const uint32_t*>(&l0);
+    lo.y = *reinterpret_cast<const uint32_t*>(&l1);
+    __nv_bfloat16* o = out + static_cast<long long>(r) * ldo + k;
+    *reinterpret_cast<uint2*>(o) = hi;
+    if (mode == 2) continue;
+    *reinterpret_cast<uint2*>(o + K) = mode ? lo : hi;
+    *reinterpret_cast<uint2*>(o + 2 * K) = mode ? hi : lo;
+  }
+}
+
 int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* out, long long ldo, cudaStream_t s) {
   if (rows <= 0) return 0;
   if ((K & 1) || (ldx & 1) || (ldo & 1) || (reinterpret_cast<uintptr_t>(x) & 7) ||
       (reinterpret_cast<uintptr_t>(out) & 3))
     return -1;
+  if ((K & 3) == 0 && (ldx & 3) == 0 && (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 7) == 0 && static_cast<long long>(rows) * (K / 4) < (1LL << 31)) {
+    const long long total4 = static_cast<long long>(rows) * (K / 4);
+    const int blocks = static_cast<int>(std::min<long long>((total4 + 255) / 256, 148LL * 16));
+    split3_vec4_kernel<<<blocks, 256, 0, s>>>(x, ldx, rows, K, mode, static_cast<__nv_bfloat16*>(out), ldo);
+    return ok(cudaGetLastError());
+  }
   const long long total = static_cast<long long>(rows) * (K / 2);
   const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
   split3_kernel<<<blocks, 256, 0, s>>>(x, ldx, rows, K, mode, static_cast<__nv_bfloat16*>(out), ldo);
