@@ -173,7 +173,11 @@ struct F32Tiled {
   static constexpr int SMEM = (kTQ * LD + 2 * NBUF * kTK * LD + kTQ * LDP) * 4;  // Q, K / V buffers, P
 };
 
-template <int D>
+// HX: the head is blockIdx.x and the work item blockIdx.y, so the blocks are
+// dispatched item by item (the list is heaviest first) with every head of an
+// item together; otherwise (more work items than a grid's y extent) the
+// reverse.
+template <int D, bool HX>
 __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(AttnArgs a) {
   using C = F32Tiled<D>;
   constexpr int KPT = C::KPT, LD = C::LD, LDP = C::LDP, QPT = C::QPT;
@@ -186,8 +190,8 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int qg = tid / C::G, g = tid % C::G;
-  const int2 wk = a.work[blockIdx.x];
-  const int head = blockIdx.y;
+  const int2 wk = a.work[HX ? blockIdx.y : blockIdx.x];
+  const int head = HX ? blockIdx.x : blockIdx.y;
   const int kvh = head / (a.hq / a.hkv);
   const int s0 = a.cu[wk.x];
   const int L = a.cu[wk.x + 1] - s0;
@@ -380,11 +384,16 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
 template <int D>
 int launch_f32_tiled(const AttnArgs& a, cudaStream_t s) {
   using C = F32Tiled<D>;
-  auto kern = attn_f32_tiled_kernel<D>;
-  static std::atomic<unsigned long long> attr{0};  // one bit per device
-  if (set_smem_limit_once(kern, C::SMEM, attr) != cudaSuccess) return -3;
-  dim3 grid(a.n_work, a.hq);
-  kern<<<grid, C::THREADS, C::SMEM, s>>>(a);
+  static std::atomic<unsigned long long> attr{0}, attr_hx{0};  // one bit per device
+  if (a.n_work <= 65535) {
+    auto kern = attn_f32_tiled_kernel<D, true>;
+    if (set_smem_limit_once(kern, C::SMEM, attr_hx) != cudaSuccess) return -3;
+    kern<<<dim3(a.hq, a.n_work), C::THREADS, C::SMEM, s>>>(a);
+  } else {
+    auto kern = attn_f32_tiled_kernel<D, false>;
+    if (set_smem_limit_once(kern, C::SMEM, attr) != cudaSuccess) return -3;
+    kern<<<dim3(a.n_work, a.hq), C::THREADS, C::SMEM, s>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
