@@ -32,9 +32,8 @@
 //              exp2(s - m) as bf16 into shared memory in the K-major
 //              128-byte-swizzle layout the MMA reads. m is only raised when
 //              the block max exceeds it by more than 2^8, and then O is
-//              rescaled in TMEM. A quarter of the exp2 run as a cubic on the
-//              FMA pipe, the rest on the special-function unit. At the end of
-//              a tile, O / l goes as bf16 through the slot's P buffer to TMA
+//              rescaled in TMEM. The exp2 run on the special-function
+//              unit. At the end of a tile, O / l goes as bf16 through the slot's P buffer to TMA
 //              tensor stores of the warp's 16 rows (whole-row stores for a
 //              warp that crosses the end of the text); for head_dim 256 each
 //              thread stores its 128 columns straight to the output row.
@@ -245,41 +244,6 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
       "mov.b64 {%0, %1}, rs;\n\t}"
       : "+f"(s0), "+f"(s1)
       : "f"(a0), "f"(a1));
-}
-
-// 2^a, 2^b for a, b <= 8 on the FMA pipe, for the share of the softmax
-// exponentials taken off the special-function unit. Range reduction x = j + f
-// with j = rint(x) (the 1.5 * 2^23 rounding constant: t = x + c holds j in its
-// low mantissa bits) and f in [-1/2, 1/2]; 2^f by a cubic, then j is added to
-// the exponent field: bits(t) << 23 == j << 23 modulo 2^32. The cubic is this
-// file's own minimax fit of 2^f on [-1/2, 1/2] (Lawson's iteratively
-// reweighted least squares on relative error): max relative error 7.5e-5,
-// well under the 2^-9 rounding step of the bf16 P it feeds. Inputs are
-// clamped at -126, so a masked score (-inf) gives ~1e-38 instead of 0.
-__device__ __forceinline__ void exp2_poly2(float& a, float& b) {
-  const float xa = fmaxf(a, -126.0f), xb = fmaxf(b, -126.0f);
-  uint32_t ta, tb, pa, pb;
-  asm("{\n\t.reg .b64 x, t, j, f, p, k;\n\t"
-      "mov.b64 x, {%4, %5};\n\t"
-      "mov.b64 k, 0x4B4000004B400000;\n\t"  // 1.5 * 2^23
-      "add.rn.f32x2 t, x, k;\n\t"
-      "mov.b64 k, 0xCB400000CB400000;\n\t"  // -1.5 * 2^23
-      "add.rn.f32x2 j, t, k;\n\t"
-      "mov.b64 k, 0xBF800000BF800000;\n\t"  // -1
-      "fma.rn.f32x2 f, j, k, x;\n\t"
-      "mov.b64 k, 0x3D61FBAF3D61FBAF;\n\t"  // c3 = 0.0551716648
-      "mov.b64 p, 0x3E786F103E786F10;\n\t"  // c2 = 0.2426111698
-      "fma.rn.f32x2 p, f, k, p;\n\t"
-      "mov.b64 k, 0x3F31798D3F31798D;\n\t"  // c1 = 0.6932609677
-      "fma.rn.f32x2 p, p, f, k;\n\t"
-      "mov.b64 k, 0x3F7FFB493F7FFB49;\n\t"  // c0 = 0.9999280572
-      "fma.rn.f32x2 p, p, f, k;\n\t"
-      "mov.b64 {%0, %1}, t;\n\t"
-      "mov.b64 {%2, %3}, p;\n\t}"
-      : "=r"(ta), "=r"(tb), "=r"(pa), "=r"(pb)
-      : "f"(xa), "f"(xb));
-  a = __uint_as_float((ta << 23) + pa);
-  b = __uint_as_float((tb << 23) + pb);
 }
 
 // bf16x2 {lo, hi} with round-to-nearest-even, one instruction.
@@ -580,11 +544,11 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
           for (int t = 0; t < 8; t += 2)
             fma2_bcast(x[t], x[t + 1], __uint_as_float(sv[c + t]), __uint_as_float(sv[c + t + 1]), p.scale_log2,
                        neg_m);
-          // A quarter of the exponentials on the FMA pipe, the rest on the
-          // special-function unit.
+          // Every exponential on the special-function unit (moving a
+          // quarter or a half of them to a cubic on the FMA pipe measured
+          // 2-3% slower here).
 #pragma unroll
-          for (int t = 0; t < 6; ++t) x[t] = ex2_approx(x[t]);
-          exp2_poly2(x[6], x[7]);
+          for (int t = 0; t < 8; ++t) x[t] = ex2_approx(x[t]);
           add2(rs[0], rs[1], x[0], x[1]);
           add2(rs[2], rs[3], x[2], x[3]);
           add2(rs[0], rs[1], x[4], x[5]);
