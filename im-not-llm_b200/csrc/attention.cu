@@ -287,14 +287,23 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
     for (int i = 0; i < QPT; ++i)
 #pragma unroll
       for (int j = 0; j < KPT; ++j) sc[i][j] = 0.f;
-#pragma unroll 2
+    // Head_dim 128: the 8 query rows of a column step are loaded before the
+    // FMAs (3.5% faster there, slower at 64); head_dim 64: the column loop
+    // unrolled by 4 (1% faster there).
+    constexpr int UNR = D == 64 ? 4 : 2;
+#pragma unroll(UNR)
     for (int c = 0; c < D; c += 4) {
       float4 kf[KPT];
 #pragma unroll
       for (int j = 0; j < KPT; ++j) kf[j] = *reinterpret_cast<const float4*>(sK + (kc0 + j) * LD + c);
+      float4 qa[QPT];
+      if constexpr (D == 128) {
+#pragma unroll
+        for (int i = 0; i < QPT; ++i) qa[i] = *reinterpret_cast<const float4*>(sQ + (qrow0 + i) * LD + c);
+      }
 #pragma unroll
       for (int i = 0; i < QPT; ++i) {
-        const float4 qf = *reinterpret_cast<const float4*>(sQ + (qrow0 + i) * LD + c);
+        const float4 qf = D == 128 ? qa[i] : *reinterpret_cast<const float4*>(sQ + (qrow0 + i) * LD + c);
 #pragma unroll
         for (int j = 0; j < KPT; ++j) {
           sc[i][j] = fmaf(qf.x, kf[j].x, sc[i][j]);
