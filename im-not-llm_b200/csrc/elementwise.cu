@@ -1026,6 +1026,59 @@ int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* 
   return ok(cudaGetLastError());
 }
 
+// Split-K partial planes summed in slice order (+ the residual), four
+// columns per thread when rows and pointers allow, else one.
+template <int V>
+__global__ void splits_reduce_kernel(const float* __restrict__ ws, long long plane, long long ldw, int splits, int rows,
+                                     int cols, const float* resid, long long ldr, float* out, long long ldo) {
+  const int cv = cols / V;
+  const long long total = static_cast<long long>(rows) * cv;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cv);
+    const int c = static_cast<int>(i - static_cast<long long>(r) * cv) * V;
+    auto ld = [](const float* p, float (&v)[V]) {
+      if constexpr (V == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      } else {
+        v[0] = *p;
+      }
+    };
+    float acc[V];
+    ld(ws + static_cast<long long>(r) * ldw + c, acc);
+    for (int sl = 1; sl < splits; ++sl) {
+      float p[V];
+      ld(ws + sl * plane + static_cast<long long>(r) * ldw + c, p);
+#pragma unroll
+      for (int j = 0; j < V; ++j) acc[j] += p[j];
+    }
+    if (resid) {
+      float q[V];
+      ld(resid + static_cast<long long>(r) * ldr + c, q);
+#pragma unroll
+      for (int j = 0; j < V; ++j) acc[j] = q[j] + acc[j];
+    }
+    float* o = out + static_cast<long long>(r) * ldo + c;
+    if constexpr (V == 4) *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    else *o = acc[0];
+  }
+}
+
+int splits_reduce_f32(const float* ws, long long plane, long long ldw, int splits, int rows, int cols,
+                      const float* resid, long long ldr, float* out, long long ldo, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  if (splits < 1) return -1;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool v4 = (cols % 4) == 0 && (ldw % 4) == 0 && (plane % 4) == 0 && (ldo % 4) == 0 && al(ws) && al(out) &&
+                  (!resid || (al(resid) && (ldr % 4) == 0));
+  const long long total = static_cast<long long>(rows) * (v4 ? cols / 4 : cols);
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  if (v4) splits_reduce_kernel<4><<<blocks, 256, 0, s>>>(ws, plane, ldw, splits, rows, cols, resid, ldr, out, ldo);
+  else splits_reduce_kernel<1><<<blocks, 256, 0, s>>>(ws, plane, ldw, splits, rows, cols, resid, ldr, out, ldo);
+  return ok(cudaGetLastError());
+}
+
 // out = a + b over rows x cols (f32; out may alias a or b).
 __global__ void add_rows_f32_kernel(float* out, long long ldo, const float* a, long long lda, const float* b,
                                     long long ldb, int rows, int cols) {

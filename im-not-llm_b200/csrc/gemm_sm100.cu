@@ -66,7 +66,26 @@ struct EpiArgs {
   const int* seg;
   int* pooled;
   long long ldp;
+  // split-K (f32 output only): the K blocks of a tile are cut into `splits`
+  // slices; slice s writes its partial product at out + s * split_stride
+  int splits;
+  long long split_stride;
 };
+
+// A work unit of the persistent schedule: a tile and the K blocks [kb0, kb1)
+// of its slice (the whole K without split-K).
+struct Unit {
+  int tile, kb0, kb1, slice;
+};
+__device__ __forceinline__ Unit unit_of(int u, int splits, int k_blocks) {
+  Unit w;
+  w.tile = u / splits;
+  w.slice = u - w.tile * splits;
+  const int per = (k_blocks + splits - 1) / splits;
+  w.kb0 = w.slice * per;
+  w.kb1 = min(k_blocks, w.kb0 + per);
+  return w;
+}
 
 // Output path of one epilogue warp: 32 rows x 32 bf16 columns at a time go
 // through a double-buffered 2 KB staging area in shared memory (64-byte rows,
@@ -199,7 +218,7 @@ __device__ __forceinline__ void qk_head(uint32_t t_row, int c0, float rs, const 
 // columns [half * BN/2, (half + 1) * BN/2) of the tile.
 template <int BN, int EPI, int ACT>
 __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, int half, const EpiArgs& e,
-                                              OutStage& st, int lane) {
+                                              OutStage& st, int lane, long long out_off = 0) {
   constexpr int HW = BN / 2;
   const bool row_ok = row < e.M;
   const int row0 = row - lane;  // first row of this warp's 32
@@ -324,7 +343,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row, int n0, i
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
       if constexpr (EPI == INL_EPI_F32 || EPI == INL_EPI_RESID_F32) {
         if (!row_ok) continue;
-        float* dst = reinterpret_cast<float*>(e.out) + static_cast<long long>(row) * e.ldo + col;
+        float* dst = reinterpret_cast<float*>(e.out) + out_off + static_cast<long long>(row) * e.ldo + col;
         if constexpr (EPI == INL_EPI_RESID_F32) {
           // read before the store: out may alias the residual
           const float* src = reinterpret_cast<const float*>(e.resid) + static_cast<long long>(row) * e.ldr + col;
@@ -397,6 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  const int splits = e.splits > 1 ? e.splits : 1;
+  const int num_units = num_tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -427,9 +448,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, splits, k_blocks);
+        const int mb = w.tile / n_tiles, nb = w.tile - (w.tile / n_tiles) * n_tiles;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status, INL_DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
@@ -462,11 +484,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, splits, k_blocks);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status, INL_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, status, INL_DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -479,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             umma_bf16(d_tmem, a_desc + static_cast<uint64_t>(kk * 2), b_desc + static_cast<uint64_t>(kk * 2), idesc,
-                      (kb | kk) != 0 ? 1u : 0u);
+                      (kb != w.kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -502,13 +525,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     OutStage st{&tmO, sOut + (warp - 2) * 2 * kStageChunkBytes, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const Unit w = unit_of(u, splits, k_blocks);
+      const int mb = w.tile / n_tiles, nb = w.tile - (w.tile / n_tiles) * n_tiles;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = mb * kBM + quad * 32 + lane;
-      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e, st, lane);
+      epilogue_tile<BN, EPI, ACT>(t_row, row, nb * BN, half, e, st, lane, w.slice * e.split_stride);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -579,6 +603,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int n_tiles = (N + C::BN - 1) / C::BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  const int splits = e.splits > 1 ? e.splits : 1;
+  const int num_units = num_tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -609,11 +635,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
-        const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+      for (int u = pair; u < num_units && ok; u += n_pairs) {
+        const Unit w = unit_of(u, splits, k_blocks);
+        const int mb = w.tile / n_tiles, nb = w.tile - (w.tile / n_tiles) * n_tiles;
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_row = nb * C::BN + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status, INL_DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
@@ -650,11 +677,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+      for (int u = pair; u < num_units && ok; u += n_pairs) {
+        const Unit w = unit_of(u, splits, k_blocks);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status, INL_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, status, INL_DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -667,7 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             umma_bf16_pair(d_tmem, a_desc + static_cast<uint64_t>(kk * 2), b_desc + static_cast<uint64_t>(kk * 2), idesc,
-                           (kb | kk) != 0 ? 1u : 0u);
+                           (kb != w.kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit_pair(smem_u32(&empty[stage]));
           umma_commit_pair(empty_peer0 + static_cast<uint32_t>(stage * sizeof(uint64_t)));
@@ -693,13 +721,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tempty_lead0 = mapa_shared(smem_u32(&tempty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
-      const int mb = tile / n_tiles, nb = tile - (tile / n_tiles) * n_tiles;
+    for (int u = pair; u < num_units; u += n_pairs) {
+      const Unit w = unit_of(u, splits, k_blocks);
+      const int mb = w.tile / n_tiles, nb = w.tile - (w.tile / n_tiles) * n_tiles;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, status, INL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * C::BN);
       const int row = mb * 2 * kBM + static_cast<int>(rank) * kBM + quad * 32 + lane;
-      epilogue_tile<C::BN, EPI, ACT>(t_row, row, nb * C::BN, half, e, st, lane);
+      epilogue_tile<C::BN, EPI, ACT>(t_row, row, nb * C::BN, half, e, st, lane, w.slice * e.split_stride);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_lead0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
@@ -763,7 +792,7 @@ cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   static std::atomic<unsigned long long> attr_set{0};  // per instantiation, one bit per device
   cudaError_t aerr = set_smem_limit_once(kern, C::SMEM_BYTES, attr_set);
   if (aerr != cudaSuccess) return aerr;
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * (e.splits > 1 ? e.splits : 1);
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
@@ -779,7 +808,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   static std::atomic<unsigned long long> attr_set{0};  // per instantiation, one bit per device
   cudaError_t aerr = set_smem_limit_once(kern, C::SMEM_BYTES, attr_set);
   if (aerr != cudaSuccess) return aerr;
-  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + C::BN - 1) / C::BN);
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + C::BN - 1) / C::BN) * (e.splits > 1 ? e.splits : 1);
   int pairs = num_sms() / 2;
   if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
   if (tiles < pairs) pairs = tiles;
@@ -875,6 +904,12 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
     bn = g.force_bn;
   }
   if (g.ss_in && (g.ss_in_parts <= 0 || g.ss_dim <= 0)) return -1;
+  const int k_blocks = (g.K + kBK - 1) / kBK;
+  if (g.splits > 1) {
+    // every slice must hold at least one K block
+    const int per = (k_blocks + g.splits - 1) / g.splits;
+    if (g.epi != INL_EPI_F32 || (g.splits - 1) * per >= k_blocks) return -1;
+  }
   if (g.epi == INL_EPI_SEGMAX) {
     if (!g.seg || !g.pooled || g.ldp < g.M) return -1;
     bn = 256;
@@ -901,6 +936,8 @@ int gemm_bf16_tn(const GemmArgs& g, cudaStream_t stream) {
   EpiArgs e{g.out, g.ldo, g.resid, g.ldr, g.ss_in, g.ss_in_parts, g.ss_dim, g.ss_eps, g.ss_out,
             (g.N + INL_SS_COLS - 1) / INL_SS_COLS, g.qn, g.kn, g.pos, g.cos, g.sin, g.hq, g.hkv, g.d, g.max_pos,
             g.qk_eps, g.status, g.M, g.N, g.seg, g.pooled, g.ldp};
+  e.splits = g.splits > 1 ? g.splits : 1;
+  e.split_stride = static_cast<long long>(g.M) * g.ldo;
   cudaError_t err;
   if (pair) {
     switch (g.epi) {

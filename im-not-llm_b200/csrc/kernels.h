@@ -69,6 +69,9 @@ struct GemmArgs {
   int max_ctas = 0;   // 0 = one CTA per SM
   int force_bn = 0;   // 0 = automatic tile width
   int cta_pair = 1;   // 1 = 256 x 256 tiles on CTA pairs (cta_group::2) where the epilogue allows, 0 = one CTA per tile
+  // split-K (INL_EPI_F32 only): each tile's K blocks in `splits` slices, slice
+  // s writing its partial product to out + s * M * ldo (splits_reduce_f32 sums them)
+  int splits = 1;
 };
 
 // tcgen05 bf16 GEMM; returns 0 on success, <0 on bad arguments / launch error.
@@ -182,6 +185,11 @@ int token_positions(const int* cu, int n, int T, int* pos, cudaStream_t s);
 // (activation side), mode 1 [hi | lo | hi] (weight side); mode 2 writes [hi]
 // alone ([rows, K], a bf16 product); K, ldx, ldo even.
 int split3_bf16(const float* x, long long ldx, int rows, int K, int mode, void* out, long long ldo, cudaStream_t s);
+// out = sum over s < splits of ws[s * plane + row * ldw + col], in that order,
+// plus resid when given (f32; out may alias resid): the second half of a
+// split-K product.
+int splits_reduce_f32(const float* ws, long long plane, long long ldw, int splits, int rows, int cols,
+                      const float* resid, long long ldr, float* out, long long ldo, cudaStream_t s);
 // out = a + b (f32 rows; out may alias a or b).
 int add_rows_f32(float* out, long long ldo, const float* a, long long lda, const float* b, long long ldb, int rows,
                  int cols, cudaStream_t s);

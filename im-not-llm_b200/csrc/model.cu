@@ -1134,6 +1134,47 @@ int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int
                           !(reinterpret_cast<uintptr_t>(resid) & 15) && (ldr % 4) == 0;
   const bool fuse_gated = epi == INL_EPI_GATED_BF16 && out_al && (m->gate_block == 64 || m->gate_block == 128) &&
                           (N % (2 * m->gate_block)) == 0;
+  // Split-K when M is small: with fewer 256 x 256 tiles than half the SMs'
+  // CTA pairs (config 1's 1,024 rows: 16 tiles for o and down), each tile's
+  // K' is cut into up to 4 slices of at least 8 K blocks, written as f32
+  // partial planes and summed in slice order with the residual by a second
+  // kernel (deterministic).
+  int splits = 1;
+  if ((plain || epi == INL_EPI_RESID_BF16) && (N % 256) == 0 && N > 128 && out_al &&
+      (epi != INL_EPI_RESID_BF16 || (resid && !(reinterpret_cast<uintptr_t>(resid) & 15) && (ldr % 4) == 0))) {
+    const long long pairs = inl::num_sms_cached() / 2;
+    const long long tiles = ((M + 255) / 256) * static_cast<long long>(N / 256);
+    const int kb = static_cast<int>((K3 + 63) / 64);
+    if (tiles * 2 <= pairs) {
+      splits = static_cast<int>(std::min<long long>(4, pairs / tiles));
+      while (splits > 1 && kb / splits < 8) --splits;
+    }
+  }
+  if (splits > 1) {
+    const size_t plane = static_cast<size_t>(M) * N;
+    if (m->splitk_ws.ensure(plane * splits * 4) != cudaSuccess) return -3;
+    inl::GemmArgs g;
+    g.A = m->split_a.as<__nv_bfloat16>();
+    g.lda = K3;
+    g.W = static_cast<const __nv_bfloat16*>(w3);
+    g.ldw = K3;
+    g.M = M;
+    g.N = N;
+    g.K = static_cast<int>(K3);
+    g.epi = INL_EPI_F32;
+    g.out = m->splitk_ws.p;
+    g.ldo = N;
+    g.splits = splits;
+    g.status = m->d_status;
+    int r = inl::gemm_bf16_tn(g, m->stream);  // counted by linear()
+    if (r) return r == -1 ? -1 : -3;
+    r = inl::splits_reduce_f32(m->splitk_ws.as<float>(), static_cast<long long>(plane), N, splits, M, N,
+                               epi == INL_EPI_RESID_BF16 ? static_cast<const float*>(resid) : nullptr, ldr,
+                               static_cast<float*>(out), ldo, m->stream);
+    if (r) return -3;
+    m->launches++;
+    return 0;
+  }
   if (fuse_resid || fuse_gated) {
     inl::GemmArgs g;
     g.A = m->split_a.as<__nv_bfloat16>();
@@ -1151,8 +1192,7 @@ int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int
     g.resid = static_cast<const __nv_bfloat16*>(resid);  // read as f32 by this epilogue
     g.ldr = ldr;
     g.status = m->d_status;
-    const int r = inl::gemm_bf16_tn(g, m->stream);
-    if (r == 0) m->launches++;
+    const int r = inl::gemm_bf16_tn(g, m->stream);  // counted by linear()
     return r == 0 ? 0 : (r == -1 ? -1 : -3);
   }
   float* dst = static_cast<float*>(out);
@@ -1174,9 +1214,8 @@ int linear_split3(inl_model* m, const void* A, long long lda, const void* W, int
   g.out = dst;
   g.ldo = ldd;
   g.status = m->d_status;
-  int r = inl::gemm_bf16_tn(g, m->stream);
+  int r = inl::gemm_bf16_tn(g, m->stream);  // counted by linear()
   if (r) return r == -1 ? -1 : -3;
-  m->launches++;
   if (epi == INL_EPI_RESID_BF16) {
     r = inl::add_rows_f32(static_cast<float*>(out), ldo, static_cast<const float*>(resid), ldr, dst, ldd, M, N,
                           m->stream);

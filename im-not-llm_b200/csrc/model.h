@@ -193,6 +193,7 @@ struct inl_model {
   std::unordered_map<uintptr_t, void*> split_w;
   inl::DevBuf split_a, split_c;
   inl::DevBuf seg_scratch;  // mean pooling's per-chunk partial sums
+  inl::DevBuf splitk_ws;    // split-K partial products of the f32 GEMMs
   inl::DevBuf lastbuf, work_last;
   int n_work_last = 0;
   bool prune_last = true;  // off: every layer runs on every row (tests compare the two)
