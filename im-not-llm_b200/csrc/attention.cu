@@ -207,9 +207,9 @@ __global__ void __launch_bounds__(F32Tiled<D>::THREADS) attn_f32_tiled_kernel(At
   const float* kbase = static_cast<const float*>(a.k) + static_cast<long long>(s0) * a.ldk + kvh * D;
   const float* vbase = static_cast<const float*>(a.v) + static_cast<long long>(s0) * a.ldv + kvh * D;
 
-  // Every copy is in flight at once (cp.async); K / V tiles are double
-  // buffered, tile t + 1 streaming in while tile t is computed. Rows past the
-  // text are zero-filled.
+  // ASYNC: every copy in flight at once (cp.async), K / V tiles double
+  // buffered, tile t + 1 streaming in while tile t is computed; otherwise
+  // plain 16-byte loads into one buffer. Rows past the text are zero-filled.
   constexpr int C4 = D / 4;  // float4 per row
   if constexpr (C::ASYNC) {
 #pragma unroll 4
